@@ -1,0 +1,240 @@
+"""GPU parity of the individual sm_100a kernels (through the C-ABI op entry points) against
+plain PyTorch fp32 restatements of the same ops on the same bf16/fp16-rounded operands."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from tsd_b200 import synth, tsd
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def rel(a, b):
+    a = a.double().flatten()
+    b = b.double().flatten()
+    return float(((a - b).norm() / (b.norm() + 1e-30)).item())
+
+
+def ref_gemm(W, X, taps, pad):
+    """X [nb][S][K] (bf16), W [M][taps*K] (bf16) -> fp32 [nb][S][M]."""
+    nb, S, K = X.shape
+    M = W.shape[0]
+    Wf = W.float().view(M, taps, K)
+    Xf = X.float()
+    out = torch.zeros(nb, S, M, device=X.device)
+    for tap in range(taps):
+        sh = torch.zeros_like(Xf)
+        off = tap - pad
+        lo, hi = max(0, -off), min(S, S - off)
+        if hi > lo:
+            sh[:, lo:hi] = Xf[:, lo + off:hi + off]
+        out += sh @ Wf[:, tap, :].T
+    return out
+
+
+def rnd(*shape, scale=1.0, dtype=torch.bfloat16, g=None):
+    return (scale * torch.randn(*shape, generator=g, device=DEV)).to(dtype)
+
+
+@pytest.fixture(autouse=True)
+def _seed():
+    torch.manual_seed(0)
+
+
+@pytest.mark.parametrize("M,K,taps,pad,nb,S", [
+    (256, 128, 1, 0, 1, 300),     # linear, two token tiles
+    (128, 64, 3, 1, 2, 194),      # conv k3 with batch boundaries (latent input proj shape)
+    (384, 256, 3, 1, 3, 17),      # ragged tiny sequence
+    (128, 192, 7, 3, 2, 40),      # conv k7 (sync input proj / final conv)
+    (128, 128, 1, 0, 1, 1),       # single token
+    (512, 1536, 1, 0, 1, 388),    # QKV-like K
+])
+def test_gemm_store(M, K, taps, pad, nb, S):
+    W = rnd(M, taps * K, scale=0.05)
+    X = rnd(nb, S, K)
+    bias = torch.randn(M, device=DEV)
+    out = torch.empty(nb, S, M, device=DEV)
+    tsd.op_gemm(W, M, K, taps, pad, X, nb, S, K, S * K, tsd.EPI_STORE, tsd.ACT_NONE, bias, out, 0, M)
+    torch.cuda.synchronize()
+    ref = ref_gemm(W, X, taps, pad) + bias
+    assert rel(out, ref) < 1e-5
+
+
+def test_gemm_store_bf16_silu_and_m_valid():
+    M, K, S = 128, 128, 50
+    W = rnd(M, 3 * K, scale=0.05)
+    X = rnd(2, S, K)
+    bias = torch.randn(M, device=DEV)
+    out = torch.zeros(2, S, 64, device=DEV, dtype=torch.bfloat16)
+    tsd.op_gemm(W, M, K, 3, 1, X, 2, S, K, S * K, tsd.EPI_STORE, tsd.ACT_SILU, bias, out, 1, 64, m_valid=64)
+    torch.cuda.synchronize()
+    ref = torch.nn.functional.silu(ref_gemm(W, X, 3, 1) + bias)[..., :64]
+    assert rel(out.float(), ref) < 4e-3
+    assert rel(out.float(), ref.to(torch.bfloat16).float()) < 1e-3
+
+
+@pytest.mark.parametrize("taps", [1, 3])
+def test_gemm_swiglu(taps):
+    F, K, S = 256, 128, 100
+    W1, W3 = rnd(F, taps * K, scale=0.05), rnd(F, taps * K, scale=0.05)
+    W13 = torch.empty(2 * F, taps * K, device=DEV, dtype=torch.bfloat16)
+    for b in range(F // 128):
+        W13[256 * b:256 * b + 128] = W1[128 * b:128 * b + 128]
+        W13[256 * b + 128:256 * b + 256] = W3[128 * b:128 * b + 128]
+    X = rnd(2, S, K)
+    out = torch.empty(2, S, F, device=DEV, dtype=torch.bfloat16)
+    tsd.op_gemm(W13, 2 * F, K, taps, taps // 2, X, 2, S, K, S * K, tsd.EPI_SWIGLU, 0, None, out, 1, F)
+    torch.cuda.synchronize()
+    ref = torch.nn.functional.silu(ref_gemm(W1, X, taps, taps // 2)) * ref_gemm(W3, X, taps, taps // 2)
+    assert rel(out.float(), ref) < 4e-3
+
+
+@pytest.mark.parametrize("per_token,splits,taps", [(1, 1, 3), (1, 4, 3), (0, 1, 1), (0, 4, 1)])
+def test_gemm_gate_residual(per_token, splits, taps):
+    M, K, S, nb = 256, 512, 72, 2
+    W = rnd(M, taps * K, scale=0.03)
+    X = rnd(nb, S, K)
+    bias = torch.randn(M, device=DEV)
+    gate = torch.randn(nb * S if per_token else nb, M, device=DEV)
+    x0 = torch.randn(nb, S, M, device=DEV)
+    x = x0.clone()
+    tsd.op_gemm(W, M, K, taps, taps // 2, X, nb, S, K, S * K, tsd.EPI_GATE_RESID, 0, bias, None, 0, 0,
+                resid=x, ldr=M, gate=gate, ldg=M, gate_div=1 if per_token else S, max_splits=splits)
+    torch.cuda.synchronize()
+    g = gate.view(nb, S, M) if per_token else gate.view(nb, 1, M)
+    ref = x0 + g * (ref_gemm(W, X, taps, taps // 2) + bias)
+    assert rel(x, ref) < 1e-5
+
+
+def test_gemm_strided_slice_of_joint_buffer():
+    """linear1 reads its stream's rows out of the joint attention output [B][Sj][H]."""
+    H, B, Sj, off, S = 128, 2, 300, 194, 72
+    ao = rnd(B, Sj, H)
+    W = rnd(H, 3 * H, scale=0.05)
+    out = torch.empty(B, S, H, device=DEV)
+    tsd.op_gemm(W, H, H, 3, 1, ao[:, off:], B, S, H, Sj * H, tsd.EPI_STORE, 0, None, out, 0, H)
+    torch.cuda.synchronize()
+    ref = ref_gemm(W, ao[:, off:off + S].contiguous(), 3, 1)
+    assert rel(out, ref) < 1e-5
+
+
+@pytest.mark.parametrize("wtype", [synth.GGML_BF16, synth.GGML_F32, synth.GGML_Q8_0])
+@pytest.mark.parametrize("N", [1, 2, 5])
+def test_gemv(wtype, N):
+    M, K = 300, 512
+    w = (0.02 * np.random.default_rng(1).standard_normal((M, K))).astype(np.float32)
+    if wtype == synth.GGML_BF16:
+        raw = synth.f32_to_bf16_bits(w)
+    elif wtype == synth.GGML_Q8_0:
+        raw = synth.quantize_q8_0(w)
+    else:
+        raw = w
+    wt = synth.WTensor("w", (K, M), wtype, raw)
+    Wd = torch.from_numpy(np.ascontiguousarray(raw).view(np.uint8).copy()).to(DEV)
+    wf = torch.from_numpy(wt.dequant()).to(DEV)
+    x = torch.randn(N, K, device=DEV)
+    bias = torch.randn(M, device=DEV)
+    y = torch.empty(N, M, device=DEV)
+    tsd.op_gemv(Wd, wtype, None, M, K, x, K, N, bias, tsd.ACT_SILU, int(wtype == synth.GGML_BF16), y, 0, M)
+    torch.cuda.synchronize()
+    xr = x.to(torch.bfloat16).float() if wtype == synth.GGML_BF16 else x
+    ref = torch.nn.functional.silu(xr @ wf.T + bias)
+    assert rel(y, ref) < 1e-5
+
+
+def test_gemv_swiglu_pair():
+    M, K, N = 256, 256, 2
+    w1 = (0.05 * torch.randn(M, K, device=DEV)).to(torch.bfloat16)
+    w3 = (0.05 * torch.randn(M, K, device=DEV)).to(torch.bfloat16)
+    x = torch.randn(N, K, device=DEV)
+    y = torch.empty(N, M, device=DEV)
+    tsd.op_gemv(w1, synth.GGML_BF16, w3, M, K, x, K, N, None, 0, 1, y, 0, M)
+    torch.cuda.synchronize()
+    xr = x.to(torch.bfloat16).float()
+    ref = torch.nn.functional.silu(xr @ w1.float().T) * (xr @ w3.float().T)
+    assert rel(y, ref) < 1e-5
+
+
+def ref_attention(Q, K, V, B, nh, S):
+    q, k, v = (t.float().view(B, nh, S, 64) for t in (Q, K, V))
+    p = torch.softmax(q @ k.transpose(-1, -2) / 8.0, dim=-1)
+    return (p @ v).permute(0, 2, 1, 3).reshape(B, S, nh * 64)
+
+
+@pytest.mark.parametrize("B,nh,S", [(1, 1, 1), (1, 2, 63), (2, 3, 128), (2, 4, 194), (2, 24, 471), (1, 2, 700)])
+def test_attention(B, nh, S):
+    Q = rnd(B * nh, S, 64, scale=1.5, dtype=torch.float16)
+    K = rnd(B * nh, S, 64, scale=1.5, dtype=torch.float16)
+    V = rnd(B * nh, S, 64, dtype=torch.float16)
+    out = torch.empty(B, S, nh * 64, device=DEV, dtype=torch.bfloat16)
+    err = torch.zeros(1, device=DEV, dtype=torch.int32)
+    tsd.op_attention(Q, K, V, B, nh, S, out, nh * 64, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = ref_attention(Q, K, V, B, nh, S)
+    assert rel(out.float(), ref.to(torch.bfloat16).float()) < 2e-3
+    assert rel(out.float(), ref) < 4e-3
+
+
+def test_attention_row_stride_and_peaked_softmax():
+    """Large logits (peaked softmax, running-max rescale across KV chunks) into a wider buffer."""
+    B, nh, S = 1, 2, 300
+    Q = rnd(B * nh, S, 64, scale=4.0, dtype=torch.float16)
+    K = rnd(B * nh, S, 64, scale=4.0, dtype=torch.float16)
+    V = rnd(B * nh, S, 64, dtype=torch.float16)
+    out = torch.zeros(B, S, 512, device=DEV, dtype=torch.bfloat16)
+    tsd.op_attention(Q, K, V, B, nh, S, out, 512)
+    torch.cuda.synchronize()
+    ref = ref_attention(Q, K, V, B, nh, S)
+    assert rel(out[..., :128].float(), ref) < 4e-3
+    assert float(out[..., 128:].abs().max()) == 0.0
+
+
+@pytest.mark.parametrize("per_token", [1, 0])
+def test_ln_modulate(per_token):
+    rows_per_item, nb, H = 50, 3, 384
+    rows = rows_per_item * nb
+    x = 3.0 * torch.randn(rows, H, device=DEV) + 1.0
+    x[7] = 0.5                        # zero-variance row: eps decides
+    nmod = rows if per_token else nb
+    mod = torch.randn(nmod, 6 * H, device=DEV)
+    y = torch.empty(rows, H, device=DEV, dtype=torch.bfloat16)
+    tsd.op_ln_modulate(x, rows, H, mod[:, 0:], mod[:, H:], 6 * H, per_token, rows_per_item, y)
+    torch.cuda.synchronize()
+    idx = torch.arange(rows, device=DEV) if per_token else torch.arange(rows, device=DEV) // rows_per_item
+    ln = torch.nn.functional.layer_norm(x, (H,), eps=1e-5)
+    ref = ln * (1 + mod[idx, H:2 * H]) + mod[idx, :H]
+    assert rel(y.float(), ref.to(torch.bfloat16).float()) < 1e-3
+
+
+def test_qk_norm_rope():
+    B, S, nh, Sj, off = 2, 40, 3, 100, 30
+    H = nh * 64
+    qkv = torch.randn(B, S, 3 * H, device=DEV)
+    qg = 1 + 0.1 * torch.randn(64, device=DEV)
+    kg = 1 + 0.1 * torch.randn(64, device=DEV)
+    Q = torch.zeros(B * nh, Sj, 64, device=DEV, dtype=torch.float16)
+    K, V = torch.zeros_like(Q), torch.zeros_like(Q)
+    fs = 194.0 / 72.0
+    tsd.op_qk_norm_rope(qkv, B, S, H, nh, qg, kg, 1, fs, 10000.0, Q, K, V, Sj, off)
+    torch.cuda.synchronize()
+
+    def ref(x, g):
+        x = x.view(B, S, nh, 64)
+        x = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6) * g
+        i = torch.arange(32, device=DEV, dtype=torch.float32)
+        ang = fs * (torch.arange(S, device=DEV, dtype=torch.float32)[:, None] * 10000.0 ** (-2 * i / 64))
+        c, s = torch.cos(ang)[None, :, None], torch.sin(ang)[None, :, None]
+        x0, x1 = x[..., 0::2], x[..., 1::2]
+        return torch.stack([x0 * c - x1 * s, x0 * s + x1 * c], -1).view(B, S, nh, 64)
+
+    def got(T):
+        return T.view(B, nh, Sj, 64)[:, :, off:off + S].permute(0, 2, 1, 3).float()
+
+    assert rel(got(Q), ref(qkv[..., :H], qg)) < 1e-3
+    assert rel(got(K), ref(qkv[..., H:2 * H], kg)) < 1e-3
+    assert rel(got(V), qkv[..., 2 * H:].reshape(B, S, nh, 64)) < 1e-3
+    assert float(Q.view(B, nh, Sj, 64)[:, :, :off].abs().max()) == 0.0

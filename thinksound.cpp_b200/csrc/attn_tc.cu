@@ -1,0 +1,261 @@
+// attn_tc.cu — tcgen05 flash attention for the MM-DiT joint and fused blocks (sm_100a).
+//
+// Replaces the reference's `attention` (src/mmdit.cpp:85-94): softmax(Q K^T / sqrt(64)) V per
+// head with no mask, K and V in F16 (:89-90) and F32 softmax/accumulation
+// (ggml_flash_attn_ext_set_prec F32, :92). Q, K, V arrive fp16 head-major
+// [B*nh][S][64]; for the joint blocks S is the [latent | clip | text] concatenation
+// (:251-254), which the QKV producers write in place, so no concat/split copies exist.
+//
+// One CTA per (128-query tile, batch*head). Warp 0: TMA (Q once, K/V 128-row chunks through a
+// 3-stage ring). Warp 1: TMEM owner + MMA issuer: S_j = Q K_j^T into one of two 128-column
+// TMEM buffers, O += P_j V_j into a 64-column TMEM accumulator (V as an MN-major operand).
+// Warps 2-5: online softmax, one query row per thread (TMEM lane), P_j written fp16 into a
+// 128-B-swizzled shared tile, O rescaled in TMEM when the running max moves, final 1/l scale
+// and bf16 token-major store out[b][t][h*64 + d].
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tsd {
+
+namespace {
+
+constexpr int kQT = 128, kKV = 128, kHD = 64, kStages = 3;
+constexpr int kTileBytes = 128 * 128;               // 128 rows x 64 fp16
+constexpr int kOffQ = 0;
+constexpr int kOffK = kOffQ + kTileBytes;
+constexpr int kOffV = kOffK + kStages * kTileBytes;
+constexpr int kOffP = kOffV + kStages * kTileBytes;  // 2 sub-tiles (kv 0-63, 64-127)
+constexpr int kOffBar = kOffP + 2 * kTileBytes;
+constexpr int kSmemBytes = kOffBar + 256 + 1024;
+constexpr uint32_t kTmemCols = 512;                  // S0 @0, S1 @128, O @256
+constexpr uint32_t kColO = 256;
+
+struct AttnArgs {
+    int S, nh;
+    long long ldo;
+    __nv_bfloat16 * out;
+    int * err;
+    float scale_log2;
+};
+
+__global__ void __launch_bounds__(192, 1)
+attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+               const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t * bars = reinterpret_cast<uint64_t *>(smem + kOffBar);
+    uint64_t * q_full = bars + 0;
+    uint64_t * kv_full = bars + 1;          // [3]
+    uint64_t * kv_empty = bars + 4;         // [3]
+    uint64_t * s_full = bars + 7;           // [2]
+    uint64_t * s_free = bars + 9;           // [2]
+    uint64_t * p_full = bars + 11;
+    uint64_t * pv_done = bars + 12;
+    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(bars + 13);
+    volatile int * s_abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q0 = blockIdx.x * kQT;
+    const int bh = blockIdx.y;
+    const int S = a.S;
+    const int nchunks = (S + kKV - 1) / kKV;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < kStages; ++s) { mbar_init(&kv_full[s], 1); mbar_init(&kv_empty[s], 1); }
+        for (int s = 0; s < 2; ++s) { mbar_init(&s_full[s], 1); mbar_init(&s_free[s], 128); }
+        mbar_init(p_full, 128);
+        mbar_init(pv_done, 1);
+        *s_abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) { tma_prefetch(&tmQ); tma_prefetch(&tmK); tma_prefetch(&tmV); }
+    if (warp == 1) { tmem_alloc(tmem_slot, kTmemCols); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            mbar_arrive_expect_tx(q_full, kTileBytes);
+            tma_load_3d(smem + kOffQ, &tmQ, q_full, 0, q0, bh);
+            int issued = 0;
+            for (int j = 0; j < nchunks; ++j, ++issued) {
+                const int s = j % kStages;
+                if (j >= kStages && !mbar_wait(&kv_empty[s], ((j / kStages) & 1) ^ 1, s_abort, a.err, DEV_TIMEOUT_ATTN))
+                    break;
+                mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
+                tma_load_3d(smem + kOffK + s * kTileBytes, &tmK, &kv_full[s], 0, j * kKV, bh);
+                tma_load_3d(smem + kOffV + s * kTileBytes, &tmV, &kv_full[s], 0, j * kKV, bh);
+            }
+            if (*s_abort) {
+                const unsigned long long t0 = globaltimer();
+                while (!mbar_try_wait(q_full, 0) && globaltimer() - t0 < kWaitNs) {}
+                for (int i = (issued > kStages ? issued - kStages : 0); i < issued; ++i) {
+                    const unsigned long long t1 = globaltimer();
+                    while (!mbar_try_wait(&kv_full[i % kStages], (i / kStages) & 1) && globaltimer() - t1 < kWaitNs) {}
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc_s = make_idesc_f16(128, kKV, false, false);
+            const uint32_t idesc_o = make_idesc_f16(128, kHD, false, true);
+            const uint32_t sq = smem_u32(smem + kOffQ);
+            bool ok = mbar_wait(q_full, 0, s_abort, a.err, DEV_TIMEOUT_ATTN);
+            auto issue_s = [&](int j) -> bool {
+                const int s = j % kStages;
+                if (!mbar_wait(&kv_full[s], (j / kStages) & 1, s_abort, a.err, DEV_TIMEOUT_ATTN)) return false;
+                if (j >= 2 && !mbar_wait(&s_free[j & 1], ((j >> 1) - 1) & 1, s_abort, a.err, DEV_TIMEOUT_ATTN)) return false;
+                tc_fence_after();
+                const uint64_t qd = make_sdesc_sw128(sq);
+                const uint64_t kd = make_sdesc_sw128(smem_u32(smem + kOffK + s * kTileBytes));
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) umma_f16_ss(tmem + (j & 1) * 128, qd + 2 * kk, kd + 2 * kk, idesc_s, kk > 0);
+                umma_commit(&s_full[j & 1]);
+                return true;
+            };
+            if (ok) ok = issue_s(0);
+            for (int j = 0; ok && j < nchunks; ++j) {
+                if (j + 1 < nchunks && !issue_s(j + 1)) { ok = false; break; }
+                if (!mbar_wait(p_full, j & 1, s_abort, a.err, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+                tc_fence_after();
+                const int s = j % kStages;
+                const uint32_t vb = smem_u32(smem + kOffV + s * kTileBytes);
+                const uint32_t pb = smem_u32(smem + kOffP);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint64_t pd = make_sdesc_sw128(pb + (kk >> 2) * kTileBytes) + 2 * (kk & 3);
+                    const uint64_t vd = make_sdesc_sw128(vb + kk * 2048);
+                    umma_f16_ss(tmem + kColO, pd, vd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(&kv_empty[s]);
+                umma_commit(pv_done);
+            }
+            if (!ok) umma_commit(pv_done);   // lets no waiter depend on MMAs that were never issued
+        }
+    } else {
+        // ---------------- softmax + epilogue (warps 2..5) ----------------
+        const int q = warp & 3;
+        const int r = q * 32 + lane;                   // query row within the tile (TMEM lane)
+        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+        uint8_t * prow = smem + kOffP + r * 128;
+        float m_run = -INFINITY, l_run = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nchunks; ++j) {
+            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, s_abort, a.err, DEV_TIMEOUT_ATTN))) { ok = false; break; }
+            tc_fence_after();
+            float sv[128];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                float tmp[32];
+                tmem_ld32(lane_base + (j & 1) * 128 + c * 32, tmp);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) sv[c * 32 + i] = tmp[i];
+            }
+            tc_fence_before();
+            mbar_arrive(&s_free[j & 1]);
+            const int valid = S - j * kKV;            // columns >= valid are padding keys
+            float mx = m_run;
+#pragma unroll
+            for (int i = 0; i < 128; ++i) {
+                sv[i] = (i < valid) ? sv[i] * a.scale_log2 : -INFINITY;
+                mx = fmaxf(mx, sv[i]);
+            }
+            const float alpha = ex2_approx(m_run - mx);   // 0 on the first chunk
+            float rs = 0.f;
+#pragma unroll
+            for (int i = 0; i < 128; ++i) { sv[i] = ex2_approx(sv[i] - mx); rs += sv[i]; }
+            l_run = l_run * alpha + rs;
+            m_run = mx;
+            if (j > 0) {
+                // PV_{j-1} done: O is stable (rescale it) and the P tile is free.
+                if (!__all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, s_abort, a.err, DEV_TIMEOUT_ATTN))) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    float o[32];
+                    tmem_ld32(lane_base + kColO + c * 32, o);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                    tmem_st32(lane_base + kColO + c * 32, o);
+                }
+            }
+            // P (fp16) into the 128-B swizzled K-major tile: row r, 16-B chunk ch -> ch ^ (r & 7)
+#pragma unroll
+            for (int sub = 0; sub < 2; ++sub) {
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch) {
+                    const int c0 = sub * 64 + ch * 8;
+                    uint4 u;
+                    __half2 * h2 = reinterpret_cast<__half2 *>(&u);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) h2[e] = __floats2half2_rn(sv[c0 + 2 * e], sv[c0 + 2 * e + 1]);
+                    *reinterpret_cast<uint4 *>(prow + sub * kTileBytes + ((ch ^ (r & 7)) << 4)) = u;
+                }
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+        if (ok && __all_sync(0xffffffffu, mbar_wait(pv_done, (nchunks - 1) & 1, s_abort, a.err, DEV_TIMEOUT_ATTN))) {
+            tc_fence_after();
+            const int t = q0 + r;
+            const float inv = 1.0f / l_run;
+            const int b = bh / a.nh, h = bh % a.nh;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                float o[32];
+                tmem_ld32(lane_base + kColO + c * 32, o);
+                if (t < S) {
+                    __nv_bfloat16 * dst = a.out + ((long long)b * S + t) * a.ldo + h * kHD + c * 32;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        uint4 u;
+                        __nv_bfloat162 * p2 = reinterpret_cast<__nv_bfloat162 *>(&u);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) p2[i] = __floats2bfloat162_rn(o[e * 8 + 2 * i] * inv, o[e * 8 + 2 * i + 1] * inv);
+                        *reinterpret_cast<uint4 *>(dst + e * 8) = u;
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+}  // namespace
+
+bool attn_plan(AttnLaunch & L, const void * Q, const void * K, const void * V, int B, int nh, int S, void * out,
+               long long ldo, int * err) {
+    if (S < 1 || B < 1 || nh < 1 || (ldo % 8)) return false;
+    const uint64_t rows = S, heads = (uint64_t)B * nh;
+    bool ok = make_tmap_3d(&L.tmQ, Q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, kHD, rows, heads, kHD * 2, rows * kHD * 2, kHD, kQT, 1) &&
+              make_tmap_3d(&L.tmK, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, kHD, rows, heads, kHD * 2, rows * kHD * 2, kHD, kKV, 1) &&
+              make_tmap_3d(&L.tmV, V, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, kHD, rows, heads, kHD * 2, rows * kHD * 2, kHD, kKV, 1);
+    L.S = S; L.nh = nh; L.B = B; L.ldo = ldo; L.out = out; L.err = err;
+    L.scale = 1.0f / 8.0f;
+    return ok;
+}
+
+cudaError_t attn_launch(const AttnLaunch & L, cudaStream_t st) {
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        attr = true;
+    }
+    AttnArgs a;
+    a.S = L.S; a.nh = L.nh; a.ldo = L.ldo; a.out = reinterpret_cast<__nv_bfloat16 *>(L.out); a.err = L.err;
+    a.scale_log2 = L.scale * 1.4426950408889634f;
+    dim3 grid((L.S + kQT - 1) / kQT, L.B * L.nh);
+    attn_tc_kernel<<<grid, 192, kSmemBytes, st>>>(L.tmQ, L.tmK, L.tmV, a);
+    return cudaGetLastError();
+}
+
+}  // namespace tsd

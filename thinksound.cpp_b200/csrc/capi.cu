@@ -1,0 +1,411 @@
+// capi.cu — extern "C" entry points of libtsd_b200 (include/tsd.h, include/tsd_ops.h).
+#include "runtime.h"
+#include "../../include/tsd_ops.h"
+
+#include <cstring>
+#include <vector>
+
+using namespace tsd;
+
+struct tsd_model {
+    Model * m = nullptr;
+    cudaStream_t stream = nullptr;
+};
+
+namespace {
+
+int make_stream(tsd_model * h) {
+    TSD_CUDA_TRY(cudaSetDevice(h->m->device));
+    TSD_CUDA_TRY(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
+    return TSD_OK;
+}
+
+// Reads and clears the device error word; maps it to a status.
+int check_device(Model & m, cudaStream_t st) {
+    TSD_CUDA_TRY(cudaStreamSynchronize(st));
+    int e = 0;
+    TSD_CUDA_TRY(cudaMemcpy(&e, m.d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e) {
+        fprintf(stderr, "tsd: device error word %d (a bounded wait expired)\n", e);
+        cudaMemset(m.d_err, 0, sizeof(int));
+        return TSD_ERR_DEVICE;
+    }
+    return TSD_OK;
+}
+
+int get_plan(Model & m, const Shape & sh, Plan ** out) {
+    if (!m.finalized) return TSD_ERR_STATE;
+    if (!m.plan || !(m.plan->sh == sh)) {
+        m.plan.reset();
+        const int rc = plan_build(m, sh, m.plan);
+        if (rc) return rc;
+    }
+    *out = m.plan.get();
+    return TSD_OK;
+}
+
+struct Inputs {
+    const float * latent, * t, * clip_f, * sync_f, * text_f, * t5, * gtext;
+};
+
+int stage_inputs(Model & m, Plan & p, const Inputs & in, cudaStream_t st) {
+    const Shape & s = p.sh;
+    const size_t B = (size_t)s.B;
+    TSD_CUDA_TRY(cudaMemcpyAsync(p.lat_in, in.latent, B * m.L * s.T * 4, cudaMemcpyDefault, st));
+    TSD_CUDA_TRY(cudaMemcpyAsync(p.t_in, in.t, B * 4, cudaMemcpyDefault, st));
+    TSD_CUDA_TRY(cudaMemcpyAsync(p.clip_in, in.clip_f, B * s.clip_S * m.clip_dim * 4, cudaMemcpyDefault, st));
+    TSD_CUDA_TRY(cudaMemcpyAsync(p.sync_in, in.sync_f, B * s.sync_S * m.sync_dim * 4, cudaMemcpyDefault, st));
+    if (s.text_S) TSD_CUDA_TRY(cudaMemcpyAsync(p.text_in, in.text_f, B * s.text_S * m.text_dim * 4, cudaMemcpyDefault, st));
+    if (s.t5_S) TSD_CUDA_TRY(cudaMemcpyAsync(p.t5_in, in.t5, B * s.t5_S * m.t5_dim * 4, cudaMemcpyDefault, st));
+    TSD_CUDA_TRY(cudaMemcpyAsync(p.gtext_in, in.gtext, B * m.text_dim * 4, cudaMemcpyDefault, st));
+    return TSD_OK;
+}
+
+bool shape_ok(int B, int64_t T, int64_t clip_S, int64_t sync_S, int64_t text_S, int64_t t5_S) {
+    return B >= 1 && T >= 1 && T <= (1 << 20) && clip_S >= 1 && clip_S <= (1 << 20) && sync_S >= 8 && sync_S % 8 == 0 &&
+           sync_S <= (1 << 20) && text_S >= 0 && t5_S >= 0 && text_S + t5_S >= 1 && text_S + t5_S <= (1 << 20);
+}
+
+std::vector<float> host_f32(const RawTensor & t) {
+    std::vector<float> out((size_t)t.n());
+    const uint8_t * h = t.host.data();
+    for (int64_t i = 0; i < t.n(); ++i) {
+        if (t.type == GT_F32) memcpy(&out[i], h + 4 * i, 4);
+        else if (t.type == GT_BF16) { uint32_t u = (uint32_t)(*(const uint16_t *)(h + 2 * i)) << 16; memcpy(&out[i], &u, 4); }
+        else if (t.type == GT_F16) { __half hv; memcpy(&hv, h + 2 * i, 2); out[i] = __half2float(hv); }
+        else {
+            const uint8_t * blk = h + (i / 32) * 34;
+            __half d; memcpy(&d, blk, 2);
+            out[i] = (float)(int8_t)blk[2 + i % 32] * __half2float(d);
+        }
+    }
+    return out;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char * tsd_version(void) { return "tsd_b200 0.1 (sm_100a)"; }
+
+int tsd_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+    return n;
+}
+
+int tsd_load_gguf(const char * path, int device, tsd_model ** out) {
+    if (!path || !out) return TSD_ERR_ARG;
+    Model * m = nullptr;
+    const int rc = model_load_gguf(path, device, &m);
+    if (rc) return rc;
+    tsd_model * h = new tsd_model();
+    h->m = m;
+    const int rs = make_stream(h);
+    if (rs) { delete m; delete h; return rs; }
+    *out = h;
+    return TSD_OK;
+}
+
+int tsd_model_create(const tsd_hparams * hp, int device, tsd_model ** out) {
+    if (!hp || !out) return TSD_ERR_ARG;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return TSD_ERR_CUDA;
+    tsd_model * h = new tsd_model();
+    h->m = new Model();
+    h->m->hp = *hp;
+    h->m->device = device;
+    cudaDeviceGetAttribute(&h->m->num_sms, cudaDevAttrMultiProcessorCount, device);
+    const int rs = make_stream(h);
+    if (rs) { delete h->m; delete h; return rs; }
+    *out = h;
+    return TSD_OK;
+}
+
+int tsd_model_set_tensor(tsd_model * h, const char * name, int ggml_type, const int64_t ne[4], const void * data,
+                         size_t nbytes) {
+    if (!h || !ne) return TSD_ERR_ARG;
+    return model_set_tensor(*h->m, name, ggml_type, ne, data, nbytes);
+}
+
+int tsd_model_finalize(tsd_model * h) {
+    if (!h) return TSD_ERR_ARG;
+    return model_finalize(*h->m);
+}
+
+void tsd_model_free(tsd_model * h) {
+    if (!h) return;
+    if (h->m) cudaSetDevice(h->m->device);
+    if (h->stream) cudaStreamDestroy(h->stream);
+    delete h->m;
+    delete h;
+}
+
+int tsd_model_get_hparams(const tsd_model * h, tsd_hparams * out) {
+    if (!h || !out) return TSD_ERR_ARG;
+    *out = h->m->hp;
+    return TSD_OK;
+}
+
+int tsd_get_tensor_f32(const tsd_model * h, const char * name, float * dst, int64_t n_dst, int64_t ne_out[4]) {
+    if (!h || !name) return TSD_ERR_ARG;
+    const RawTensor * t = h->m->get(name);
+    if (!t) {
+        fprintf(stderr, "tsd: tensor missing: '%s'\n", name);
+        return TSD_ERR_MISSING;
+    }
+    if (ne_out) for (int i = 0; i < 4; ++i) ne_out[i] = t->ne[i];
+    if (!dst) return TSD_OK;
+    if (n_dst < t->n()) return TSD_ERR_ARG;
+    if (!t->host.empty()) {
+        const std::vector<float> v = host_f32(*t);
+        memcpy(dst, v.data(), v.size() * 4);
+        return TSD_OK;
+    }
+    if (!t->d) return TSD_ERR_UNSUPPORTED;   // repacked projection weight: raw copy released
+    RawTensor tmp = *t;
+    tmp.host.resize(t->nbytes);
+    TSD_CUDA_TRY(cudaSetDevice(h->m->device));
+    TSD_CUDA_TRY(cudaMemcpy(tmp.host.data(), t->d, t->nbytes, cudaMemcpyDeviceToHost));
+    const std::vector<float> v = host_f32(tmp);
+    memcpy(dst, v.data(), v.size() * 4);
+    return TSD_OK;
+}
+
+int tsd_forward_batched(tsd_model * h, int B, const float * latent, int64_t T, const float * t, const float * clip_f,
+                        int64_t clip_S, const float * sync_f, int64_t sync_S, const float * text_f, int64_t text_S,
+                        const float * t5, int64_t t5_S, const float * global_text, float * flow_out, tsd_dbg_fn dbg,
+                        void * ud) {
+    if (!h || !latent || !t || !clip_f || !sync_f || (text_S && !text_f) || (t5_S && !t5) || !global_text || !flow_out)
+        return TSD_ERR_ARG;
+    if (!shape_ok(B, T, clip_S, sync_S, text_S, t5_S)) return TSD_ERR_ARG;
+    Model & m = *h->m;
+    TSD_CUDA_TRY(cudaSetDevice(m.device));
+    Plan * p = nullptr;
+    int rc = get_plan(m, Shape{B, (int)T, (int)clip_S, (int)sync_S, (int)text_S, (int)t5_S}, &p);
+    if (rc) return rc;
+    rc = stage_inputs(m, *p, Inputs{latent, t, clip_f, sync_f, text_f, t5, global_text}, h->stream);
+    if (rc) return rc;
+    rc = plan_run(m, *p, h->stream, dbg, ud);
+    if (rc) return rc;
+    TSD_CUDA_TRY(cudaMemcpyAsync(flow_out, p->flow, (size_t)B * T * m.L * 4, cudaMemcpyDefault, h->stream));
+    return check_device(m, h->stream);
+}
+
+int tsd_forward(tsd_model * h, const float * latent, int64_t T, float t, const float * clip_f, int64_t clip_S,
+                const float * sync_f, int64_t sync_S, const float * text_f, int64_t text_S, const float * t5, int64_t t5_S,
+                const float * global_text, float * flow_out) {
+    return tsd_forward_batched(h, 1, latent, T, &t, clip_f, clip_S, sync_f, sync_S, text_f, text_S, t5, t5_S, global_text,
+                               flow_out, nullptr, nullptr);
+}
+
+int tsd_forward_device(tsd_model * h, int B, const float * latent, int64_t T, const float * t, const float * clip_f,
+                       int64_t clip_S, const float * sync_f, int64_t sync_S, const float * text_f, int64_t text_S,
+                       const float * t5, int64_t t5_S, const float * global_text, float * flow_out, void * stream) {
+    if (!h || !latent || !t || !clip_f || !sync_f || (text_S && !text_f) || (t5_S && !t5) || !global_text || !flow_out)
+        return TSD_ERR_ARG;
+    if (!shape_ok(B, T, clip_S, sync_S, text_S, t5_S)) return TSD_ERR_ARG;
+    Model & m = *h->m;
+    TSD_CUDA_TRY(cudaSetDevice(m.device));
+    cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
+    Plan * p = nullptr;
+    int rc = get_plan(m, Shape{B, (int)T, (int)clip_S, (int)sync_S, (int)text_S, (int)t5_S}, &p);
+    if (rc) return rc;
+    rc = stage_inputs(m, *p, Inputs{latent, t, clip_f, sync_f, text_f, t5, global_text}, st);
+    if (rc) return rc;
+    rc = plan_run(m, *p, st, nullptr, nullptr);
+    if (rc) return rc;
+    TSD_CUDA_TRY(cudaMemcpyAsync(flow_out, p->flow, (size_t)B * T * m.L * 4, cudaMemcpyDeviceToDevice, st));
+    return TSD_OK;
+}
+
+int tsd_forward_profile(tsd_model * h, int B, const float * latent, int64_t T, const float * t, const float * clip_f,
+                        int64_t clip_S, const float * sync_f, int64_t sync_S, const float * text_f, int64_t text_S,
+                        const float * t5, int64_t t5_S, const float * global_text, float * flow_out, void * stream,
+                        int max_ops, int * n_ops, int * kind, int * launches, float * ms, double * flops, double * bytes) {
+    if (!h || !n_ops || !latent || !t || !clip_f || !sync_f || !global_text || !flow_out) return TSD_ERR_ARG;
+    if (!shape_ok(B, T, clip_S, sync_S, text_S, t5_S)) return TSD_ERR_ARG;
+    Model & m = *h->m;
+    TSD_CUDA_TRY(cudaSetDevice(m.device));
+    cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
+    Plan * p = nullptr;
+    int rc = get_plan(m, Shape{B, (int)T, (int)clip_S, (int)sync_S, (int)text_S, (int)t5_S}, &p);
+    if (rc) return rc;
+    rc = stage_inputs(m, *p, Inputs{latent, t, clip_f, sync_f, text_f, t5, global_text}, st);
+    if (rc) return rc;
+    std::vector<float> t_ms;
+    rc = plan_profile(m, *p, st, t_ms);
+    if (rc) return rc;
+    TSD_CUDA_TRY(cudaMemcpyAsync(flow_out, p->flow, (size_t)B * T * m.L * 4, cudaMemcpyDeviceToDevice, st));
+    *n_ops = (int)p->ops.size();
+    for (int i = 0; i < (int)p->ops.size() && i < max_ops; ++i) {
+        const Op & o = p->ops[i];
+        if (kind) kind[i] = o.kind;
+        if (launches) launches[i] = o.launches;
+        if (ms) ms[i] = t_ms[i];
+        if (flops) flops[i] = o.flops;
+        if (bytes) bytes[i] = o.bytes;
+    }
+    return check_device(m, st);
+}
+
+int tsd_sync_check(tsd_model * h, void * stream) {
+    if (!h) return TSD_ERR_ARG;
+    TSD_CUDA_TRY(cudaSetDevice(h->m->device));
+    return check_device(*h->m, stream ? (cudaStream_t)stream : h->stream);
+}
+
+int tsd_sample_batched(tsd_model * h, int P, const float * noise, int64_t T, const float * clip_f, int64_t clip_S,
+                       const float * sync_f, int64_t sync_S, const float * text_f, int64_t text_S, const float * t5,
+                       int64_t t5_S, const float * global_text, int steps, float cfg, float * out, float * flow0) {
+    if (!h || P < 1 || !noise || !clip_f || !sync_f || (text_S && !text_f) || (t5_S && !t5) || !global_text || !out || steps < 1)
+        return TSD_ERR_ARG;
+    const int B = 2 * P;
+    if (!shape_ok(B, T, clip_S, sync_S, text_S, t5_S)) return TSD_ERR_ARG;
+    Model & m = *h->m;
+    TSD_CUDA_TRY(cudaSetDevice(m.device));
+    // uncond conditioning: learned empties + zero global vector (mmdit.cpp:350-356, 364)
+    const RawTensor * es = m.get("empty_string_feat");
+    const RawTensor * et = m.get("empty_t5_feat");
+    if (!es || !et) return TSD_ERR_MISSING;
+    if (es->host.empty() || et->host.empty()) return TSD_ERR_UNSUPPORTED;
+    if (es->ne[0] != m.text_dim || es->ne[1] < text_S || et->ne[0] != m.t5_dim || et->ne[1] < t5_S) {
+        fprintf(stderr, "tsd: learned empties [%lld x %lld], [%lld x %lld] do not cover text_S %lld / t5_S %lld\n",
+                (long long)es->ne[0], (long long)es->ne[1], (long long)et->ne[0], (long long)et->ne[1], (long long)text_S,
+                (long long)t5_S);
+        return TSD_ERR_ARG;
+    }
+    const std::vector<float> es_h = host_f32(*es), et_h = host_f32(*et);
+    Plan * p = nullptr;
+    int rc = get_plan(m, Shape{B, (int)T, (int)clip_S, (int)sync_S, (int)text_S, (int)t5_S}, &p);
+    if (rc) return rc;
+    cudaStream_t st = h->stream;
+    const size_t L = (size_t)m.L;
+    // Stage the 2P conditioning items once: item 2p = cond, 2p+1 = uncond.
+    {
+        const size_t cn = (size_t)clip_S * m.clip_dim, yn = (size_t)sync_S * m.sync_dim;
+        const size_t tn = (size_t)text_S * m.text_dim, fn = (size_t)t5_S * m.t5_dim, gn = (size_t)m.text_dim;
+        std::vector<float> c2(2 * P * cn), y2(2 * P * yn), x2(2 * P * tn), f2(2 * P * fn), g2(2 * P * gn, 0.f);
+        for (int q = 0; q < P; ++q)
+            for (int k = 0; k < 2; ++k) {
+                const size_t i = 2 * q + k;
+                memcpy(&c2[i * cn], clip_f + q * cn, cn * 4);
+                memcpy(&y2[i * yn], sync_f + q * yn, yn * 4);
+                if (k == 0) {
+                    if (tn) memcpy(&x2[i * tn], text_f + q * tn, tn * 4);
+                    if (fn) memcpy(&f2[i * fn], t5 + q * fn, fn * 4);
+                    memcpy(&g2[i * gn], global_text + q * gn, gn * 4);
+                } else {
+                    if (tn) memcpy(&x2[i * tn], es_h.data(), tn * 4);
+                    if (fn) memcpy(&f2[i * fn], et_h.data(), fn * 4);
+                }
+            }
+        TSD_CUDA_TRY(cudaMemcpyAsync(p->clip_in, c2.data(), c2.size() * 4, cudaMemcpyHostToDevice, st));
+        TSD_CUDA_TRY(cudaMemcpyAsync(p->sync_in, y2.data(), y2.size() * 4, cudaMemcpyHostToDevice, st));
+        if (tn) TSD_CUDA_TRY(cudaMemcpyAsync(p->text_in, x2.data(), x2.size() * 4, cudaMemcpyHostToDevice, st));
+        if (fn) TSD_CUDA_TRY(cudaMemcpyAsync(p->t5_in, f2.data(), f2.size() * 4, cudaMemcpyHostToDevice, st));
+        TSD_CUDA_TRY(cudaMemcpyAsync(p->gtext_in, g2.data(), g2.size() * 4, cudaMemcpyHostToDevice, st));
+        TSD_CUDA_TRY(cudaStreamSynchronize(st));
+    }
+    float * x = nullptr, * f0 = nullptr, * tbuf = nullptr;
+    TSD_CUDA_TRY(cudaMalloc(&x, (size_t)P * L * T * 4));
+    if (flow0) cudaMalloc(&f0, (size_t)P * L * T * 4);
+    cudaMallocHost(&tbuf, (size_t)B * 4);
+    rc = TSD_OK;
+    cudaError_t e = cudaMemcpyAsync(x, noise, (size_t)P * L * T * 4, cudaMemcpyHostToDevice, st);
+    for (int s = 0; s < steps && e == cudaSuccess && rc == TSD_OK; ++s) {
+        const float t_curr = 1.0f - (float)s / steps, t_prev = 1.0f - (float)(s + 1) / steps;
+        e = cudaStreamSynchronize(st);      // tbuf is reused: the previous step's copy must be done
+        if (e != cudaSuccess) break;
+        for (int i = 0; i < B; ++i) tbuf[i] = t_curr;
+        e = cudaMemcpyAsync(p->t_in, tbuf, (size_t)B * 4, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = dup_latent(x, P, (int)L, (int)T, p->lat_in, st);
+        if (e != cudaSuccess) break;
+        rc = plan_run(m, *p, st, nullptr, nullptr);
+        if (rc) break;
+        e = cfg_euler(p->flow, P, (int)T, (int)L, cfg, t_prev - t_curr, x, (s == 0) ? f0 : nullptr, st);
+    }
+    if (e == cudaSuccess && rc == TSD_OK) e = cudaMemcpyAsync(out, x, (size_t)P * L * T * 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess && rc == TSD_OK && flow0 && f0) e = cudaMemcpyAsync(flow0, f0, (size_t)P * L * T * 4, cudaMemcpyDeviceToHost, st);
+    if (rc == TSD_OK) rc = (e == cudaSuccess) ? check_device(m, st) : TSD_ERR_CUDA;
+    if (e != cudaSuccess) fprintf(stderr, "tsd: sample: %s\n", cudaGetErrorString(e));
+    cudaStreamSynchronize(st);
+    cudaFree(x);
+    if (f0) cudaFree(f0);
+    cudaFreeHost(tbuf);
+    return rc;
+}
+
+int tsd_sample(tsd_model * h, const float * noise, int64_t T, const float * clip_f, int64_t clip_S, const float * sync_f,
+               int64_t sync_S, const float * text_f, int64_t text_S, const float * t5, int64_t t5_S,
+               const float * global_text, int steps, float cfg, float * out, float * flow0) {
+    return tsd_sample_batched(h, 1, noise, T, clip_f, clip_S, sync_f, sync_S, text_f, text_S, t5, t5_S, global_text, steps,
+                              cfg, out, flow0);
+}
+
+// ------------------------------- operator-level entry points -------------------------------
+
+int tsd_op_gemm(const void * W, int M, int K_in, int taps, int pad, const void * X, int nbatch, int S,
+                int64_t x_row_stride, int64_t x_batch_stride, int mode, int act, const float * bias, int m_valid,
+                void * out, int out_bf16, int64_t ldo, float * resid, int64_t ldr, const float * gate, int64_t ldg,
+                int gate_div, int max_splits, int * err, void * stream) {
+    if (!W || !X || mode < 0 || mode > 2 || (mode == EPI_GATE_RESID && (!resid || !gate || gate_div < 1)) ||
+        (mode != EPI_GATE_RESID && !out))
+        return TSD_ERR_ARG;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    GemmLaunch L;
+    const int numA = mode == EPI_SWIGLU ? 2 : 1;
+    if (!gemm_plan(L, W, M, K_in, taps, pad, numA, X, nbatch, S, x_row_stride, x_batch_stride, sms,
+                   mode == EPI_GATE_RESID ? max_splits : 1))
+        return TSD_ERR_ARG;
+    GemmParams & p = L.p;
+    p.mode = mode; p.act = act;
+    p.m_valid = m_valid > 0 ? m_valid : M;
+    p.bias = bias;
+    p.out = out; p.out_bf16 = out_bf16; p.ldo = ldo;
+    p.resid = resid; p.ldr = ldr; p.gate = gate; p.ldg = ldg; p.gate_div = gate_div > 0 ? gate_div : 1;
+    p.err = err;
+    TSD_CUDA_TRY(gemm_launch(L, (cudaStream_t)stream));
+    return TSD_OK;
+}
+
+int tsd_op_gemv(const void * W, int ggml_type, const void * W2, int M, int K, const float * x, int64_t ldx, int N,
+                const float * bias, int act, int round_bf16, void * y, int y_bf16, int64_t ldy, void * stream) {
+    if (!W || !x || !y) return TSD_ERR_ARG;
+    cudaError_t e = gemv_launch(W, ggml_type, W2, M, K, x, ldx, N, bias, act, round_bf16, y, y_bf16, ldy, (cudaStream_t)stream);
+    if (e == cudaErrorInvalidValue) return TSD_ERR_ARG;
+    TSD_CUDA_TRY(e);
+    return TSD_OK;
+}
+
+int tsd_op_attention(const void * Q, const void * K, const void * V, int B, int nh, int S, void * out, int64_t ldo, int * err,
+                     void * stream) {
+    if (!Q || !K || !V || !out) return TSD_ERR_ARG;
+    AttnLaunch L;
+    if (!attn_plan(L, Q, K, V, B, nh, S, out, ldo, err)) return TSD_ERR_ARG;
+    TSD_CUDA_TRY(attn_launch(L, (cudaStream_t)stream));
+    return TSD_OK;
+}
+
+int tsd_op_ln_modulate(const float * x, int rows, int H, const float * shift, const float * scale, int64_t ld_mod,
+                       int per_token, int rows_per_item, void * y, void * stream) {
+    if (!x || !shift || !scale || !y || rows < 1 || rows_per_item < 1) return TSD_ERR_ARG;
+    cudaError_t e = ln_modulate(x, rows, H, shift, scale, ld_mod, per_token, rows_per_item, (__nv_bfloat16 *)y, (cudaStream_t)stream);
+    if (e == cudaErrorInvalidValue) return TSD_ERR_ARG;
+    TSD_CUDA_TRY(e);
+    return TSD_OK;
+}
+
+int tsd_op_qk_norm_rope(const float * qkv, int B, int S, int H, int nh, const float * q_gain, const float * k_gain, int rope,
+                        float freq_scale, float theta, void * Q, void * K, void * V, int Sj, int s_off, void * stream) {
+    if (!qkv || !q_gain || !k_gain || !Q || !K || !V || s_off + S > Sj) return TSD_ERR_ARG;
+    cudaError_t e = qk_norm_rope(qkv, B, S, H, nh, q_gain, k_gain, rope, freq_scale, theta, (__half *)Q, (__half *)K,
+                                 (__half *)V, Sj, s_off, (cudaStream_t)stream);
+    if (e == cudaErrorInvalidValue) return TSD_ERR_ARG;
+    TSD_CUDA_TRY(e);
+    return TSD_OK;
+}
+
+}  // extern "C"

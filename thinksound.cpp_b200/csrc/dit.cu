@@ -1,0 +1,388 @@
+// dit.cu — forward plan of the MM-DiT velocity evaluation on one B200.
+//
+// Restates ts_dit::forward (src/mmdit.cpp:119-342) as a fixed sequence of kernel launches over
+// buffers allocated once per input shape (B, T, clip_S, sync_S, text_S, t5_S). The plan is
+// built once (tensor maps encoded, grids chosen) and replayed; replays are captured into a
+// CUDA graph. Token-major activations everywhere: x[b][t][H] f32 residual streams, bf16 GEMM
+// operands, fp16 head-major Q/K/V shared by the three streams of a joint block.
+#include "runtime.h"
+
+#include <algorithm>
+#include <cstring>
+
+namespace tsd {
+
+Plan::~Plan() {
+    if (graph) cudaGraphExecDestroy(graph);
+    for (void * p : allocs) cudaFree(p);
+}
+
+namespace {
+
+struct Builder {
+    Model & m;
+    Plan & P;
+    int rc = TSD_OK;
+
+    template <class T> T * alloc(size_t n) {
+        void * p = nullptr;
+        if (cudaMalloc(&p, std::max<size_t>(n * sizeof(T), 256)) != cudaSuccess) {
+            rc = TSD_ERR_CUDA;
+            return nullptr;
+        }
+        P.allocs.push_back(p);
+        return reinterpret_cast<T *>(p);
+    }
+    void op(std::function<cudaError_t(cudaStream_t)> fn, int kind = OP_ELEM, double flops = 0, double bytes = 0,
+            int launches = 1) {
+        Op o;
+        o.fn = std::move(fn);
+        o.kind = kind; o.flops = flops; o.bytes = bytes; o.launches = launches;
+        P.ops.push_back(std::move(o));
+    }
+    void snap(const char * name, const void * ptr, long long n, int kind = 0, int B = 0, int nh = 0, int S = 0) {
+        if (!P.ops.empty()) P.ops.back().snaps.push_back(Snap{name, ptr, n, kind, B, nh, S});
+    }
+
+    // GEMM over activations X [nbatch][S][K_in] (row stride xrs, batch stride xbs, elements).
+    void gemm(const GW & w, const void * X, int nbatch, int S, long long xrs, long long xbs, int mode, int act,
+              void * out, int out_bf16, long long ldo, float * resid = nullptr, long long ldr = 0,
+              const float * gate = nullptr, long long ldg = 0, int gate_div = 1, int numA = 1, int max_splits = 1,
+              long long row_off = 0, int M_override = 0) {
+        if (rc) return;
+        // Linear layers over a contiguous batch run as one long token sequence.
+        if (w.taps == 1 && xbs == (long long)S * xrs && nbatch > 1) { S *= nbatch; nbatch = 1; }
+        GemmLaunch L;
+        const int M = M_override ? M_override : w.M;
+        if (!gemm_plan(L, w.w + row_off * (long long)w.K_in * w.taps, M, w.K_in, w.taps, w.pad, numA, X, nbatch, S, xrs, xbs,
+                       m.num_sms, max_splits)) {
+            fprintf(stderr, "tsd: gemm plan failed (M %d K %d taps %d S %d)\n", M, w.K_in, w.taps, S);
+            rc = TSD_ERR_ARG;
+            return;
+        }
+        GemmParams & p = L.p;
+        p.mode = mode; p.act = act;
+        p.m_valid = M_override ? M : w.m_valid;
+        p.bias = w.bias ? w.bias + row_off : nullptr;
+        p.out = out; p.out_bf16 = out_bf16; p.ldo = ldo;
+        p.resid = resid; p.ldr = ldr; p.gate = gate; p.ldg = ldg; p.gate_div = gate_div;
+        p.err = m.d_err;
+        const double n_tok = (double)nbatch * S, kdim = (double)w.taps * w.K_in;
+        const double flops = 2.0 * p.m_valid * n_tok * kdim;
+        const double bytes = 2.0 * M * kdim + 2.0 * n_tok * w.K_in + n_tok * (mode == EPI_GATE_RESID ? 12.0 : (out_bf16 ? 2.0 : 4.0)) * (numA == 2 ? M / 2 : p.m_valid);
+        op([L](cudaStream_t st) { return gemm_launch(L, st); }, OP_GEMM, flops, bytes);
+    }
+    // Few-token GEMV over B items (chunks of 8 tokens).
+    void gemv(const VW & w, const float * x, long long ldx, int N, int act, float * y, long long ldy, int y_bf16 = 0) {
+        if (rc) return;
+        const VW wc = w;
+        op([wc, x, ldx, N, act, y, ldy, y_bf16](cudaStream_t st) {
+            for (int n0 = 0; n0 < N; n0 += 8) {
+                const int nn = std::min(8, N - n0);
+                cudaError_t e = gemv_launch(wc.w, wc.type, wc.w2, wc.M, wc.K, x + n0 * ldx, ldx, nn, wc.bias, act,
+                                            wc.type == GT_BF16, y_bf16 ? (void *)((__nv_bfloat16 *)y + n0 * ldy) : (void *)(y + n0 * ldy),
+                                            y_bf16, ldy, st);
+                if (e != cudaSuccess) return e;
+            }
+            return cudaSuccess;
+        }, OP_GEMV, 2.0 * w.M * w.K * N * (w.w2 ? 2 : 1),
+           (double)ggml_nbytes(w.type, (long long)w.M * w.K) * (w.w2 ? 2 : 1) * ((N + 7) / 8) + 4.0 * N * (w.K + w.M),
+           (N + 7) / 8);
+    }
+
+    void build() {
+        const Shape & sh = P.sh;
+        const int B = sh.B, T = sh.T, H = m.H, F = m.F, L = m.L, nh = m.nh;
+        const int cS = sh.clip_S, yS = sh.sync_S;
+        const int St = sh.text_S + sh.t5_S, Sj = T + cS + St;
+        const int maxS = std::max(std::max(T, cS), std::max(yS, St));
+        P.St = St; P.Sj = Sj; P.maxS = maxS;
+        const int R = m.ada_lat.M;
+        // ---- buffers ----
+        P.lat_in = alloc<float>((size_t)B * L * T);
+        P.clip_in = alloc<float>((size_t)B * cS * m.clip_dim);
+        P.sync_in = alloc<float>((size_t)B * yS * m.sync_dim);
+        P.text_in = alloc<float>((size_t)B * std::max(1, sh.text_S) * m.text_dim);
+        P.t5_in = alloc<float>((size_t)B * std::max(1, sh.t5_S) * m.t5_dim);
+        P.gtext_in = alloc<float>((size_t)B * m.text_dim);
+        P.t_in = alloc<float>((size_t)B);
+        P.flow = alloc<float>((size_t)B * T * L);
+        auto * lat_tok = alloc<__nv_bfloat16>((size_t)B * T * L);
+        auto * clip_tok = alloc<__nv_bfloat16>((size_t)B * cS * m.clip_dim);
+        auto * sync_tok = alloc<__nv_bfloat16>((size_t)B * yS * m.sync_dim);
+        auto * text_tok = alloc<__nv_bfloat16>((size_t)B * St * m.t5_dim);
+        auto * a1 = alloc<__nv_bfloat16>((size_t)B * maxS * H);
+        auto * hbuf = alloc<__nv_bfloat16>((size_t)B * maxS * F);
+        auto * xn = alloc<__nv_bfloat16>((size_t)B * maxS * H);
+        auto * qkv = alloc<float>((size_t)B * maxS * 3 * H);
+        float * x_lat = alloc<float>((size_t)B * T * H);
+        float * x_clip = alloc<float>((size_t)B * cS * H);
+        float * x_text = alloc<float>((size_t)B * St * H);
+        float * sync_out = alloc<float>((size_t)B * yS * H);
+        float * temb = alloc<float>((size_t)B * H);
+        float * te1 = alloc<float>((size_t)B * H);
+        float * te = alloc<float>((size_t)B * H);
+        float * text_fc = alloc<float>((size_t)B * H);
+        float * cmean = alloc<float>((size_t)B * H);
+        float * clip_fc = alloc<float>((size_t)B * H);
+        float * gsum = alloc<float>((size_t)B * H);
+        float * gch = alloc<float>((size_t)B * F);
+        float * gcm = alloc<float>((size_t)B * H);
+        float * gc = alloc<float>((size_t)B * H);
+        float * sgc = alloc<float>((size_t)B * H);
+        float * ext = alloc<float>((size_t)B * T * H);
+        auto * sext = alloc<__nv_bfloat16>((size_t)B * T * H);
+        float * mod_lat = alloc<float>((size_t)B * T * R);
+        float * mod_c = alloc<float>((size_t)B * 6 * H);
+        float * mod_t = alloc<float>((size_t)B * 6 * H);
+        auto * Qb = alloc<__half>((size_t)B * nh * Sj * 64);
+        auto * Kb = alloc<__half>((size_t)B * nh * Sj * 64);
+        auto * Vb = alloc<__half>((size_t)B * nh * Sj * 64);
+        auto * ao = alloc<__nv_bfloat16>((size_t)B * Sj * H);
+        if (rc) return;
+        int * err = m.d_err;
+        const float theta = m.hp.rope_theta;
+
+        op([err](cudaStream_t st) { return cudaMemsetAsync(err, 0, sizeof(int), st); }, OP_COPY, 0, 0, 0);
+
+        // ---- audio_input_proj (mmdit.cpp:150-155) ----
+        op([=](cudaStream_t st) { return latent_to_tokens(P.lat_in, B, L, T, lat_tok, st); });
+        gemm(m.ap0, lat_tok, B, T, L, (long long)T * L, EPI_STORE, ACT_SILU, a1, 1, H);
+        gemm(m.ap13, a1, B, T, H, (long long)T * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 2);
+        gemm(m.ap2, hbuf, B, T, F, (long long)T * F, EPI_STORE, ACT_NONE, x_lat, 0, H);
+        snap("x_in", x_lat, (long long)B * T * H);
+        // ---- t_embed (mmdit.cpp:157-161, 305-313) ----
+        const float maxp = m.hp.t_max_period;
+        op([=](cudaStream_t st) { return timestep_embed(P.t_in, B, H, maxp, temb, st); });
+        gemv(m.te0, temb, H, B, ACT_SILU, te1, H);
+        gemv(m.te2, te1, H, B, ACT_NONE, te, H);
+        snap("t_emb", te, (long long)B * H);
+        // ---- clip (mmdit.cpp:164-167) ----
+        op([=](cudaStream_t st) { return cast_f32_bf16(P.clip_in, (long long)B * cS * m.clip_dim, clip_tok, st); });
+        gemm(m.cp0, clip_tok, B, cS, m.clip_dim, (long long)cS * m.clip_dim, EPI_STORE, ACT_SILU, a1, 1, H);
+        gemm(m.cp13, a1, B, cS, H, (long long)cS * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 2);
+        gemm(m.cp2, hbuf, B, cS, F, (long long)cS * F, EPI_STORE, ACT_NONE, x_clip, 0, H);
+        snap("clip_pp", x_clip, (long long)B * cS * H);
+        // ---- sync (mmdit.cpp:168-177) ----
+        op([=](cudaStream_t st) { return sync_prep(P.sync_in, B, yS, m.sync_dim, m.sync_pe, sync_tok, st); });
+        gemm(m.sp0, sync_tok, B, yS, m.sync_dim, (long long)yS * m.sync_dim, EPI_STORE, ACT_SILU, a1, 1, H);
+        gemm(m.sp13, a1, B, yS, H, (long long)yS * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 2);
+        gemm(m.sp2, hbuf, B, yS, F, (long long)yS * F, EPI_STORE, ACT_NONE, sync_out, 0, H);
+        // ---- text (mmdit.cpp:178-183) ----
+        op([=](cudaStream_t st) {
+            return text_prep(P.text_in, sh.text_S, m.text_dim, P.t5_in, sh.t5_S, m.t5_dim, B, text_tok, st);
+        });
+        gemm(m.tp0, text_tok, B, St, m.t5_dim, (long long)St * m.t5_dim, EPI_STORE, ACT_SILU, a1, 1, H);
+        gemm(m.tp13, a1, B, St, H, (long long)St * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 2);
+        gemm(m.tp2, hbuf, B, St, F, (long long)St * F, EPI_STORE, ACT_NONE, x_text, 0, H);
+        snap("text_pp", x_text, (long long)B * St * H);
+        // ---- conditioning vectors (mmdit.cpp:184-200) ----
+        gemv(m.tcp, P.gtext_in, m.text_dim, B, ACT_NONE, text_fc, H);
+        snap("text_fc", text_fc, (long long)B * H);
+        op([=](cudaStream_t st) { return seq_mean(x_clip, B, cS, H, cmean, st); });
+        gemv(m.ccp, cmean, H, B, ACT_NONE, clip_fc, H);
+        snap("clip_fc", clip_fc, (long long)B * H);
+        op([=](cudaStream_t st) { return add_vec(clip_fc, text_fc, B * H, gsum, st); });
+        gemv(m.gc13, gsum, H, B, ACT_NONE, gch, F);
+        gemv(m.gc2, gch, F, B, ACT_NONE, gcm, H);
+        snap("gcmlp", gcm, (long long)B * H);
+        op([=](cudaStream_t st) { return add_vec(gcm, te, B * H, gc, st); });
+        snap("global_c", gc, (long long)B * H);
+        op([=](cudaStream_t st) { return build_extended(sync_out, yS, gc, B, T, H, ext, sext, sgc, st); });
+        snap("extended_c", ext, (long long)B * T * H);
+        // ---- every per-token adaLN of the step in one GEMM (mmdit.cpp:209, 285) ----
+        gemm(m.ada_lat, sext, B, T, H, (long long)T * H, EPI_STORE, ACT_NONE, mod_lat, 0, R);
+
+        // ---- joint blocks (mmdit.cpp:237-272) ----
+        const int n_joint = (int)m.joint.size();
+        float * xs[3] = {x_lat, x_clip, x_text};
+        const int Ss[3] = {T, cS, St};
+        const int soff[3] = {0, T, T + cS};
+        float * modc[3] = {nullptr, mod_c, mod_t};
+        AttnLaunch AJ, AF;
+        if (!attn_plan(AJ, Qb, Kb, Vb, B, nh, Sj, ao, H, err) || !attn_plan(AF, Qb, Kb, Vb, B, nh, T, ao, H, err)) {
+            rc = TSD_ERR_ARG;
+            return;
+        }
+        for (int i = 0; i < n_joint; ++i) {
+            const auto & blk = m.joint[i];
+            for (int s = 0; s < 3; ++s) {
+                const StreamW & w = blk[s];
+                const int S = Ss[s];
+                const float * mod;
+                long long ld;
+                if (s == 0) { mod = mod_lat + w.ada_off; ld = R; }
+                else {
+                    ld = (long long)(w.pre_only ? 2 : 6) * H;
+                    gemv(w.ada, sgc, H, B, ACT_NONE, modc[s], ld);
+                    mod = modc[s];
+                }
+                op([=](cudaStream_t st) { return ln_modulate(xs[s], B * S, H, mod, mod + H, ld, s == 0, S, xn, st); });
+                if (i == 0 && s == 2) snap("text_xn", xn, (long long)B * S * H, 1);
+                gemm(w.qkv, xn, B, S, H, (long long)S * H, EPI_STORE, ACT_NONE, qkv, 0, 3 * H);
+                const float fs = (s == 1) ? (float)T / (float)cS : 1.0f;
+                const StreamW wc = w;
+                const int sofs = soff[s];
+                op([=](cudaStream_t st) {
+                    return qk_norm_rope(qkv, B, S, H, nh, wc.qg, wc.kg, s != 2, fs, theta, Qb, Kb, Vb, Sj, sofs, st);
+                });
+            }
+            if (i == 0) {
+                snap("a0_q", Qb, (long long)B * Sj * H, 2, B, nh, Sj);
+                snap("a0_k", Kb, (long long)B * Sj * H, 2, B, nh, Sj);
+                snap("a0_v", Vb, (long long)B * Sj * H, 2, B, nh, Sj);
+            }
+            op([AJ](cudaStream_t st) { return attn_launch(AJ, st); }, OP_ATTN, 4.0 * B * nh * 64.0 * Sj * Sj,
+               6.0 * B * nh * 64.0 * Sj + 2.0 * B * Sj * H);
+            if (i == 0) snap("a0_out", ao, (long long)B * Sj * H, 1);
+            for (int s = 0; s < 3; ++s) {
+                const StreamW & w = blk[s];
+                if (w.pre_only) continue;
+                const int S = Ss[s];
+                const float * mod = (s == 0) ? mod_lat + w.ada_off : modc[s];
+                const long long ld = (s == 0) ? R : 6LL * H;
+                const int gdiv = (s == 0) ? 1 : S;
+                gemm(w.l1, ao + (long long)soff[s] * H, B, S, H, (long long)Sj * H, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0,
+                     xs[s], H, mod + 2 * H, ld, gdiv, 1, 4);
+                op([=](cudaStream_t st) { return ln_modulate(xs[s], B * S, H, mod + 3 * H, mod + 4 * H, ld, s == 0, S, xn, st); });
+                gemm(w.w13, xn, B, S, H, (long long)S * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 2);
+                gemm(w.w2, hbuf, B, S, F, (long long)S * F, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, xs[s], H, mod + 5 * H,
+                     ld, gdiv, 1, 4);
+            }
+            if (i == 0) {
+                snap("jb0_lat", x_lat, (long long)B * T * H);
+                snap("jb0_clip", x_clip, (long long)B * cS * H);
+                snap("jb0_text", x_text, (long long)B * St * H);
+            }
+        }
+        snap("after_joint", x_lat, (long long)B * T * H);
+        // ---- fused blocks (mmdit.cpp:274-282) ----
+        for (const StreamW & w : m.fused) {
+            const float * mod = mod_lat + w.ada_off;
+            const long long ld = R;
+            op([=](cudaStream_t st) { return ln_modulate(x_lat, B * T, H, mod, mod + H, ld, 1, T, xn, st); });
+            gemm(w.qkv, xn, B, T, H, (long long)T * H, EPI_STORE, ACT_NONE, qkv, 0, 3 * H);
+            const StreamW wc = w;
+            op([=](cudaStream_t st) { return qk_norm_rope(qkv, B, T, H, nh, wc.qg, wc.kg, 1, 1.0f, theta, Qb, Kb, Vb, T, 0, st); });
+            op([AF](cudaStream_t st) { return attn_launch(AF, st); }, OP_ATTN, 4.0 * B * nh * 64.0 * T * T,
+               6.0 * B * nh * 64.0 * T + 2.0 * B * T * H);
+            gemm(w.l1, ao, B, T, H, (long long)T * H, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, x_lat, H, mod + 2 * H, ld, 1, 1, 4);
+            op([=](cudaStream_t st) { return ln_modulate(x_lat, B * T, H, mod + 3 * H, mod + 4 * H, ld, 1, T, xn, st); });
+            gemm(w.w13, xn, B, T, H, (long long)T * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 2);
+            gemm(w.w2, hbuf, B, T, F, (long long)T * F, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, x_lat, H, mod + 5 * H, ld, 1, 1, 4);
+        }
+        snap("after_fused", x_lat, (long long)B * T * H);
+        // ---- final layer (mmdit.cpp:284-290) ----
+        const float * fmod = mod_lat + m.final_ada_off;
+        op([=](cudaStream_t st) { return ln_modulate(x_lat, B * T, H, fmod, fmod + H, R, 1, T, xn, st); });
+        gemm(m.fconv, xn, B, T, H, (long long)T * H, EPI_STORE, ACT_NONE, P.flow, 0, L);
+        snap("flow_cl", P.flow, (long long)B * T * L);
+    }
+};
+
+void to_host_f32(const Snap & s, std::vector<float> & out) {
+    out.resize((size_t)s.n);
+    if (s.kind == 0) {
+        cudaMemcpy(out.data(), s.ptr, (size_t)s.n * 4, cudaMemcpyDeviceToHost);
+    } else if (s.kind == 1) {
+        std::vector<uint16_t> h((size_t)s.n);
+        cudaMemcpy(h.data(), s.ptr, (size_t)s.n * 2, cudaMemcpyDeviceToHost);
+        for (long long i = 0; i < s.n; ++i) { uint32_t u = (uint32_t)h[i] << 16; memcpy(&out[i], &u, 4); }
+    } else {
+        std::vector<__half> h((size_t)s.n);
+        cudaMemcpy(h.data(), s.ptr, (size_t)s.n * 2, cudaMemcpyDeviceToHost);
+        const int H = s.nh * 64;
+        for (int b = 0; b < s.B; ++b)
+            for (int hh = 0; hh < s.nh; ++hh)
+                for (int t = 0; t < s.S; ++t)
+                    for (int d = 0; d < 64; ++d)
+                        out[((size_t)b * s.S + t) * H + hh * 64 + d] =
+                            __half2float(h[(((size_t)b * s.nh + hh) * s.S + t) * 64 + d]);
+    }
+}
+
+}  // namespace
+
+int plan_build(Model & m, const Shape & sh, std::unique_ptr<Plan> & out) {
+    if (sh.B < 1 || sh.T < 1 || sh.clip_S < 1 || sh.sync_S < 8 || sh.sync_S % 8 || sh.text_S < 0 || sh.t5_S < 0 ||
+        sh.text_S + sh.t5_S < 1)
+        return TSD_ERR_ARG;
+    TSD_CUDA_TRY(cudaSetDevice(m.device));
+    std::unique_ptr<Plan> p(new Plan());
+    p->sh = sh;
+    Builder b{m, *p};
+    b.build();
+    if (b.rc) return b.rc;
+    out = std::move(p);
+    return TSD_OK;
+}
+
+int plan_profile(Model & m, Plan & p, cudaStream_t st, std::vector<float> & ms) {
+    (void)m;
+    std::vector<cudaEvent_t> ev(p.ops.size() + 1);
+    for (auto & e : ev) TSD_CUDA_TRY(cudaEventCreate(&e));
+    int rc = TSD_OK;
+    cudaError_t ce = cudaEventRecord(ev[0], st);
+    for (size_t i = 0; i < p.ops.size() && ce == cudaSuccess; ++i) {
+        ce = p.ops[i].fn(st);
+        if (ce == cudaSuccess) ce = cudaEventRecord(ev[i + 1], st);
+    }
+    if (ce == cudaSuccess) ce = cudaEventSynchronize(ev.back());
+    ms.assign(p.ops.size(), 0.f);
+    if (ce == cudaSuccess)
+        for (size_t i = 0; i < p.ops.size(); ++i) cudaEventElapsedTime(&ms[i], ev[i], ev[i + 1]);
+    else {
+        fprintf(stderr, "tsd: profile: %s\n", cudaGetErrorString(ce));
+        rc = TSD_ERR_CUDA;
+    }
+    for (auto & e : ev) cudaEventDestroy(e);
+    return rc;
+}
+
+int plan_run(Model & m, Plan & p, cudaStream_t st, tsd_dbg_fn dbg, void * ud) {
+    if (dbg) {
+        std::vector<float> h;
+        for (const Op & o : p.ops) {
+            TSD_CUDA_TRY(o.fn(st));
+            if (!o.snaps.empty()) {
+                TSD_CUDA_TRY(cudaStreamSynchronize(st));
+                for (const Snap & s : o.snaps) {
+                    to_host_f32(s, h);
+                    dbg(ud, s.name.c_str(), h.data(), (int64_t)h.size());
+                }
+            }
+        }
+        return TSD_OK;
+    }
+    if (!p.graph || p.graph_stream != st) {
+        if (p.graph) { cudaGraphExecDestroy(p.graph); p.graph = nullptr; }
+        cudaStreamCaptureStatus cs;
+        TSD_CUDA_TRY(cudaStreamIsCapturing(st, &cs));
+        const bool can_capture = (st != nullptr) && cs == cudaStreamCaptureStatusNone;
+        if (!can_capture) {
+            for (const Op & o : p.ops) TSD_CUDA_TRY(o.fn(st));
+            return TSD_OK;
+        }
+        cudaGraph_t g;
+        TSD_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        cudaError_t e = cudaSuccess;
+        for (const Op & o : p.ops) {
+            e = o.fn(st);
+            if (e != cudaSuccess) break;
+        }
+        cudaError_t e2 = cudaStreamEndCapture(st, &g);
+        if (e != cudaSuccess || e2 != cudaSuccess) {
+            if (e2 == cudaSuccess) cudaGraphDestroy(g);
+            fprintf(stderr, "tsd: graph capture failed: %s\n", cudaGetErrorString(e != cudaSuccess ? e : e2));
+            return TSD_ERR_CUDA;
+        }
+        e = cudaGraphInstantiate(&p.graph, g, 0);
+        cudaGraphDestroy(g);
+        TSD_CUDA_TRY(e);
+        p.graph_stream = st;
+    }
+    TSD_CUDA_TRY(cudaGraphLaunch(p.graph, st));
+    return TSD_OK;
+}
+
+}  // namespace tsd

@@ -1,0 +1,119 @@
+// kernels.h — host-side launch interface of the sm_100a kernels (internal to libtsd_b200).
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace tsd {
+
+// ---------------------------------------------------------------------------------------------
+// tcgen05 GEMM:  out[b][t][m] = epi( sum_tap sum_k  X[b][t + tap - pad][k] * W[m][tap*K_in + k] )
+//   W: bf16, [M rows][taps*K_in] (tap-major columns), via a 2-D tensor map (box 64 x 128*numA).
+//   X: bf16 activations, [nbatch][S][K_in] with arbitrary row / batch strides, via a 3-D tensor
+//      map (box 64 x BN x 1). Rows outside [0, S) of an item read as zero (conv padding).
+// One CTA computes a 128-feature x BN-token tile (two 128-feature tiles for the SwiGLU pair).
+// ---------------------------------------------------------------------------------------------
+enum EpiMode : int {
+    EPI_STORE = 0,       // out = act(acc + bias)                       (f32 or bf16)
+    EPI_SWIGLU = 1,      // out = silu(acc_w1) * acc_w3                  (bf16)
+    EPI_GATE_RESID = 2,  // resid += gate * (acc + bias)                 (f32, split-K via atomics)
+};
+enum Act : int { ACT_NONE = 0, ACT_SILU = 1 };
+
+struct GemmParams {
+    int M;             // weight rows covered by the grid (multiple of 128; per A tile of 128)
+    int S;             // tokens per batch item
+    int nbatch;
+    int K_in;          // input features per tap (multiple of 64)
+    int taps, pad;
+    int BN;            // token tile (multiple of 16, <= 256)
+    int n_tiles;       // ceil(S / BN)
+    int splits;        // split-K factor
+    int mode, act;
+    int m_valid;       // features >= m_valid are not stored (zero-padded weight rows)
+    const float * bias;
+    void * out; int out_bf16; long long ldo;       // out row = b*S + t
+    float * resid; long long ldr;
+    const float * gate; long long ldg; int gate_div;   // gate row = out row / gate_div
+    int * err;
+};
+
+struct GemmLaunch {
+    CUtensorMap tmA, tmB;
+    GemmParams p;
+    int numA;           // 1, or 2 for the SwiGLU pair
+    dim3 grid;
+};
+
+// Tensor-map helpers (driver entry point resolved at first use).
+bool make_tmap_2d(CUtensorMap * m, const void * ptr, CUtensorMapDataType dt, int esize,
+                  uint64_t d0, uint64_t d1, uint64_t stride1_bytes, uint32_t b0, uint32_t b1);
+bool make_tmap_3d(CUtensorMap * m, const void * ptr, CUtensorMapDataType dt, int esize,
+                  uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
+                  uint32_t b0, uint32_t b1, uint32_t b2);
+
+// Fill `L` for a GEMM; returns false on unsupported arguments.
+bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pad, int numA,
+               const void * X, int nbatch, int S, long long x_row_stride, long long x_batch_stride,
+               int num_sms, int max_splits);
+cudaError_t gemm_launch(const GemmLaunch & L, cudaStream_t st);
+
+// ---------------------------------------------------------------------------------------------
+// GEMV for a handful of tokens (N <= 8): y[n][m] = act(sum_k x[n][k] * W[m][k] + bias[m]),
+// weights in their stored ggml type (0 f32, 30 bf16, 8 q8_0), read once from HBM.
+// dual: W2 given -> y = silu(W x) * (W2 x) (SwiGLU pair, no bias).
+// round_bf16: round x to bf16 first (what the reference's mul_mat does for BF16 weights).
+// ---------------------------------------------------------------------------------------------
+cudaError_t gemv_launch(const void * W, int wtype, const void * W2, int M, int K, const float * x,
+                        long long ldx, int N, const float * bias, int act, int round_bf16,
+                        void * y, int y_bf16, long long ldy, cudaStream_t st);
+
+// ---------------------------------------------------------------------------------------------
+// Attention (tcgen05): O = softmax(Q K^T * scale) V per (batch, head); Q, K, V fp16
+// [B*nh][S][64] (head-major). O written bf16 token-major: out[b][t][h*64 + d], row stride ldo.
+// ---------------------------------------------------------------------------------------------
+struct AttnLaunch {
+    CUtensorMap tmQ, tmK, tmV;
+    int S, nh, B;
+    long long ldo;
+    void * out;
+    int * err;
+    float scale;
+};
+bool attn_plan(AttnLaunch & L, const void * Q, const void * K, const void * V, int B, int nh, int S,
+               void * out, long long ldo, int * err);
+cudaError_t attn_launch(const AttnLaunch & L, cudaStream_t st);
+
+// ---------------------------------------------------------------------------------------------
+// Elementwise / normalisation kernels
+// ---------------------------------------------------------------------------------------------
+// y = LN(x) * (1 + scale) + shift, LN eps 1e-5 without affine; x f32 [rows][H];
+// shift/scale rows: row (per_token) or row / rows_per_item. y bf16 [rows][H].
+cudaError_t ln_modulate(const float * x, int rows, int H, const float * shift, const float * scale,
+                        long long ld_mod, int per_token, int rows_per_item, __nv_bfloat16 * y, cudaStream_t st);
+// qkv f32 [B][S][3H] (Q|K|V column blocks) -> RMSNorm(q,k)*gain, RoPE (if fscale > 0), fp16
+// head-major at sequence offset s_off of joint buffers [B][nh][Sj][64].
+cudaError_t qk_norm_rope(const float * qkv, int B, int S, int H, int nh, const float * qg, const float * kg,
+                         int rope, float fscale, float theta, __half * Q, __half * K, __half * V, int Sj, int s_off,
+                         cudaStream_t st);
+cudaError_t latent_to_tokens(const float * lat, int B, int C, int T, __nv_bfloat16 * y, cudaStream_t st);
+cudaError_t sync_prep(const float * sync, int B, int S, int C, const float * pos_emb, __nv_bfloat16 * y, cudaStream_t st);
+cudaError_t text_prep(const float * text, int text_S, int text_dim, const float * t5, int t5_S, int t5_dim,
+                      int B, __nv_bfloat16 * y, cudaStream_t st);
+cudaError_t timestep_embed(const float * t, int B, int H, float max_period, float * y, cudaStream_t st);
+cudaError_t seq_mean(const float * x, int B, int S, int H, float * y, cudaStream_t st);
+cudaError_t add_vec(const float * a, const float * b, int n, float * y, cudaStream_t st);
+// ext[b][t] = sync[b][floor((t+0.5)*sync_S/T)] + gc[b]; sext = bf16(silu(ext)); sgc = silu(gc)
+cudaError_t build_extended(const float * sync, int sync_S, const float * gc, int B, int T, int H,
+                           float * ext, __nv_bfloat16 * sext, float * sgc, cudaStream_t st);
+cudaError_t cast_f32_bf16(const float * x, long long n, __nv_bfloat16 * y, cudaStream_t st);
+// CFG combine + Euler update on [B2][T][L] flows: pairs (cond = item 2p, uncond = 2p+1);
+// x [P][L][T] (t fastest) += dt * (u + (c - u) * cfg); optionally also store v into flow0.
+cudaError_t cfg_euler(const float * flow, int P, int T, int L, float cfg, float dt, float * x, float * flow0,
+                      cudaStream_t st);
+// Pack x [P][L][T] into both halves of the batched latent input [2P][L][T].
+cudaError_t dup_latent(const float * x, int P, int L, int T, float * lat2, cudaStream_t st);
+
+}  // namespace tsd

@@ -1,0 +1,136 @@
+// runtime.h — host runtime of libtsd_b200: device weight store and forward plans.
+#pragma once
+#include "kernels.h"
+#include "../../include/tsd.h"
+
+#include <array>
+#include <cstdio>
+#include <functional>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+namespace tsd {
+
+#define TSD_CUDA_TRY(expr)                                                                                  \
+    do {                                                                                                    \
+        cudaError_t e_ = (expr);                                                                            \
+        if (e_ != cudaSuccess) {                                                                            \
+            fprintf(stderr, "tsd: CUDA error %s at %s:%d: %s\n", cudaGetErrorName(e_), __FILE__, __LINE__,     \
+                    cudaGetErrorString(e_));                                                                \
+            return TSD_ERR_CUDA;                                                                            \
+        }                                                                                                   \
+    } while (0)
+
+enum : int { GT_F32 = 0, GT_F16 = 1, GT_Q8_0 = 8, GT_BF16 = 30 };
+size_t ggml_nbytes(int type, int64_t n);
+
+// A tensor as stored (ggml type and layout) in device memory; small tensors keep a host copy.
+struct RawTensor {
+    int type = GT_F32;
+    int64_t ne[4] = {1, 1, 1, 1};
+    void * d = nullptr;
+    size_t nbytes = 0;
+    std::vector<uint8_t> host;
+    int64_t n() const { return ne[0] * ne[1] * ne[2] * ne[3]; }
+};
+
+// A projection weight repacked for the tcgen05 GEMM: bf16 [M][taps*K_in], tap-major columns.
+struct GW {
+    __nv_bfloat16 * w = nullptr;
+    int M = 0, K_in = 0, taps = 1, pad = 0, m_valid = 0;
+    float * bias = nullptr;
+};
+// A weight used by the few-token GEMV in its stored type.
+struct VW {
+    const void * w = nullptr, * w2 = nullptr;
+    int type = GT_F32, M = 0, K = 0;
+    const float * bias = nullptr;
+};
+struct StreamW {
+    bool present = false, pre_only = false, conv = false;
+    GW qkv, l1, w13, w2;
+    const float * qg = nullptr, * kg = nullptr;
+    long long ada_off = 0;   // latent-style: first row in the batched adaLN weight
+    int ada_rows = 0;
+    VW ada;                  // global-conditioned (clip / text): GEMV weight
+};
+
+struct Plan;
+
+struct Model {
+    tsd_hparams hp{};
+    int device = 0, num_sms = 148;
+    int H = 0, nh = 0, F = 0, L = 64;
+    int clip_dim = 1024, sync_dim = 768, text_dim = 1024, t5_dim = 2048;
+    bool finalized = false;
+    std::unordered_map<std::string, RawTensor> raw;
+    std::vector<void *> allocs;
+
+    GW ap0, ap13, ap2, cp0, cp13, cp2, sp0, sp13, sp2, tp0, tp13, tp2, fconv;
+    VW te0, te2, tcp, ccp, gc13, gc2;
+    const float * sync_pe = nullptr;
+    GW ada_lat;                // all latent-style adaLN weights stacked (joint latent, fused, final)
+    long long final_ada_off = 0;
+    std::vector<std::array<StreamW, 3>> joint;
+    std::vector<StreamW> fused;
+    int * d_err = nullptr;
+    std::unique_ptr<Plan> plan;
+
+    ~Model();
+    void * dalloc(size_t bytes);
+    const RawTensor * get(const std::string & n) const {
+        auto it = raw.find(n);
+        return it == raw.end() ? nullptr : &it->second;
+    }
+};
+
+int model_set_tensor(Model & m, const char * name, int type, const int64_t ne[4], const void * data, size_t nbytes);
+int model_finalize(Model & m);
+int model_load_gguf(const char * path, int device, Model ** out);
+
+// Debug snapshot of a device buffer after an op of the forward.
+struct Snap {
+    std::string name;
+    const void * ptr;
+    long long n;
+    int kind;          // 0 f32, 1 bf16, 2 fp16 head-major [B][nh][S][64] (S = rows) -> [B][S][H]
+    int B, nh, S;
+};
+enum OpKind : int { OP_GEMM = 0, OP_GEMV = 1, OP_ATTN = 2, OP_ELEM = 3, OP_COPY = 4 };
+struct Op {
+    std::function<cudaError_t(cudaStream_t)> fn;
+    std::vector<Snap> snaps;
+    int kind = OP_ELEM;
+    int launches = 1;          // kernel launches the op issues
+    double flops = 0, bytes = 0;   // algorithmic work of the op
+};
+
+struct Shape {
+    int B, T, clip_S, sync_S, text_S, t5_S;
+    bool operator==(const Shape & o) const {
+        return B == o.B && T == o.T && clip_S == o.clip_S && sync_S == o.sync_S && text_S == o.text_S && t5_S == o.t5_S;
+    }
+};
+
+struct Plan {
+    Shape sh{};
+    int St = 0, Sj = 0, maxS = 0;
+    // inputs / output (device)
+    float * lat_in = nullptr, * clip_in = nullptr, * sync_in = nullptr, * text_in = nullptr, * t5_in = nullptr;
+    float * gtext_in = nullptr, * t_in = nullptr, * flow = nullptr;
+    std::vector<Op> ops;
+    std::vector<void *> allocs;
+    cudaGraphExec_t graph = nullptr;
+    cudaStream_t graph_stream = nullptr;
+    ~Plan();
+};
+
+int plan_build(Model & m, const Shape & sh, std::unique_ptr<Plan> & out);
+// Enqueue the forward (inputs already in the plan's buffers).
+int plan_run(Model & m, Plan & p, cudaStream_t st, tsd_dbg_fn dbg, void * ud);
+// Run the forward op by op with CUDA events around each op; per-op milliseconds.
+int plan_profile(Model & m, Plan & p, cudaStream_t st, std::vector<float> & ms);
+
+}  // namespace tsd
