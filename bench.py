@@ -311,7 +311,7 @@ def main():
                 "gemv": {"launches": int(prof["launches"][kinds == 1].sum()), "ms": v_ms,
                          "gbs": v_by / (v_ms / 1000.0) / 1e9 if v_ms else None},
                 "other_ms": tot_ms - g_ms - a_ms - v_ms, "profiled_step_ms": tot_ms,
-                "step_tflops_device": fl["total"] * args.pairs / 2 * 2 / (ms_max / args.steps / 1000.0) / 1e12,
+                "step_tflops_device": fl["total"] / (ms_max / args.steps / 1000.0) / 1e12,
             },
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": d2h},
             "gpu_launches": launches_per_step * args.steps,

@@ -75,6 +75,9 @@ TSD_API int tsd_forward_profile(struct tsd_model * m, int B, const float * laten
                                 const float * text_f, int64_t text_S, const float * t5, int64_t t5_S,
                                 const float * global_text, float * flow_out, void * stream, int max_ops, int * n_ops,
                                 int * kind, int * launches, float * ms, double * flops, double * bytes);
+/* Label of op i of the model's current forward plan (stage, kind, GEMM shape and grid), or
+ * NULL if there is no plan or i is out of range. Valid until the plan is rebuilt. */
+TSD_API const char * tsd_plan_op_label(struct tsd_model * m, int i);
 
 #ifdef __cplusplus
 }

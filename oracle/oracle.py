@@ -76,9 +76,12 @@ class OracleModel:
                 raise RuntimeError(f"tso_model_set({name}) -> {rc}")
 
     def __del__(self):
-        if getattr(self, "h", None):
-            lib().tso_model_free(self.h)
-            self.h = None
+        try:
+            if getattr(self, "h", None) and _lib is not None:
+                _lib.tso_model_free(self.h)
+                self.h = None
+        except Exception:
+            pass
 
     def forward(self, x, mode: int = MODE_GGML, dbg: bool = False):
         """One batch item (synth.DitInputs). Returns flow [T][latent] (and dbg dict)."""

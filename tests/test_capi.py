@@ -94,3 +94,23 @@ def test_gguf_writer_round_trip(tmp_path):
     t = got["joint_blocks.0.latent_block.attn.qkv.weight"]
     assert int(t.tensor_type) == synth.GGML_Q8_0
     assert np.array_equal(np.asarray(t.data).view(np.uint8).ravel(), W[t.name].data.view(np.uint8).ravel())
+
+
+SHIM_SRC = os.path.join(REPO, "tests", "shim", "ts_dit_demo.cpp")
+
+
+def build_shim_demo(out_dir):
+    """Compile the ts_dit drop-in demo against include/ and libtsd_b200.so (g++, C++17)."""
+    import subprocess
+    exe = os.path.join(str(out_dir), "ts_dit_demo")
+    libdir = os.path.join(REPO, "thinksound.cpp_b200")
+    subprocess.run(["g++", "-std=c++17", "-O1", "-I", os.path.join(REPO, "include"), SHIM_SRC, "-o", exe,
+                    "-L", libdir, "-ltsd_b200", f"-Wl,-rpath,{libdir}"], check=True)
+    return exe
+
+
+def test_ts_dit_shim_compiles_and_reports_load_failure(tmp_path):
+    import subprocess
+    exe = build_shim_demo(tmp_path)
+    r = subprocess.run([exe, str(tmp_path / "missing.gguf"), "20", "8", "24", "1"], capture_output=True, text=True)
+    assert r.returncode == 1 and "load failed" in r.stderr

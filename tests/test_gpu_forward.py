@@ -31,28 +31,54 @@ def small_bf16():
     return hp, W, tsd.DitModel.from_weights(hp, W), oracle.OracleModel(hp, W)
 
 
+STAGES = ("x_in", "t_emb", "clip_pp", "text_pp", "clip_fc", "text_fc", "gcmlp", "global_c", "extended_c", "text_xn",
+          "a0_q", "a0_k", "a0_v", "a0_out", "jb0_lat", "jb0_clip", "jb0_text", "after_joint", "after_fused", "flow_cl")
+BF16_STAGES = ("text_xn", "a0_out")   # stored bf16 on the GPU: the precision their consumer GEMM reads
+
+
+def check_stages(dg, b, nb, x, hp, W, om, factor=2.5, floor_min=1e-3):
+    """Per-stage parity with a measured noise floor.
+
+    The reference rounds every mul_mat operand to bf16; two correct implementations of that
+    arithmetic (the C++ oracle and the PyTorch emulation) already differ because 1e-7-level
+    accumulation-order differences flip bf16 roundings, and the flips compound over the blocks.
+    Each stage must be within `factor` x that floor (at least `floor_min`) of the oracle, and at
+    least as close to the exact-f32 restatement as the reference arithmetic itself is.
+    """
+    import torch
+    import torch_ref
+    fo, do = om.forward(x, mode=oracle.MODE_GGML, dbg=True)
+    fe, de = om.forward(x, mode=oracle.MODE_EXACT, dbg=True)
+    dt = {}
+    torch_ref.TorchDiT(hp, W, dtype=torch.float32, emulate=True).forward(x, dbg=dt)
+    report = {}
+    for name in STAGES:
+        g = dg[name].reshape(nb, -1)[b]
+        o, e, t = do[name], de[name], dt[name]
+        if name in BF16_STAGES:
+            o, t = bf16_round(o), bf16_round(t)
+        floor = max(floor_min, oracle.rel_l2(t, o))
+        err = oracle.rel_l2(g, o)
+        report[name] = (err, floor)
+        assert err <= factor * floor, (name, err, floor)
+        if name not in BF16_STAGES and name != "t_emb":
+            assert oracle.rel_l2(g, e) <= 1.1 * oracle.rel_l2(o, e) + 5e-4, (name, oracle.rel_l2(g, e), oracle.rel_l2(o, e))
+    return report
+
+
 def test_forward_stages_match_oracle(small_bf16):
     hp, W, m, om = small_bf16
     items = synth.make_inputs(hp, seed=4242, batch=2, **SHAPE)
     flow, dg = m.forward(items, dbg=True)
     for b, x in enumerate(items):
-        fo, do = om.forward(x, mode=oracle.MODE_GGML, dbg=True)
-        for name in ("x_in", "t_emb", "clip_pp", "text_pp", "clip_fc", "text_fc", "gcmlp", "global_c", "extended_c",
-                     "text_xn", "a0_q", "a0_k", "a0_v", "a0_out", "jb0_lat", "jb0_clip", "jb0_text", "after_joint",
-                     "after_fused", "flow_cl"):
-            g = dg[name].reshape(2, -1)[b]
-            o = do[name]
-            if name in ("text_xn", "a0_out"):     # stored bf16 on the GPU (the GEMM operand precision)
-                o = bf16_round(o)
-            tol = 2e-3 if name in ("after_joint", "after_fused", "jb0_lat", "jb0_clip", "jb0_text") else 1e-3
-            if name == "flow_cl":
-                tol = 2e-3
-            assert oracle.rel_l2(g, o) < tol, (b, name, oracle.rel_l2(g, o))
-        assert oracle.rel_l2(flow[b], fo) < 2e-3
+        check_stages(dg, b, 2, x, hp, W, om)
+        assert oracle.rel_l2(flow[b], om.forward(x, mode=oracle.MODE_GGML)) < 5e-3
 
 
-@pytest.mark.parametrize("wtype,tol", [("f32", 2e-3), ("q8_0", 1e-2)])
+@pytest.mark.parametrize("wtype,tol", [("f32", 1e-2), ("q8_0", 1e-2)])
 def test_forward_weight_types(wtype, tol):
+    """F32 projection weights run as bf16 on the tensor cores (activations bf16, f32 accumulate);
+    Q8_0 weights are dequantised exactly (q * fp16 scale) before the bf16 tensor-core path."""
     hp = synth.DitHParams(**SMALL)
     W = synth.make_weights(hp, seed=99, wtype=wtype)
     items = synth.make_inputs(hp, seed=5, batch=1, **SHAPE)
@@ -90,8 +116,11 @@ def test_sampler_matches_oracle(small_bf16):
     x = synth.make_inputs(hp, seed=4242, batch=1, **SHAPE)[0]
     lat, f0 = m.sample([x], steps=3, cfg=5.0, want_flow0=True)
     lo, fo = om.sample(x, steps=3, cfg=5.0, mode=oracle.MODE_GGML, want_flow0=True)
-    assert oracle.rel_l2(f0[0], fo) < 5e-3
-    assert oracle.rel_l2(lat[0], lo) < 5e-3
+    le, fe = om.sample(x, steps=3, cfg=5.0, mode=oracle.MODE_EXACT, want_flow0=True)
+    # CFG 5 amplifies the cond/uncond rounding noise five-fold in the velocity
+    assert oracle.rel_l2(f0[0], fo) < 1.5e-2 and oracle.rel_l2(lat[0], lo) < 1e-2
+    assert oracle.rel_l2(f0[0], fe) <= 1.2 * oracle.rel_l2(fo, fe) + 2e-3
+    assert oracle.rel_l2(lat[0], le) <= 1.2 * oracle.rel_l2(lo, le) + 2e-3
 
 
 def test_sampler_batched_prompts(small_bf16):
@@ -118,6 +147,46 @@ def test_reference_model_width_h1024(tmp_path):
     W = synth.make_weights(hp, seed=2, wtype="bf16")
     items = synth.make_inputs(hp, seed=3, batch=1, T=44, clip_S=16, sync_S=48, text_S=77, t5_S=77)
     m = tsd.DitModel.from_weights(hp, W)
-    flow = m.forward(items)
-    ref = oracle.OracleModel(hp, W).forward(items[0], mode=oracle.MODE_GGML)
-    assert oracle.rel_l2(flow[0], ref) < 2e-3
+    flow, dg = m.forward(items, dbg=True)
+    check_stages(dg, 0, 1, items[0], hp, W, oracle.OracleModel(hp, W))
+
+
+def test_cfg1_joint_layer_shapes_h1536():
+    """BASELINE config 1 shapes (H=1536, 24x64 heads, T=194, clip 72, text 77+128, joint S=471)
+    through a model with one full joint block, per-stage against the oracle."""
+    hp = synth.DitHParams(hidden=1536, n_head=24, depth=3, fused_depth=1)
+    W = synth.make_weights(hp, seed=1234, wtype="bf16")
+    items = synth.make_inputs(hp, seed=4242, batch=2, T=194, clip_S=72, sync_S=216, text_S=77, t5_S=128)
+    m = tsd.DitModel.from_weights(hp, W)
+    flow, dg = m.forward(items, dbg=True)
+    rep = check_stages(dg, 0, 2, items[0], hp, W, oracle.OracleModel(hp, W))
+    print({k: f"{e:.2e}/{f:.2e}" for k, (e, f) in rep.items()})
+    m.close()
+
+
+def test_ts_dit_shim_drop_in(tmp_path, small_bf16):
+    """include/ts_dit.hpp (the mmdit.h drop-in) gives the same flow and latent as the C-ABI."""
+    import subprocess
+    from test_capi import build_shim_demo
+    hp, W, m, _ = small_bf16
+    path = str(tmp_path / "dit.gguf")
+    synth.write_gguf(path, hp, W)
+    exe = build_shim_demo(tmp_path)
+    T, cS, yS, steps = 20, 8, 24, 2
+    out = str(tmp_path / "out.bin")
+    r = subprocess.run([exe, path, str(T), str(cS), str(yS), str(steps), out], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    for name in ("x_in", "a0_q", "a0_out", "after_joint", "after_fused", "flow_cl"):
+        assert name in r.stdout
+    data = np.fromfile(out, np.float32)
+    flow_c, lat_c = data[:T * 64].reshape(T, 64), data[T * 64:].reshape(64, T)
+    f32 = lambda a: np.asarray(a, np.float64).astype(np.float32)
+    noise = f32(np.sin(0.37 * np.arange(64 * T))).reshape(64, T)
+    text = f32(np.cos(0.11 * np.arange(77 * 1024))).reshape(77, 1024)
+    t5 = f32(np.sin(0.05 * np.arange(77 * 2048) + 1.0)).reshape(77, 2048)
+    gt = f32(np.cos(0.7 * np.arange(1024)))
+    clip = np.tile(W["empty_clip_feat"].dequant().reshape(1, 1024), (cS, 1))
+    sync = np.tile(W["empty_sync_feat"].dequant().reshape(1, 768), (yS, 1))
+    item = synth.DitInputs(noise, clip, sync, text, t5, gt, 1.0)
+    assert oracle.rel_l2(flow_c, m.forward([item])[0]) < 1e-5
+    assert oracle.rel_l2(lat_c, m.sample([item], steps=steps, cfg=5.0)[0]) < 1e-5

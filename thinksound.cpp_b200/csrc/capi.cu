@@ -249,6 +249,11 @@ int tsd_forward_profile(tsd_model * h, int B, const float * latent, int64_t T, c
     return check_device(m, st);
 }
 
+const char * tsd_plan_op_label(tsd_model * h, int i) {
+    if (!h || !h->m->plan || i < 0 || i >= (int)h->m->plan->ops.size()) return nullptr;
+    return h->m->plan->ops[i].label.c_str();
+}
+
 int tsd_sync_check(tsd_model * h, void * stream) {
     if (!h) return TSD_ERR_ARG;
     TSD_CUDA_TRY(cudaSetDevice(h->m->device));

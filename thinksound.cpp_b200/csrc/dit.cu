@@ -23,6 +23,7 @@ struct Builder {
     Model & m;
     Plan & P;
     int rc = TSD_OK;
+    std::string tag = "pre";   // label prefix of the ops being added
 
     template <class T> T * alloc(size_t n) {
         void * p = nullptr;
@@ -38,6 +39,7 @@ struct Builder {
         Op o;
         o.fn = std::move(fn);
         o.kind = kind; o.flops = flops; o.bytes = bytes; o.launches = launches;
+        o.label = tag + (kind == OP_GEMM ? " gemm" : kind == OP_GEMV ? " gemv" : kind == OP_ATTN ? " attn" : kind == OP_COPY ? " copy" : " elem");
         P.ops.push_back(std::move(o));
     }
     void snap(const char * name, const void * ptr, long long n, int kind = 0, int B = 0, int nh = 0, int S = 0) {
@@ -71,6 +73,10 @@ struct Builder {
         const double flops = 2.0 * p.m_valid * n_tok * kdim;
         const double bytes = 2.0 * M * kdim + 2.0 * n_tok * w.K_in + n_tok * (mode == EPI_GATE_RESID ? 12.0 : (out_bf16 ? 2.0 : 4.0)) * (numA == 2 ? M / 2 : p.m_valid);
         op([L](cudaStream_t st) { return gemm_launch(L, st); }, OP_GEMM, flops, bytes);
+        char buf[160];
+        snprintf(buf, sizeof buf, " M=%d N=%d K=%d taps=%d BN=%d grid=%ux%ux%u mode=%d", p.m_valid, nbatch * S,
+                 w.taps * w.K_in, w.taps, p.BN, L.grid.x, L.grid.y, L.grid.z, mode);
+        P.ops.back().label += buf;
     }
     // Few-token GEMV over B items (chunks of 8 tokens).
     void gemv(const VW & w, const float * x, long long ldx, int N, int act, float * y, long long ldy, int y_bf16 = 0) {
@@ -141,42 +147,55 @@ struct Builder {
         auto * ao = alloc<__nv_bfloat16>((size_t)B * Sj * H);
         if (rc) return;
         int * err = m.d_err;
+        // Values the op closures need, copied out of the plan and model: the closures outlive
+        // this builder, so they must not reach P or m through the builder's `this`.
+        float * const lat_in = P.lat_in, * const t_in = P.t_in, * const clip_in = P.clip_in;
+        float * const sync_in = P.sync_in, * const text_in = P.text_in, * const t5_in = P.t5_in;
+        const int clip_dim = m.clip_dim, sync_dim = m.sync_dim, text_dim = m.text_dim, t5_dim = m.t5_dim;
+        const float * const sync_pe = m.sync_pe;
+        const int text_S = sh.text_S, t5_S = sh.t5_S;
         const float theta = m.hp.rope_theta;
 
         op([err](cudaStream_t st) { return cudaMemsetAsync(err, 0, sizeof(int), st); }, OP_COPY, 0, 0, 0);
 
         // ---- audio_input_proj (mmdit.cpp:150-155) ----
-        op([=](cudaStream_t st) { return latent_to_tokens(P.lat_in, B, L, T, lat_tok, st); });
+        tag = "pre.audio";
+        op([=](cudaStream_t st) { return latent_to_tokens(lat_in, B, L, T, lat_tok, st); });
         gemm(m.ap0, lat_tok, B, T, L, (long long)T * L, EPI_STORE, ACT_SILU, a1, 1, H);
         gemm(m.ap13, a1, B, T, H, (long long)T * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 2);
         gemm(m.ap2, hbuf, B, T, F, (long long)T * F, EPI_STORE, ACT_NONE, x_lat, 0, H);
         snap("x_in", x_lat, (long long)B * T * H);
         // ---- t_embed (mmdit.cpp:157-161, 305-313) ----
+        tag = "pre.temb";
         const float maxp = m.hp.t_max_period;
-        op([=](cudaStream_t st) { return timestep_embed(P.t_in, B, H, maxp, temb, st); });
+        op([=](cudaStream_t st) { return timestep_embed(t_in, B, H, maxp, temb, st); });
         gemv(m.te0, temb, H, B, ACT_SILU, te1, H);
         gemv(m.te2, te1, H, B, ACT_NONE, te, H);
         snap("t_emb", te, (long long)B * H);
         // ---- clip (mmdit.cpp:164-167) ----
-        op([=](cudaStream_t st) { return cast_f32_bf16(P.clip_in, (long long)B * cS * m.clip_dim, clip_tok, st); });
+        tag = "pre.clip";
+        op([=](cudaStream_t st) { return cast_f32_bf16(clip_in, (long long)B * cS * clip_dim, clip_tok, st); });
         gemm(m.cp0, clip_tok, B, cS, m.clip_dim, (long long)cS * m.clip_dim, EPI_STORE, ACT_SILU, a1, 1, H);
         gemm(m.cp13, a1, B, cS, H, (long long)cS * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 2);
         gemm(m.cp2, hbuf, B, cS, F, (long long)cS * F, EPI_STORE, ACT_NONE, x_clip, 0, H);
         snap("clip_pp", x_clip, (long long)B * cS * H);
         // ---- sync (mmdit.cpp:168-177) ----
-        op([=](cudaStream_t st) { return sync_prep(P.sync_in, B, yS, m.sync_dim, m.sync_pe, sync_tok, st); });
+        tag = "pre.sync";
+        op([=](cudaStream_t st) { return sync_prep(sync_in, B, yS, sync_dim, sync_pe, sync_tok, st); });
         gemm(m.sp0, sync_tok, B, yS, m.sync_dim, (long long)yS * m.sync_dim, EPI_STORE, ACT_SILU, a1, 1, H);
         gemm(m.sp13, a1, B, yS, H, (long long)yS * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 2);
         gemm(m.sp2, hbuf, B, yS, F, (long long)yS * F, EPI_STORE, ACT_NONE, sync_out, 0, H);
         // ---- text (mmdit.cpp:178-183) ----
+        tag = "pre.text";
         op([=](cudaStream_t st) {
-            return text_prep(P.text_in, sh.text_S, m.text_dim, P.t5_in, sh.t5_S, m.t5_dim, B, text_tok, st);
+            return text_prep(text_in, text_S, text_dim, t5_in, t5_S, t5_dim, B, text_tok, st);
         });
         gemm(m.tp0, text_tok, B, St, m.t5_dim, (long long)St * m.t5_dim, EPI_STORE, ACT_SILU, a1, 1, H);
         gemm(m.tp13, a1, B, St, H, (long long)St * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 2);
         gemm(m.tp2, hbuf, B, St, F, (long long)St * F, EPI_STORE, ACT_NONE, x_text, 0, H);
         snap("text_pp", x_text, (long long)B * St * H);
         // ---- conditioning vectors (mmdit.cpp:184-200) ----
+        tag = "pre.cond";
         gemv(m.tcp, P.gtext_in, m.text_dim, B, ACT_NONE, text_fc, H);
         snap("text_fc", text_fc, (long long)B * H);
         op([=](cudaStream_t st) { return seq_mean(x_clip, B, cS, H, cmean, st); });
@@ -191,6 +210,7 @@ struct Builder {
         op([=](cudaStream_t st) { return build_extended(sync_out, yS, gc, B, T, H, ext, sext, sgc, st); });
         snap("extended_c", ext, (long long)B * T * H);
         // ---- every per-token adaLN of the step in one GEMM (mmdit.cpp:209, 285) ----
+        tag = "adaln";
         gemm(m.ada_lat, sext, B, T, H, (long long)T * H, EPI_STORE, ACT_NONE, mod_lat, 0, R);
 
         // ---- joint blocks (mmdit.cpp:237-272) ----
@@ -209,6 +229,7 @@ struct Builder {
             for (int s = 0; s < 3; ++s) {
                 const StreamW & w = blk[s];
                 const int S = Ss[s];
+                tag = "j" + std::to_string(i) + (s == 0 ? ".lat" : s == 1 ? ".clip" : ".text");
                 const float * mod;
                 long long ld;
                 if (s == 0) { mod = mod_lat + w.ada_off; ld = R; }
@@ -232,6 +253,7 @@ struct Builder {
                 snap("a0_k", Kb, (long long)B * Sj * H, 2, B, nh, Sj);
                 snap("a0_v", Vb, (long long)B * Sj * H, 2, B, nh, Sj);
             }
+            tag = "j" + std::to_string(i);
             op([AJ](cudaStream_t st) { return attn_launch(AJ, st); }, OP_ATTN, 4.0 * B * nh * 64.0 * Sj * Sj,
                6.0 * B * nh * 64.0 * Sj + 2.0 * B * Sj * H);
             if (i == 0) snap("a0_out", ao, (long long)B * Sj * H, 1);
@@ -239,6 +261,7 @@ struct Builder {
                 const StreamW & w = blk[s];
                 if (w.pre_only) continue;
                 const int S = Ss[s];
+                tag = "j" + std::to_string(i) + (s == 0 ? ".lat" : s == 1 ? ".clip" : ".text");
                 const float * mod = (s == 0) ? mod_lat + w.ada_off : modc[s];
                 const long long ld = (s == 0) ? R : 6LL * H;
                 const int gdiv = (s == 0) ? 1 : S;
@@ -257,7 +280,9 @@ struct Builder {
         }
         snap("after_joint", x_lat, (long long)B * T * H);
         // ---- fused blocks (mmdit.cpp:274-282) ----
+        int fi = 0;
         for (const StreamW & w : m.fused) {
+            tag = "f" + std::to_string(fi++);
             const float * mod = mod_lat + w.ada_off;
             const long long ld = R;
             op([=](cudaStream_t st) { return ln_modulate(x_lat, B * T, H, mod, mod + H, ld, 1, T, xn, st); });
@@ -273,6 +298,7 @@ struct Builder {
         }
         snap("after_fused", x_lat, (long long)B * T * H);
         // ---- final layer (mmdit.cpp:284-290) ----
+        tag = "final";
         const float * fmod = mod_lat + m.final_ada_off;
         op([=](cudaStream_t st) { return ln_modulate(x_lat, B * T, H, fmod, fmod + H, R, 1, T, xn, st); });
         gemm(m.fconv, xn, B, T, H, (long long)T * H, EPI_STORE, ACT_NONE, P.flow, 0, L);

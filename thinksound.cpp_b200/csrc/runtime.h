@@ -102,6 +102,7 @@ enum OpKind : int { OP_GEMM = 0, OP_GEMV = 1, OP_ATTN = 2, OP_ELEM = 3, OP_COPY 
 struct Op {
     std::function<cudaError_t(cudaStream_t)> fn;
     std::vector<Snap> snaps;
+    std::string label;        // e.g. "f3 gemm M=8192 N=388 K=4608 grid=32x4x1"
     int kind = OP_ELEM;
     int launches = 1;          // kernel launches the op issues
     double flops = 0, bytes = 0;   // algorithmic work of the op

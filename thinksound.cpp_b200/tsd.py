@@ -29,7 +29,7 @@ EXPORTS = [
     "tsd_model_get_hparams", "tsd_get_tensor_f32", "tsd_forward", "tsd_forward_batched",
     "tsd_forward_device", "tsd_sync_check", "tsd_sample", "tsd_sample_batched", "tsd_version",
     "tsd_device_count", "tsd_op_gemm", "tsd_op_gemv", "tsd_op_attention", "tsd_op_ln_modulate",
-    "tsd_op_qk_norm_rope", "tsd_forward_profile",
+    "tsd_op_qk_norm_rope", "tsd_forward_profile", "tsd_plan_op_label",
 ]
 
 
@@ -89,6 +89,8 @@ def lib() -> ctypes.CDLL:
         fn = getattr(L, name)
         fn.argtypes = args
         fn.restype = ctypes.c_int
+    L.tsd_plan_op_label.argtypes = [vp, i32]
+    L.tsd_plan_op_label.restype = ctypes.c_char_p
     L.tsd_model_free.restype = None
     L.tsd_version.restype = ctypes.c_char_p
     _lib = L
@@ -167,7 +169,10 @@ class DitModel:
         n = int(np.prod(list(ne)))
         out = np.empty(n, np.float32)
         check("tsd_get_tensor_f32", lib().tsd_get_tensor_f32(self.h, name.encode(), _fp(out), n, ne))
-        return out.reshape(tuple(reversed([int(v) for v in ne])))
+        dims = [int(v) for v in ne]
+        while len(dims) > 1 and dims[-1] == 1:      # ggml pads unused trailing dims with 1
+            dims.pop()
+        return out.reshape(tuple(reversed(dims)))
 
     def forward(self, items: Sequence, dbg: bool = False):
         """Batched velocity evaluation of synth.DitInputs items -> flow [B][T][latent_dim]."""
@@ -211,8 +216,9 @@ class DitModel:
                                        nbytes)
         check("tsd_forward_profile", rc)
         k = min(n.value, max_ops)
+        labels = [(lib().tsd_plan_op_label(self.h, i) or b"").decode() for i in range(k)]
         return dict(kind=np.array(kind[:k]), launches=np.array(launches[:k]), ms=np.array(ms[:k]),
-                    flops=np.array(flops[:k]), bytes=np.array(nbytes[:k]))
+                    flops=np.array(flops[:k]), bytes=np.array(nbytes[:k]), labels=labels)
 
     def sync_check(self, stream: int = 0) -> None:
         check("tsd_sync_check", lib().tsd_sync_check(self.h, ctypes.c_void_p(stream)))
