@@ -37,11 +37,15 @@ extern "C" {
  * W bf16 [M][taps*K_in]; X bf16 rows with the given row / batch strides (elements);
  * out row index b*S + t. M multiple of 128 (256 for SWIGLU), K_in multiple of 64.
  * GATE_RESID reads gate row (out row / gate_div): 1 for a per-token gate, S for one per item.
- * max_splits > 1 allows split-K (GATE_RESID only: partial sums are added atomically). */
+ * Split-K (max_splits > 1) needs scratch from the caller: `ws` (ws_floats floats) for partial
+ * tiles and `counters` (n_counters ints, zero before the first call; the kernel leaves them
+ * zero). Partials are summed in a fixed order, so results do not depend on timing. With
+ * ws == NULL the GEMM runs without splitting K. */
 TSD_API int tsd_op_gemm(const void * W, int M, int K_in, int taps, int pad, const void * X, int nbatch, int S,
                 int64_t x_row_stride, int64_t x_batch_stride, int mode, int act, const float * bias, int m_valid,
                 void * out, int out_bf16, int64_t ldo, float * resid, int64_t ldr, const float * gate, int64_t ldg,
-                int gate_div, int max_splits, int * err, void * stream);
+                int gate_div, int max_splits, float * ws, int64_t ws_floats, int * counters, int n_counters,
+                int * err, void * stream);
 
 /* Few-token GEMV with weights in their stored ggml type (0 F32, 30 BF16, 8 Q8_0), N <= 8
  * (the [H,1]-column mul_mats of mmdit.cpp:158-160,185-192,209). W2 != NULL: SwiGLU pair. */

@@ -103,12 +103,16 @@ def test_forward_from_gguf_equals_from_weights(tmp_path, small_bf16):
 
 
 def test_batched_equals_single(small_bf16):
+    """Batch items are independent; a different batch size may tile the GEMMs (and order the
+    f32 sums) differently, so agreement is at the bf16 rounding-noise level, while repeating
+    the same call is bit-exact."""
     hp, W, m, _ = small_bf16
     items = synth.make_inputs(hp, seed=31, batch=3, **SHAPE)
     fb = m.forward(items)
+    assert np.array_equal(fb, m.forward(items))
     for b in range(3):
         fs = m.forward([items[b]])
-        assert oracle.rel_l2(fb[b], fs[0]) < 1e-5
+        assert oracle.rel_l2(fb[b], fs[0]) < 3e-3
 
 
 def test_sampler_matches_oracle(small_bf16):
@@ -127,9 +131,10 @@ def test_sampler_batched_prompts(small_bf16):
     hp, W, m, _ = small_bf16
     items = synth.make_inputs(hp, seed=8, batch=3, **SHAPE)
     lat = m.sample(items, steps=2, cfg=5.0)
+    assert np.array_equal(lat, m.sample(items, steps=2, cfg=5.0))
     for p in range(3):
         single = m.sample([items[p]], steps=2, cfg=5.0)
-        assert oracle.rel_l2(lat[p], single[0]) < 1e-5
+        assert oracle.rel_l2(lat[p], single[0]) < 1e-2
 
 
 def test_bad_shapes_are_rejected(small_bf16):

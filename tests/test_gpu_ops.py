@@ -51,6 +51,8 @@ def _seed():
     (128, 192, 7, 3, 2, 40),      # conv k7 (sync input proj / final conv)
     (128, 128, 1, 0, 1, 1),       # single token
     (512, 1536, 1, 0, 1, 388),    # QKV-like K
+    (4096, 256, 1, 0, 1, 2000),   # > one tile per persistent CTA (TMEM double buffer cycles)
+    (1024, 128, 3, 1, 4, 500),    # conv, many tiles per CTA, ragged last tile per item
 ])
 def test_gemm_store(M, K, taps, pad, nb, S):
     W = rnd(M, taps * K, scale=0.05)
@@ -76,14 +78,14 @@ def test_gemm_store_bf16_silu_and_m_valid():
     assert rel(out.float(), ref.to(torch.bfloat16).float()) < 1e-3
 
 
-@pytest.mark.parametrize("taps", [1, 3])
-def test_gemm_swiglu(taps):
-    F, K, S = 256, 128, 100
+@pytest.mark.parametrize("taps,F,S", [(1, 256, 100), (3, 256, 100), (3, 2048, 700)])
+def test_gemm_swiglu(taps, F, S):
+    K = 128
     W1, W3 = rnd(F, taps * K, scale=0.05), rnd(F, taps * K, scale=0.05)
     W13 = torch.empty(2 * F, taps * K, device=DEV, dtype=torch.bfloat16)
-    for b in range(F // 128):
-        W13[256 * b:256 * b + 128] = W1[128 * b:128 * b + 128]
-        W13[256 * b + 128:256 * b + 256] = W3[128 * b:128 * b + 128]
+    for b in range(F // 64):                     # 64-row interleave: w1 block, matching w3 block
+        W13[128 * b:128 * b + 64] = W1[64 * b:64 * b + 64]
+        W13[128 * b + 64:128 * b + 128] = W3[64 * b:64 * b + 64]
     X = rnd(2, S, K)
     out = torch.empty(2, S, F, device=DEV, dtype=torch.bfloat16)
     tsd.op_gemm(W13, 2 * F, K, taps, taps // 2, X, 2, S, K, S * K, tsd.EPI_SWIGLU, 0, None, out, 1, F)
@@ -92,21 +94,59 @@ def test_gemm_swiglu(taps):
     assert rel(out.float(), ref) < 4e-3
 
 
-@pytest.mark.parametrize("per_token,splits,taps", [(1, 1, 3), (1, 4, 3), (0, 1, 1), (0, 4, 1)])
-def test_gemm_gate_residual(per_token, splits, taps):
-    M, K, S, nb = 256, 512, 72, 2
+@pytest.mark.parametrize("per_token,splits,taps,M,S", [(1, 1, 3, 256, 72), (1, 4, 3, 256, 72), (0, 1, 1, 256, 72),
+                                                        (0, 4, 1, 256, 72), (1, 8, 3, 1536, 600)])
+def test_gemm_gate_residual(per_token, splits, taps, M, S):
+    K, nb = 512, 2
     W = rnd(M, taps * K, scale=0.03)
     X = rnd(nb, S, K)
     bias = torch.randn(M, device=DEV)
     gate = torch.randn(nb * S if per_token else nb, M, device=DEV)
     x0 = torch.randn(nb, S, M, device=DEV)
-    x = x0.clone()
-    tsd.op_gemm(W, M, K, taps, taps // 2, X, nb, S, K, S * K, tsd.EPI_GATE_RESID, 0, bias, None, 0, 0,
-                resid=x, ldr=M, gate=gate, ldg=M, gate_div=1 if per_token else S, max_splits=splits)
+    ws = torch.empty(8 << 20, device=DEV) if splits > 1 else None
+    counters = torch.zeros(1 << 16, device=DEV, dtype=torch.int32) if splits > 1 else None
+    outs = []
+    for _ in range(2):
+        x = x0.clone()
+        tsd.op_gemm(W, M, K, taps, taps // 2, X, nb, S, K, S * K, tsd.EPI_GATE_RESID, 0, bias, None, 0, 0,
+                    resid=x, ldr=M, gate=gate, ldg=M, gate_div=1 if per_token else S, max_splits=splits,
+                    ws=ws, counters=counters)
+        outs.append(x)
     torch.cuda.synchronize()
     g = gate.view(nb, S, M) if per_token else gate.view(nb, 1, M)
     ref = x0 + g * (ref_gemm(W, X, taps, taps // 2) + bias)
-    assert rel(x, ref) < 1e-5
+    assert rel(outs[0], ref) < 1e-5
+    assert torch.equal(outs[0], outs[1])          # split-K partials are summed in a fixed order
+    if counters is not None:
+        assert int(counters.abs().sum()) == 0     # the kernel leaves its arrival counters zero
+
+
+@pytest.mark.parametrize("mode", [tsd.EPI_STORE, tsd.EPI_SWIGLU])
+def test_gemm_split_k_store_and_swiglu(mode):
+    """Long-K, few-token GEMMs split K across CTAs; the last CTA of a tile reduces and runs the epilogue."""
+    M, K, nb, S, taps = 512, 1536, 2, 40, 3
+    W = rnd(M, taps * K, scale=0.02)
+    X = rnd(nb, S, K)
+    bias = torch.randn(M, device=DEV)
+    ws = torch.empty(8 << 20, device=DEV)
+    counters = torch.zeros(1 << 16, device=DEV, dtype=torch.int32)
+    Fo = M // 2 if mode == tsd.EPI_SWIGLU else M
+    outs = []
+    for _ in range(2):
+        out = torch.empty(nb, S, Fo, device=DEV)
+        tsd.op_gemm(W, M, K, taps, 1, X, nb, S, K, S * K, mode, 0, bias if mode == tsd.EPI_STORE else None, out, 0, Fo,
+                    max_splits=8, ws=ws, counters=counters)
+        outs.append(out)
+    torch.cuda.synchronize()
+    acc = ref_gemm(W, X, taps, 1)
+    if mode == tsd.EPI_STORE:
+        ref = acc + bias
+    else:
+        Wv = acc.view(nb, S, M // 128, 2, 64)
+        ref = (torch.nn.functional.silu(Wv[:, :, :, 0]) * Wv[:, :, :, 1]).reshape(nb, S, Fo)
+    assert rel(outs[0], ref) < 1e-5
+    assert torch.equal(outs[0], outs[1])
+    assert int(counters.abs().sum()) == 0
 
 
 def test_gemm_strided_slice_of_joint_buffer():

@@ -41,6 +41,7 @@ struct AttnArgs {
 __global__ void __launch_bounds__(192, 1)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
+    pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t * bars = reinterpret_cast<uint64_t *>(smem + kOffBar);

@@ -28,6 +28,8 @@ int check_device(Model & m, cudaStream_t st) {
     if (e) {
         fprintf(stderr, "tsd: device error word %d (a bounded wait expired)\n", e);
         cudaMemset(m.d_err, 0, sizeof(int));
+        // an interrupted split-K GEMM may have left arrival counts behind
+        if (m.plan && m.plan->counters) cudaMemset(m.plan->counters, 0, sizeof(int) * m.plan->n_counters);
         return TSD_ERR_DEVICE;
     }
     return TSD_OK;
@@ -353,24 +355,26 @@ int tsd_sample(tsd_model * h, const float * noise, int64_t T, const float * clip
 int tsd_op_gemm(const void * W, int M, int K_in, int taps, int pad, const void * X, int nbatch, int S,
                 int64_t x_row_stride, int64_t x_batch_stride, int mode, int act, const float * bias, int m_valid,
                 void * out, int out_bf16, int64_t ldo, float * resid, int64_t ldr, const float * gate, int64_t ldg,
-                int gate_div, int max_splits, int * err, void * stream) {
+                int gate_div, int max_splits, float * ws, int64_t ws_floats, int * counters, int n_counters,
+                int * err, void * stream) {
     if (!W || !X || mode < 0 || mode > 2 || (mode == EPI_GATE_RESID && (!resid || !gate || gate_div < 1)) ||
-        (mode != EPI_GATE_RESID && !out))
+        (mode != EPI_GATE_RESID && !out) || (ws && !counters))
         return TSD_ERR_ARG;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     GemmLaunch L;
-    const int numA = mode == EPI_SWIGLU ? 2 : 1;
-    if (!gemm_plan(L, W, M, K_in, taps, pad, numA, X, nbatch, S, x_row_stride, x_batch_stride, sms,
-                   mode == EPI_GATE_RESID ? max_splits : 1))
+    const int swiglu = mode == EPI_SWIGLU;
+    if (!gemm_plan(L, W, M, K_in, taps, pad, swiglu, X, nbatch, S, x_row_stride, x_batch_stride, sms,
+                   ws ? max_splits : 1, ws ? ws_floats : 0, ws ? n_counters : 0))
         return TSD_ERR_ARG;
     GemmParams & p = L.p;
     p.mode = mode; p.act = act;
-    p.m_valid = m_valid > 0 ? m_valid : M;
+    p.m_valid = m_valid > 0 ? m_valid : (swiglu ? M / 2 : M);
     p.bias = bias;
     p.out = out; p.out_bf16 = out_bf16; p.ldo = ldo;
     p.resid = resid; p.ldr = ldr; p.gate = gate; p.ldg = ldg; p.gate_div = gate_div > 0 ? gate_div : 1;
+    p.ws = ws; p.counters = counters;
     p.err = err;
     TSD_CUDA_TRY(gemm_launch(L, (cudaStream_t)stream));
     return TSD_OK;

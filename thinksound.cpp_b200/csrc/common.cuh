@@ -183,6 +183,13 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// ---- programmatic dependent launch ----
+// Wait until the grids this one depends on have completed and their writes are visible
+// (no-op when the kernel was launched without the programmatic-serialization attribute).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the next kernel in the stream to start launching (its pdl_wait still waits for us).
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 // ---- numerics ----
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 // 2^x on the SFU (ex2.approx); used for the softmax exponent.

@@ -24,6 +24,11 @@ struct Builder {
     Plan & P;
     int rc = TSD_OK;
     std::string tag = "pre";   // label prefix of the ops being added
+    // Split-K scratch shared by all GEMMs of the plan (they run one after another).
+    static constexpr long long kWsFloats = 8ll << 20;   // 32 MB of partial tiles
+    static constexpr int kCounters = 1 << 16;
+    float * ws = nullptr;
+    int * counters = nullptr;
 
     template <class T> T * alloc(size_t n) {
         void * p = nullptr;
@@ -49,29 +54,31 @@ struct Builder {
     // GEMM over activations X [nbatch][S][K_in] (row stride xrs, batch stride xbs, elements).
     void gemm(const GW & w, const void * X, int nbatch, int S, long long xrs, long long xbs, int mode, int act,
               void * out, int out_bf16, long long ldo, float * resid = nullptr, long long ldr = 0,
-              const float * gate = nullptr, long long ldg = 0, int gate_div = 1, int numA = 1, int max_splits = 1,
-              long long row_off = 0, int M_override = 0) {
+              const float * gate = nullptr, long long ldg = 0, int gate_div = 1, int swiglu = 0, int max_splits = 8,
+              int out_cblk = 0, long long out_cstride = 0) {
         if (rc) return;
         // Linear layers over a contiguous batch run as one long token sequence.
         if (w.taps == 1 && xbs == (long long)S * xrs && nbatch > 1) { S *= nbatch; nbatch = 1; }
         GemmLaunch L;
-        const int M = M_override ? M_override : w.M;
-        if (!gemm_plan(L, w.w + row_off * (long long)w.K_in * w.taps, M, w.K_in, w.taps, w.pad, numA, X, nbatch, S, xrs, xbs,
-                       m.num_sms, max_splits)) {
+        const int M = w.M;
+        if (!gemm_plan(L, w.w, M, w.K_in, w.taps, w.pad, swiglu, X, nbatch, S, xrs, xbs, m.num_sms, max_splits,
+                       kWsFloats, kCounters)) {
             fprintf(stderr, "tsd: gemm plan failed (M %d K %d taps %d S %d)\n", M, w.K_in, w.taps, S);
             rc = TSD_ERR_ARG;
             return;
         }
         GemmParams & p = L.p;
         p.mode = mode; p.act = act;
-        p.m_valid = M_override ? M : w.m_valid;
-        p.bias = w.bias ? w.bias + row_off : nullptr;
+        p.m_valid = swiglu ? w.M / 2 : w.m_valid;
+        p.bias = w.bias;
         p.out = out; p.out_bf16 = out_bf16; p.ldo = ldo;
+        p.out_cblk = out_cblk; p.out_cstride = out_cstride;
         p.resid = resid; p.ldr = ldr; p.gate = gate; p.ldg = ldg; p.gate_div = gate_div;
+        p.ws = ws; p.counters = counters;
         p.err = m.d_err;
         const double n_tok = (double)nbatch * S, kdim = (double)w.taps * w.K_in;
-        const double flops = 2.0 * p.m_valid * n_tok * kdim;
-        const double bytes = 2.0 * M * kdim + 2.0 * n_tok * w.K_in + n_tok * (mode == EPI_GATE_RESID ? 12.0 : (out_bf16 ? 2.0 : 4.0)) * (numA == 2 ? M / 2 : p.m_valid);
+        const double flops = 2.0 * (swiglu ? 2 * p.m_valid : p.m_valid) * n_tok * kdim;
+        const double bytes = 2.0 * M * kdim + 2.0 * n_tok * w.K_in + n_tok * (mode == EPI_GATE_RESID ? 12.0 : (out_bf16 ? 2.0 : 4.0)) * p.m_valid;
         op([L](cudaStream_t st) { return gemm_launch(L, st); }, OP_GEMM, flops, bytes);
         char buf[160];
         snprintf(buf, sizeof buf, " M=%d N=%d K=%d taps=%d BN=%d grid=%ux%ux%u mode=%d", p.m_valid, nbatch * S,
@@ -145,8 +152,17 @@ struct Builder {
         auto * Kb = alloc<__half>((size_t)B * nh * Sj * 64);
         auto * Vb = alloc<__half>((size_t)B * nh * Sj * 64);
         auto * ao = alloc<__nv_bfloat16>((size_t)B * Sj * H);
+        ws = alloc<float>((size_t)kWsFloats);
+        counters = alloc<int>((size_t)kCounters);
         if (rc) return;
+        if (cudaMemset(counters, 0, sizeof(int) * kCounters) != cudaSuccess) { rc = TSD_ERR_CUDA; return; }
+        P.counters = counters;
+        P.n_counters = kCounters;
         int * err = m.d_err;
+        // Per-token adaLN output is column-blocked: chunk k of the stacked weight rows is one
+        // contiguous [B*T][H] plane at mod_lat + k * BTH (row stride H), so each block's
+        // shift / scale / gate rows are dense and page-local.
+        const long long BTH = (long long)B * T * H;
         // Values the op closures need, copied out of the plan and model: the closures outlive
         // this builder, so they must not reach P or m through the builder's `this`.
         float * const lat_in = P.lat_in, * const t_in = P.t_in, * const clip_in = P.clip_in;
@@ -162,7 +178,7 @@ struct Builder {
         tag = "pre.audio";
         op([=](cudaStream_t st) { return latent_to_tokens(lat_in, B, L, T, lat_tok, st); });
         gemm(m.ap0, lat_tok, B, T, L, (long long)T * L, EPI_STORE, ACT_SILU, a1, 1, H);
-        gemm(m.ap13, a1, B, T, H, (long long)T * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 2);
+        gemm(m.ap13, a1, B, T, H, (long long)T * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 1);
         gemm(m.ap2, hbuf, B, T, F, (long long)T * F, EPI_STORE, ACT_NONE, x_lat, 0, H);
         snap("x_in", x_lat, (long long)B * T * H);
         // ---- t_embed (mmdit.cpp:157-161, 305-313) ----
@@ -176,14 +192,14 @@ struct Builder {
         tag = "pre.clip";
         op([=](cudaStream_t st) { return cast_f32_bf16(clip_in, (long long)B * cS * clip_dim, clip_tok, st); });
         gemm(m.cp0, clip_tok, B, cS, m.clip_dim, (long long)cS * m.clip_dim, EPI_STORE, ACT_SILU, a1, 1, H);
-        gemm(m.cp13, a1, B, cS, H, (long long)cS * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 2);
+        gemm(m.cp13, a1, B, cS, H, (long long)cS * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 1);
         gemm(m.cp2, hbuf, B, cS, F, (long long)cS * F, EPI_STORE, ACT_NONE, x_clip, 0, H);
         snap("clip_pp", x_clip, (long long)B * cS * H);
         // ---- sync (mmdit.cpp:168-177) ----
         tag = "pre.sync";
         op([=](cudaStream_t st) { return sync_prep(sync_in, B, yS, sync_dim, sync_pe, sync_tok, st); });
         gemm(m.sp0, sync_tok, B, yS, m.sync_dim, (long long)yS * m.sync_dim, EPI_STORE, ACT_SILU, a1, 1, H);
-        gemm(m.sp13, a1, B, yS, H, (long long)yS * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 2);
+        gemm(m.sp13, a1, B, yS, H, (long long)yS * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 1);
         gemm(m.sp2, hbuf, B, yS, F, (long long)yS * F, EPI_STORE, ACT_NONE, sync_out, 0, H);
         // ---- text (mmdit.cpp:178-183) ----
         tag = "pre.text";
@@ -191,7 +207,7 @@ struct Builder {
             return text_prep(text_in, text_S, text_dim, t5_in, t5_S, t5_dim, B, text_tok, st);
         });
         gemm(m.tp0, text_tok, B, St, m.t5_dim, (long long)St * m.t5_dim, EPI_STORE, ACT_SILU, a1, 1, H);
-        gemm(m.tp13, a1, B, St, H, (long long)St * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 2);
+        gemm(m.tp13, a1, B, St, H, (long long)St * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 1);
         gemm(m.tp2, hbuf, B, St, F, (long long)St * F, EPI_STORE, ACT_NONE, x_text, 0, H);
         snap("text_pp", x_text, (long long)B * St * H);
         // ---- conditioning vectors (mmdit.cpp:184-200) ----
@@ -211,9 +227,14 @@ struct Builder {
         snap("extended_c", ext, (long long)B * T * H);
         // ---- every per-token adaLN of the step in one GEMM (mmdit.cpp:209, 285) ----
         tag = "adaln";
-        gemm(m.ada_lat, sext, B, T, H, (long long)T * H, EPI_STORE, ACT_NONE, mod_lat, 0, R);
+        gemm(m.ada_lat, sext, B, T, H, (long long)T * H, EPI_STORE, ACT_NONE, mod_lat, 0, H, nullptr, 0, nullptr, 0, 1, 0,
+             8, H, BTH);
+        (void)R;
 
         // ---- joint blocks (mmdit.cpp:237-272) ----
+        // A stream's adaLN chunk k (shift, scale, gate_msa, shift_mlp, scale_mlp, gate_mlp) is at
+        // mod + k * cs with row stride ld: latent rows per token (cs = BTH, ld = H), clip / text
+        // one row per item (cs = H, ld = 6H or 2H).
         const int n_joint = (int)m.joint.size();
         float * xs[3] = {x_lat, x_clip, x_text};
         const int Ss[3] = {T, cS, St};
@@ -226,19 +247,22 @@ struct Builder {
         }
         for (int i = 0; i < n_joint; ++i) {
             const auto & blk = m.joint[i];
+            const float * mods[3];
+            long long lds[3], css[3];
             for (int s = 0; s < 3; ++s) {
                 const StreamW & w = blk[s];
                 const int S = Ss[s];
                 tag = "j" + std::to_string(i) + (s == 0 ? ".lat" : s == 1 ? ".clip" : ".text");
-                const float * mod;
-                long long ld;
-                if (s == 0) { mod = mod_lat + w.ada_off; ld = R; }
+                if (s == 0) { mods[s] = mod_lat + (w.ada_off / H) * BTH; lds[s] = H; css[s] = BTH; }
                 else {
-                    ld = (long long)(w.pre_only ? 2 : 6) * H;
-                    gemv(w.ada, sgc, H, B, ACT_NONE, modc[s], ld);
-                    mod = modc[s];
+                    lds[s] = (long long)(w.pre_only ? 2 : 6) * H;
+                    css[s] = H;
+                    gemv(w.ada, sgc, H, B, ACT_NONE, modc[s], lds[s]);
+                    mods[s] = modc[s];
                 }
-                op([=](cudaStream_t st) { return ln_modulate(xs[s], B * S, H, mod, mod + H, ld, s == 0, S, xn, st); });
+                const float * mod = mods[s];
+                const long long ld = lds[s], cs = css[s];
+                op([=](cudaStream_t st) { return ln_modulate(xs[s], B * S, H, mod, mod + cs, ld, s == 0, S, xn, st); });
                 if (i == 0 && s == 2) snap("text_xn", xn, (long long)B * S * H, 1);
                 gemm(w.qkv, xn, B, S, H, (long long)S * H, EPI_STORE, ACT_NONE, qkv, 0, 3 * H);
                 const float fs = (s == 1) ? (float)T / (float)cS : 1.0f;
@@ -262,15 +286,15 @@ struct Builder {
                 if (w.pre_only) continue;
                 const int S = Ss[s];
                 tag = "j" + std::to_string(i) + (s == 0 ? ".lat" : s == 1 ? ".clip" : ".text");
-                const float * mod = (s == 0) ? mod_lat + w.ada_off : modc[s];
-                const long long ld = (s == 0) ? R : 6LL * H;
+                const float * mod = mods[s];
+                const long long ld = lds[s], cs = css[s];
                 const int gdiv = (s == 0) ? 1 : S;
                 gemm(w.l1, ao + (long long)soff[s] * H, B, S, H, (long long)Sj * H, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0,
-                     xs[s], H, mod + 2 * H, ld, gdiv, 1, 4);
-                op([=](cudaStream_t st) { return ln_modulate(xs[s], B * S, H, mod + 3 * H, mod + 4 * H, ld, s == 0, S, xn, st); });
-                gemm(w.w13, xn, B, S, H, (long long)S * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 2);
-                gemm(w.w2, hbuf, B, S, F, (long long)S * F, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, xs[s], H, mod + 5 * H,
-                     ld, gdiv, 1, 4);
+                     xs[s], H, mod + 2 * cs, ld, gdiv);
+                op([=](cudaStream_t st) { return ln_modulate(xs[s], B * S, H, mod + 3 * cs, mod + 4 * cs, ld, s == 0, S, xn, st); });
+                gemm(w.w13, xn, B, S, H, (long long)S * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 1);
+                gemm(w.w2, hbuf, B, S, F, (long long)S * F, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, xs[s], H, mod + 5 * cs,
+                     ld, gdiv);
             }
             if (i == 0) {
                 snap("jb0_lat", x_lat, (long long)B * T * H);
@@ -283,24 +307,24 @@ struct Builder {
         int fi = 0;
         for (const StreamW & w : m.fused) {
             tag = "f" + std::to_string(fi++);
-            const float * mod = mod_lat + w.ada_off;
-            const long long ld = R;
-            op([=](cudaStream_t st) { return ln_modulate(x_lat, B * T, H, mod, mod + H, ld, 1, T, xn, st); });
+            const float * mod = mod_lat + (w.ada_off / H) * BTH;
+            const long long ld = H, cs = BTH;
+            op([=](cudaStream_t st) { return ln_modulate(x_lat, B * T, H, mod, mod + cs, ld, 1, T, xn, st); });
             gemm(w.qkv, xn, B, T, H, (long long)T * H, EPI_STORE, ACT_NONE, qkv, 0, 3 * H);
             const StreamW wc = w;
             op([=](cudaStream_t st) { return qk_norm_rope(qkv, B, T, H, nh, wc.qg, wc.kg, 1, 1.0f, theta, Qb, Kb, Vb, T, 0, st); });
             op([AF](cudaStream_t st) { return attn_launch(AF, st); }, OP_ATTN, 4.0 * B * nh * 64.0 * T * T,
                6.0 * B * nh * 64.0 * T + 2.0 * B * T * H);
-            gemm(w.l1, ao, B, T, H, (long long)T * H, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, x_lat, H, mod + 2 * H, ld, 1, 1, 4);
-            op([=](cudaStream_t st) { return ln_modulate(x_lat, B * T, H, mod + 3 * H, mod + 4 * H, ld, 1, T, xn, st); });
-            gemm(w.w13, xn, B, T, H, (long long)T * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 2);
-            gemm(w.w2, hbuf, B, T, F, (long long)T * F, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, x_lat, H, mod + 5 * H, ld, 1, 1, 4);
+            gemm(w.l1, ao, B, T, H, (long long)T * H, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, x_lat, H, mod + 2 * cs, ld, 1);
+            op([=](cudaStream_t st) { return ln_modulate(x_lat, B * T, H, mod + 3 * cs, mod + 4 * cs, ld, 1, T, xn, st); });
+            gemm(w.w13, xn, B, T, H, (long long)T * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 1);
+            gemm(w.w2, hbuf, B, T, F, (long long)T * F, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, x_lat, H, mod + 5 * cs, ld, 1);
         }
         snap("after_fused", x_lat, (long long)B * T * H);
         // ---- final layer (mmdit.cpp:284-290) ----
         tag = "final";
-        const float * fmod = mod_lat + m.final_ada_off;
-        op([=](cudaStream_t st) { return ln_modulate(x_lat, B * T, H, fmod, fmod + H, R, 1, T, xn, st); });
+        const float * fmod = mod_lat + (m.final_ada_off / H) * BTH;
+        op([=](cudaStream_t st) { return ln_modulate(x_lat, B * T, H, fmod, fmod + BTH, H, 1, T, xn, st); });
         gemm(m.fconv, xn, B, T, H, (long long)T * H, EPI_STORE, ACT_NONE, P.flow, 0, L);
         snap("flow_cl", P.flow, (long long)B * T * L);
     }

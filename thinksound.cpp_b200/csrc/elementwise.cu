@@ -22,6 +22,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 __global__ void ln_modulate_kernel(const float * __restrict__ x, int rows, int H, const float * __restrict__ shift,
                                    const float * __restrict__ scale, long long ld_mod, int per_token, int rows_per_item,
                                    __nv_bfloat16 * __restrict__ y) {
+    pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -57,6 +58,7 @@ __global__ void qk_norm_rope_kernel(const float * __restrict__ qkv, int B, int S
                                     const float * __restrict__ qg, const float * __restrict__ kg, int rope, float fscale,
                                     float theta, __half * __restrict__ Q, __half * __restrict__ K,
                                     __half * __restrict__ V, int Sj, int s_off) {
+    pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (w >= (long long)B * S * nh) return;
@@ -85,6 +87,7 @@ __global__ void qk_norm_rope_kernel(const float * __restrict__ qkv, int B, int S
 }
 
 __global__ void latent_to_tokens_kernel(const float * __restrict__ lat, int B, int C, int T, __nv_bfloat16 * __restrict__ y) {
+    pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)B * C * T) return;
     const int c = (int)(i % C);
@@ -95,6 +98,7 @@ __global__ void latent_to_tokens_kernel(const float * __restrict__ lat, int B, i
 
 __global__ void sync_prep_kernel(const float * __restrict__ sync, int B, int S, int C, const float * __restrict__ pe,
                                  __nv_bfloat16 * __restrict__ y) {
+    pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)B * S * C) return;
     const int c = (int)(i % C);
@@ -104,6 +108,7 @@ __global__ void sync_prep_kernel(const float * __restrict__ sync, int B, int S, 
 
 __global__ void text_prep_kernel(const float * __restrict__ text, int text_S, int text_dim, const float * __restrict__ t5,
                                  int t5_S, int t5_dim, int B, __nv_bfloat16 * __restrict__ y) {
+    pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const int St = text_S + t5_S;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)B * St * t5_dim) return;
@@ -117,6 +122,7 @@ __global__ void text_prep_kernel(const float * __restrict__ text, int text_S, in
 }
 
 __global__ void timestep_embed_kernel(const float * __restrict__ t, int B, int H, float max_period, float * __restrict__ y) {
+    pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     const int half = H / 2;
     if (i >= B * half) return;
@@ -129,6 +135,7 @@ __global__ void timestep_embed_kernel(const float * __restrict__ t, int B, int H
 }
 
 __global__ void seq_mean_kernel(const float * __restrict__ x, int B, int S, int H, float * __restrict__ y) {
+    pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= B * H) return;
     const int b = i / H, h = i % H;
@@ -138,12 +145,14 @@ __global__ void seq_mean_kernel(const float * __restrict__ x, int B, int S, int 
 }
 
 __global__ void add_vec_kernel(const float * a, const float * b, int n, float * y) {
+    pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) y[i] = a[i] + b[i];
 }
 
 __global__ void build_extended_kernel(const float * __restrict__ sync, int sync_S, const float * __restrict__ gc, int B,
                                       int T, int H, float * __restrict__ ext, __nv_bfloat16 * __restrict__ sext) {
+    pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)B * T * H) return;
     const int h = (int)(i % H);
@@ -156,17 +165,20 @@ __global__ void build_extended_kernel(const float * __restrict__ sync, int sync_
 }
 
 __global__ void silu_vec_kernel(const float * __restrict__ x, int n, float * __restrict__ y) {
+    pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) y[i] = silu_f(x[i]);
 }
 
 __global__ void cast_kernel(const float * __restrict__ x, long long n, __nv_bfloat16 * __restrict__ y) {
+    pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) y[i] = __float2bfloat16_rn(x[i]);
 }
 
 __global__ void cfg_euler_kernel(const float * __restrict__ flow, int P, int T, int L, float cfg, float dt,
                                  float * __restrict__ x, float * __restrict__ flow0) {
+    pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)P * L * T) return;
     const int t = (int)(i % T);
@@ -180,6 +192,7 @@ __global__ void cfg_euler_kernel(const float * __restrict__ flow, int P, int T, 
 }
 
 __global__ void dup_latent_kernel(const float * __restrict__ x, int P, int L, int T, float * __restrict__ lat2) {
+    pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const long long per = (long long)L * T;
     if (i >= (long long)P * per) return;

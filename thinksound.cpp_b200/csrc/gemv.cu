@@ -49,6 +49,7 @@ __global__ void __launch_bounds__(256)
 gemv_kernel(const void * __restrict__ W, const void * __restrict__ W2, int M, int K, const float * __restrict__ x,
             long long ldx, int N, const float * __restrict__ bias, int act, int round_bf16, void * y, int y_bf16,
             long long ldy) {
+    pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m = blockIdx.x * 8 + warp;
     if (m >= M) return;

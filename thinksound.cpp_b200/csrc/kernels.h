@@ -13,7 +13,7 @@ namespace tsd {
 //   W: bf16, [M rows][taps*K_in] (tap-major columns), via a 2-D tensor map (box 64 x 128*numA).
 //   X: bf16 activations, [nbatch][S][K_in] with arbitrary row / batch strides, via a 3-D tensor
 //      map (box 64 x BN x 1). Rows outside [0, S) of an item read as zero (conv padding).
-// One CTA computes a 128-feature x BN-token tile (two 128-feature tiles for the SwiGLU pair).
+// Persistent CTAs walk 128-feature x BN-token output tiles (SwiGLU: 64 w1 + 64 w3 rows per tile).
 // ---------------------------------------------------------------------------------------------
 enum EpiMode : int {
     EPI_STORE = 0,       // out = act(acc + bias)                       (f32 or bf16)
@@ -23,7 +23,9 @@ enum EpiMode : int {
 enum Act : int { ACT_NONE = 0, ACT_SILU = 1 };
 
 struct GemmParams {
-    int M;             // weight rows covered by the grid (multiple of 128; per A tile of 128)
+    int M;             // weight rows (multiple of 128; one A tile = 128 rows)
+    int mblocks;       // M / 128
+    int order;         // tile walk: 0 m-block-major, 1 token-tile-major
     int S;             // tokens per batch item
     int nbatch;
     int K_in;          // input features per tap (multiple of 64)
@@ -35,17 +37,22 @@ struct GemmParams {
     int m_valid;       // features >= m_valid are not stored (zero-padded weight rows)
     const float * bias;
     void * out; int out_bf16; long long ldo;       // out row = b*S + t
+    int out_cblk; long long out_cstride;           // column blocking: feature m at (m / cblk) * cstride + m % cblk
     float * resid; long long ldr;
     const float * gate; long long ldg; int gate_div;   // gate row = out row / gate_div
+    float * ws;        // split-K partials [out tile][split][BN][128] (splits > 1)
+    int * counters;    // per out tile arrival counters, zero between launches
     int * err;
 };
 
 struct GemmLaunch {
     CUtensorMap tmA, tmB;
     GemmParams p;
-    int numA;           // 1, or 2 for the SwiGLU pair
-    dim3 grid;
+    dim3 grid;          // persistent: min(tiles, SMs) CTAs
 };
+
+// Programmatic dependent launch on (default) unless TSD_NO_PDL is set to a non-zero value.
+bool pdl_enabled();
 
 // Tensor-map helpers (driver entry point resolved at first use).
 bool make_tmap_2d(CUtensorMap * m, const void * ptr, CUtensorMapDataType dt, int esize,
@@ -54,10 +61,15 @@ bool make_tmap_3d(CUtensorMap * m, const void * ptr, CUtensorMapDataType dt, int
                   uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
                   uint32_t b0, uint32_t b1, uint32_t b2);
 
-// Fill `L` for a GEMM; returns false on unsupported arguments.
-bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pad, int numA,
+// Fill `L` for a GEMM; returns false on unsupported arguments. swiglu: W holds w1/w3 rows
+// interleaved in 64-row blocks and the output has M / 2 features. Split-K (max_splits > 1) is
+// used only if ws_floats / n_counters can hold the partials; the caller then sets p.ws and
+// p.counters (counters zeroed once; the kernel leaves them zero).
+bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pad, int swiglu,
                const void * X, int nbatch, int S, long long x_row_stride, long long x_batch_stride,
-               int num_sms, int max_splits);
+               int num_sms, int max_splits, long long ws_floats = 0, int n_counters = 0);
+// Workspace floats a planned launch needs (0 when it does not split K).
+long long gemm_ws_floats(const GemmLaunch & L);
 cudaError_t gemm_launch(const GemmLaunch & L, cudaStream_t st);
 
 // ---------------------------------------------------------------------------------------------

@@ -7,7 +7,7 @@
 // weights are repacked once into the layouts the kernels read:
 //   * conv weights ggml [K, IC, OC] -> bf16 [OC][K*IC] (tap-major, one K-block per tap);
 //   * qkv rows f = 3c + j (split_qkv, mmdit.cpp:67-76) -> [Q rows | K rows | V rows];
-//   * SwiGLU w1 / w3 -> one matrix interleaved in 128-row blocks (w1 block, w3 block, ...);
+//   * SwiGLU w1 / w3 -> one matrix interleaved in 64-row blocks (w1 block, w3 block, ...);
 //   * every per-token adaLN weight (joint latent blocks, fused blocks, final layer) stacked
 //     into one matrix, so all of them run as one GEMM per forward;
 //   * F32 / F16 / Q8_0 projection weights are converted to bf16 for the tensor cores.
@@ -187,7 +187,7 @@ struct Finalizer {
         consumed.push_back(p + ".weight");
         return g;
     }
-    // SwiGLU pair: w1, w3 ([K_in, F] or [taps, K_in, F]) interleaved in 128-row blocks.
+    // SwiGLU pair: w1, w3 ([K_in, F] or [taps, K_in, F]) interleaved in 64-row blocks.
     GW w13(const std::string & p, int taps, int pad) {
         GW g;
         const RawTensor * t1 = need(p + ".w1.weight");
@@ -195,13 +195,13 @@ struct Finalizer {
         if (!t1 || !t3) return g;
         const int F = (int)(taps == 1 ? t1->ne[1] : t1->ne[2]);
         const int K_in = (int)(taps == 1 ? t1->ne[0] : t1->ne[1]);
-        if (F % 128) { fprintf(stderr, "tsd: %s: FFN width %d not a multiple of 128\n", p.c_str(), F); rc = TSD_ERR_UNSUPPORTED; return g; }
+        if (F % 64) { fprintf(stderr, "tsd: %s: FFN width %d not a multiple of 64\n", p.c_str(), F); rc = TSD_ERR_UNSUPPORTED; return g; }
         g.M = 2 * F; g.K_in = K_in; g.taps = taps; g.pad = pad; g.m_valid = 2 * F;
         g.w = reinterpret_cast<__nv_bfloat16 *>(m.dalloc((size_t)2 * F * taps * K_in * 2));
         if (!g.w) { rc = TSD_ERR_CUDA; return g; }
         std::vector<int> m1(2 * F, -2), m3(2 * F, -2);
-        for (int b = 0; b < F / 128; ++b)
-            for (int r = 0; r < 128; ++r) { m1[256 * b + r] = 128 * b + r; m3[256 * b + 128 + r] = 128 * b + r; }
+        for (int b = 0; b < F / 64; ++b)
+            for (int r = 0; r < 64; ++r) { m1[128 * b + r] = 64 * b + r; m3[128 * b + 64 + r] = 64 * b + r; }
         repack(g.w, (long long)taps * K_in, m1, t1, K_in, taps);
         repack(g.w, (long long)taps * K_in, m3, t3, K_in, taps);
         consumed.push_back(p + ".w1.weight");

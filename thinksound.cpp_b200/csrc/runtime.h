@@ -121,6 +121,8 @@ struct Plan {
     // inputs / output (device)
     float * lat_in = nullptr, * clip_in = nullptr, * sync_in = nullptr, * text_in = nullptr, * t5_in = nullptr;
     float * gtext_in = nullptr, * t_in = nullptr, * flow = nullptr;
+    int * counters = nullptr;   // split-K arrival counters (re-zeroed after a device error)
+    int n_counters = 0;
     std::vector<Op> ops;
     std::vector<void *> allocs;
     cudaGraphExec_t graph = nullptr;

@@ -76,7 +76,7 @@ def lib() -> ctypes.CDLL:
         "tsd_version": [],
         "tsd_device_count": [],
         "tsd_op_gemm": [vp, i32, i32, i32, i32, vp, i32, i32, i64, i64, i32, i32, vp, i32, vp, i32, i64, vp, i64, vp,
-                        i64, i32, i32, vp, vp],
+                        i64, i32, i32, vp, i64, vp, i32, vp, vp],
         "tsd_op_gemv": [vp, i32, vp, i32, i32, vp, i64, i32, vp, i32, i32, vp, i32, i64, vp],
         "tsd_op_attention": [vp, vp, vp, i32, i32, i32, vp, i64, vp, vp],
         "tsd_op_ln_modulate": [vp, i32, i32, vp, vp, i64, i32, i32, vp, vp],
@@ -243,10 +243,13 @@ def _ptr(t) -> Optional[int]:
 
 
 def op_gemm(W, M, K_in, taps, pad, X, nbatch, S, x_row_stride, x_batch_stride, mode, act, bias, out, out_bf16, ldo,
-            resid=None, ldr=0, gate=None, ldg=0, gate_div=1, max_splits=1, m_valid=0, err=None, stream=0):
+            resid=None, ldr=0, gate=None, ldg=0, gate_div=1, max_splits=1, m_valid=0, ws=None, counters=None,
+            err=None, stream=0):
+    """ws: float32 tensor of split-K partials; counters: int32 tensor, zero before first use."""
     rc = lib().tsd_op_gemm(_ptr(W), M, K_in, taps, pad, _ptr(X), nbatch, S, x_row_stride, x_batch_stride, mode, act,
                            _ptr(bias), m_valid, _ptr(out), out_bf16, ldo, _ptr(resid), ldr, _ptr(gate), ldg, gate_div,
-                           max_splits, _ptr(err), stream)
+                           max_splits, _ptr(ws), 0 if ws is None else ws.numel(), _ptr(counters),
+                           0 if counters is None else counters.numel(), _ptr(err), stream)
     check("tsd_op_gemm", rc)
 
 
