@@ -47,6 +47,19 @@ TSD_API int tsd_op_gemm(const void * W, int M, int K_in, int taps, int pad, cons
                 int gate_div, int max_splits, float * ws, int64_t ws_floats, int * counters, int n_counters,
                 int * err, void * stream);
 
+/* tsd_op_gemm for callers that cannot allocate device memory (no counterpart in the
+ * reference): same arguments and results, but the split-K scratch comes from fixed
+ * file-scope device arrays in the library (8 MB of partial tiles + 32 KB of counters, held by
+ * every GPU that loads the library until exit), so the call performs no cudaMalloc/cudaFree.
+ * Outputs are limited to m_valid * nbatch * S <= 1048576 values; larger requests return
+ * TSD_ERR_ARG with a message. The first call on a device looks up the arrays' addresses
+ * (make it before any stream capture). All calls on a device share the arrays: calls that
+ * overlap on the GPU race. */
+TSD_API int tsd_op_gemm_static(const void * W, int M, int K_in, int taps, int pad, const void * X, int nbatch, int S,
+                               int64_t x_row_stride, int64_t x_batch_stride, int mode, int act, const float * bias,
+                               int m_valid, void * out, int out_bf16, int64_t ldo, float * resid, int64_t ldr,
+                               const float * gate, int64_t ldg, int gate_div, int max_splits, int * err, void * stream);
+
 /* Few-token GEMV with weights in their stored ggml type (0 F32, 30 BF16, 8 Q8_0), N <= 8
  * (the [H,1]-column mul_mats of mmdit.cpp:158-160,185-192,209). W2 != NULL: SwiGLU pair. */
 TSD_API int tsd_op_gemv(const void * W, int ggml_type, const void * W2, int M, int K, const float * x, int64_t ldx, int N,

@@ -29,7 +29,7 @@ EXPORTS = [
     "tsd_model_get_hparams", "tsd_get_tensor_f32", "tsd_forward", "tsd_forward_batched",
     "tsd_forward_device", "tsd_sync_check", "tsd_sample", "tsd_sample_batched", "tsd_version",
     "tsd_device_count", "tsd_op_gemm", "tsd_op_gemv", "tsd_op_attention", "tsd_op_ln_modulate",
-    "tsd_op_qk_norm_rope", "tsd_forward_profile", "tsd_plan_op_label",
+    "tsd_op_qk_norm_rope", "tsd_forward_profile", "tsd_plan_op_label", "tsd_op_gemm_static",
 ]
 
 
@@ -77,6 +77,8 @@ def lib() -> ctypes.CDLL:
         "tsd_device_count": [],
         "tsd_op_gemm": [vp, i32, i32, i32, i32, vp, i32, i32, i64, i64, i32, i32, vp, i32, vp, i32, i64, vp, i64, vp,
                         i64, i32, i32, vp, i64, vp, i32, vp, vp],
+        "tsd_op_gemm_static": [vp, i32, i32, i32, i32, vp, i32, i32, i64, i64, i32, i32, vp, i32, vp, i32, i64, vp,
+                               i64, vp, i64, i32, i32, vp, vp],
         "tsd_op_gemv": [vp, i32, vp, i32, i32, vp, i64, i32, vp, i32, i32, vp, i32, i64, vp],
         "tsd_op_attention": [vp, vp, vp, i32, i32, i32, vp, i64, vp, vp],
         "tsd_op_ln_modulate": [vp, i32, i32, vp, vp, i64, i32, i32, vp, vp],
@@ -251,6 +253,15 @@ def op_gemm(W, M, K_in, taps, pad, X, nbatch, S, x_row_stride, x_batch_stride, m
                            max_splits, _ptr(ws), 0 if ws is None else ws.numel(), _ptr(counters),
                            0 if counters is None else counters.numel(), _ptr(err), stream)
     check("tsd_op_gemm", rc)
+
+
+def op_gemm_static(W, M, K_in, taps, pad, X, nbatch, S, x_row_stride, x_batch_stride, mode, act, bias, out, out_bf16,
+                   ldo, resid=None, ldr=0, gate=None, ldg=0, gate_div=1, max_splits=8, m_valid=0, err=None, stream=0):
+    """op_gemm whose split-K scratch is the library's static device arrays (no allocation)."""
+    rc = lib().tsd_op_gemm_static(_ptr(W), M, K_in, taps, pad, _ptr(X), nbatch, S, x_row_stride, x_batch_stride, mode,
+                                  act, _ptr(bias), m_valid, _ptr(out), out_bf16, ldo, _ptr(resid), ldr, _ptr(gate), ldg,
+                                  gate_div, max_splits, _ptr(err), stream)
+    check("tsd_op_gemm_static", rc)
 
 
 def op_gemv(W, ggml_type, W2, M, K, x, ldx, N, bias, act, round_bf16, y, y_bf16, ldy, stream=0):
