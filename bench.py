@@ -172,15 +172,45 @@ def run_reference(args, rank, world):
 
 
 # ----------------------------------------------------------------------------------- ours
+def profile_case(wtype):
+    """One forward (B=2, config-3 token counts) of a depth-3 model (2 joint + 1 fused blocks) with
+    the full model's GEMM / attention / GEMV shapes, op by op through tsd_forward_profile; prints
+    each op's time. Small enough (~1.3 GB of weights) for a full ncu capture of single launches."""
+    import torch
+    import __graft_entry__
+    __graft_entry__.load_package()
+    import tsd_b200.synth as synth
+    from tsd_b200 import tsd
+    hp = synth.DitHParams(hidden=1536, n_head=24, depth=3, fused_depth=1)
+    if wtype == "bf16":
+        W = make_device_weights(hp, 1234, "cuda:0")
+    else:
+        W = synth.make_weights(hp, seed=1234, wtype="q8_0", q8_random_blocks=True)
+    m = tsd.DitModel.from_weights(hp, W)
+    del W
+    X = make_device_inputs(2, CFG3, 4242, "cuda:0")
+    p = m.forward_profile(2, CFG3["T"], CFG3["clip_S"], CFG3["sync_S"], CFG3["text_S"], CFG3["t5_S"],
+                          {k: v.data_ptr() for k, v in X.items()})
+    for i, (l, ms, b) in enumerate(zip(p["labels"], p["ms"], p["bytes"])):
+        print(f"{i:3d} {ms * 1000:8.1f} us {b / ms / 1e6:7.0f} GB/s  {l}")
+    m.sync_check()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--pairs", type=int, default=1, help="CFG pairs per GPU (batch = 2 * pairs)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", choices=["bf16", "q8_0"],
+                    help="instead of the bench: one op-by-op forward of a 2 joint + 1 fused block model at "
+                         "the config-3 widths (the small case the ncu captures are taken on)")
     args = ap.parse_args()
+    if args.profile_case:
+        return profile_case(args.profile_case)
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -232,6 +262,13 @@ def main():
     a_ms, a_fl, a_by, a_n = agg(2)
     v_ms, v_fl, v_by, v_n = agg(1)
     tot_ms = float(prof["ms"].sum())
+    # attention + projection path (SURVEY's "attn+proj": qkv GEMMs, attention, out-projection GEMMs)
+    labels = prof["labels"]
+    ap = [i for i, l in enumerate(labels)
+          if kinds[i] == 2 or (kinds[i] == 0 and (" K=1536 " in l and "mode=0" in l and "M=4608" in l
+                                                    or ("mode=2" in l and (" K=4608 " in l or " K=1536 " in l))))]
+    ap_ms = float(prof["ms"][ap].sum())
+    ap_fl = float(prof["flops"][ap].sum())
 
     # ---- device-timed steps (inputs resident in HBM) ----
     for _ in range(args.warmup):
@@ -310,6 +347,9 @@ def main():
                 "attention": {"launches": a_n, "ms": a_ms, "tflops": a_fl / (a_ms / 1000.0) / 1e12 if a_ms else None},
                 "gemv": {"launches": int(prof["launches"][kinds == 1].sum()), "ms": v_ms,
                          "gbs": v_by / (v_ms / 1000.0) / 1e9 if v_ms else None},
+                "attn_proj": {"launches": len(ap), "ms": ap_ms, "tflop": ap_fl / 1e12,
+                              "tflops": ap_fl / (ap_ms / 1000.0) / 1e12 if ap_ms else None,
+                              "frac_of_sustained_peak": ap_fl / (ap_ms / 1000.0) / 1e12 / peak if ap_ms else None},
                 "other_ms": tot_ms - g_ms - a_ms - v_ms, "profiled_step_ms": tot_ms,
                 "step_tflops_device": fl["total"] / (ms_max / args.steps / 1000.0) / 1e12,
             },

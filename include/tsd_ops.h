@@ -26,7 +26,7 @@ extern "C" {
 
 /* Epilogue modes of tsd_op_gemm. */
 #define TSD_EPI_STORE 0       /* out = act(acc + bias), f32 or bf16 */
-#define TSD_EPI_SWIGLU 1      /* out = silu(acc_w1) * acc_w3 (W rows interleaved in 128-row blocks) */
+#define TSD_EPI_SWIGLU 1      /* out[f] = silu(acc[2f]) * acc[2f+1]: W rows alternate w1 / w3; no bias */
 #define TSD_EPI_GATE_RESID 2  /* resid += gate * (acc + bias) */
 #define TSD_ACT_NONE 0
 #define TSD_ACT_SILU 1

@@ -366,7 +366,7 @@ int tsd_op_gemm(const void * W, int M, int K_in, int taps, int pad, const void *
     GemmLaunch L;
     const int swiglu = mode == EPI_SWIGLU;
     if (!gemm_plan(L, W, M, K_in, taps, pad, swiglu, X, nbatch, S, x_row_stride, x_batch_stride, sms,
-                   ws ? max_splits : 1, ws ? ws_floats : 0, ws ? n_counters : 0))
+                   max_splits, ws ? ws_floats : 0, ws ? n_counters : 0))
         return TSD_ERR_ARG;
     GemmParams & p = L.p;
     p.mode = mode; p.act = act;

@@ -76,13 +76,14 @@ struct Builder {
         p.resid = resid; p.ldr = ldr; p.gate = gate; p.ldg = ldg; p.gate_div = gate_div;
         p.ws = ws; p.counters = counters;
         p.err = m.d_err;
+        gemm_finalize(L);
         const double n_tok = (double)nbatch * S, kdim = (double)w.taps * w.K_in;
         const double flops = 2.0 * (swiglu ? 2 * p.m_valid : p.m_valid) * n_tok * kdim;
         const double bytes = 2.0 * M * kdim + 2.0 * n_tok * w.K_in + n_tok * (mode == EPI_GATE_RESID ? 12.0 : (out_bf16 ? 2.0 : 4.0)) * p.m_valid;
         op([L](cudaStream_t st) { return gemm_launch(L, st); }, OP_GEMM, flops, bytes);
         char buf[160];
-        snprintf(buf, sizeof buf, " M=%d N=%d K=%d taps=%d BN=%d grid=%ux%ux%u mode=%d", p.m_valid, nbatch * S,
-                 w.taps * w.K_in, w.taps, p.BN, L.grid.x, L.grid.y, L.grid.z, mode);
+        snprintf(buf, sizeof buf, " M=%d N=%d K=%d taps=%d BN=%d grid=%ux%ux%u mode=%d%s", p.m_valid, nbatch * S,
+                 w.taps * w.K_in, w.taps, p.BN, L.grid.x, L.grid.y, L.grid.z, mode, p.epi_tma ? " tma" : "");
         P.ops.back().label += buf;
     }
     // Few-token GEMV over B items (chunks of 8 tokens).

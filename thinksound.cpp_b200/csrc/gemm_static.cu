@@ -94,8 +94,9 @@ extern "C" int tsd_op_gemm_static(const void * W, int M, int K_in, int taps, int
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     GemmLaunch L;
+    // split-K always reduces through the static workspace here (no cluster reduction)
     if (!gemm_plan(L, W, M, K_in, taps, pad, swiglu, X, nbatch, S, x_row_stride, x_batch_stride, sms, max_splits,
-                   kStaticWsFloats, kStaticCounters))
+                   kStaticWsFloats, kStaticCounters, /*allow_cluster=*/false))
         return TSD_ERR_ARG;
     GemmParams & p = L.p;
     p.mode = mode; p.act = act;

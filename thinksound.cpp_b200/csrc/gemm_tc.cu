@@ -11,9 +11,9 @@
 // split), m-block-major so CTAs running at the same time share weight tiles through L2. Warp 0
 // issues TMA into a 4-stage ring, warp 1 owns TMEM and issues tcgen05.mma into one of two
 // 256-column accumulators, warps 2-5 drain the other accumulator (thread = output feature)
-// while the next tile accumulates. SwiGLU weights are interleaved in 64-row blocks (w1 rows,
-// then the matching w3 rows), so a tile holds h1 in TMEM lanes 0-63 and h3 in lanes 64-127;
-// the epilogue pairs them through shared memory. Launched with programmatic dependent launch:
+// while the next tile accumulates. SwiGLU weight rows alternate w1 / w3 of one feature, so h1
+// and h3 of a feature sit in neighbouring TMEM lanes (= neighbouring threads) and the epilogue
+// pairs them with one register exchange. Launched with programmatic dependent launch:
 // weight tiles of the first stages are requested before the kernel waits for the activations
 // its predecessor writes.
 #include "common.cuh"
@@ -31,10 +31,9 @@ constexpr int kStages = 4;
 constexpr int kABytes = 128 * 128;          // 128 rows x 64 bf16
 constexpr int kBBytesMax = 256 * 128;       // 256 tokens x 64 bf16
 constexpr int kStageBytes = kABytes + kBBytesMax;
-constexpr int kXStride = 33;                // SwiGLU exchange row stride (floats), conflict-free
-constexpr int kXBytes = 64 * kXStride * 4;
 constexpr int kTmemCols = 512;              // two 256-column fp32 accumulators
-constexpr int kSmemBytes = kStages * kStageBytes + kXBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int kEBufBytes = 16384;          // epilogue staging buffer (x2): 32 tokens x 128 f32
+constexpr int kSmemBytes = kStages * kStageBytes + 2 * kEBufBytes + 1024 /*align*/ + 256 /*barriers*/;
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
@@ -65,6 +64,23 @@ __device__ __forceinline__ TileCoord decode(const GemmParams & p, int t, int nkb
     return c;
 }
 
+// Epilogue kinds, fixed at compile time so that each kernel instance holds only its own
+// straight-line epilogue (with every variant in one body, the skipped branches of a 32-way
+// unrolled loop made the executed path a sparse walk through tens of KB of code and the
+// epilogue warps stalled on instruction fetch).
+enum EpiKind : int { EK_F32 = 0, EK_BF16, EK_F32_SILU, EK_BF16_SILU, EK_SWIGLU_F32, EK_SWIGLU_BF16, EK_GATE, EK_COUNT };
+template <int EK> struct Epi {
+    static constexpr bool gate = EK == EK_GATE;
+    static constexpr bool swiglu = EK == EK_SWIGLU_F32 || EK == EK_SWIGLU_BF16;
+    static constexpr bool bf16 = EK == EK_BF16 || EK == EK_BF16_SILU || EK == EK_SWIGLU_BF16;
+    static constexpr bool silu = EK == EK_F32_SILU || EK == EK_BF16_SILU;
+};
+
+template <bool BF16> __device__ __forceinline__ void put(void * out, long long i, float v) {
+    if (BF16) reinterpret_cast<__nv_bfloat16 *>(out)[i] = __float2bfloat16_rn(v);
+    else reinterpret_cast<float *>(out)[i] = v;
+}
+
 struct EpiCtx {
     int m;               // output feature of this thread
     bool m_ok;           // m is stored by this thread
@@ -74,72 +90,376 @@ struct EpiCtx {
     long long col;       // output column offset of feature m (after column blocking)
 };
 
-// Epilogue of one 32-column chunk of final accumulator values v (thread = feature e.m).
-// Fully unrolled and predicated so v[] stays in registers (a partially unrolled loop with an
-// early exit made the compiler spill it to local memory).
-__device__ __forceinline__ void emit_chunk(const GemmParams & p, const EpiCtx & e, int j0, float (&v)[32], float * xbuf,
-                                           int q, int lane, bool swiglu) {
-    if (swiglu) {
-        if (q >= 2) {
+// STORE: thread = feature e.m, 32 token columns j0.. of it; every warp store writes 32
+// consecutive features of one output row.
+template <int EK>
+__device__ __forceinline__ void emit_store(const GemmParams & p, const EpiCtx & e, int j0, const uint32_t (&v)[32]) {
+    if (!e.m_ok) return;
+    const int ncols = e.ncols - j0;
+    const long long base = (e.row_base + j0) * p.ldo + e.col;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) xbuf[((q - 2) * 32 + lane) * kXStride + j] = v[j];
-        }
-        epi_bar();
-        if (q < 2) {
+    for (int j = 0; j < 32; ++j) {
+        float val = __uint_as_float(v[j]) + e.bias;
+        if (Epi<EK>::silu) val = silu_f(val);
+        if (j < ncols) put<Epi<EK>::bf16>(p.out, base + (long long)j * p.ldo, val);
+    }
+}
+
+// SWIGLU: tile rows alternate w1 / w3 of one feature, so lanes 2i and 2i+1 hold h1 and h3 of
+// feature e.m. One exchange gives the even lane h3 of columns 0-15 and the odd lane h1 of
+// columns 16-31; each lane then finishes 16 of the 32 columns.
+template <int EK>
+__device__ __forceinline__ void emit_swiglu(const GemmParams & p, const EpiCtx & e, int j0, const uint32_t (&w)[32],
+                                            int lane) {
+    const bool odd = lane & 1;
+    float o[16];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]) * xbuf[(q * 32 + lane) * kXStride + j];
-        }
-        epi_bar();
+    for (int j = 0; j < 16; ++j) {
+        const float lo = __uint_as_float(w[j]), hi = __uint_as_float(w[j + 16]);
+        const float r = __shfl_xor_sync(0xffffffffu, odd ? lo : hi, 1);
+        const float h1 = odd ? r : lo, h3 = odd ? hi : r;
+        o[j] = silu_f(h1) * h3;
     }
     if (!e.m_ok) return;
-    const long long row0 = e.row_base + j0;
-    const int ncols = e.ncols - j0;
-    if (p.mode == EPI_GATE_RESID) {
-        // All gate and residual loads of the chunk are issued before any store: with the
-        // read-modify-write interleaved, possible aliasing serialised 32 memory round trips.
-        float * dst = p.resid + row0 * p.ldr + e.m;
-        const long long grow = row0 / p.gate_div;        // gate row of token row0
-        int gpos = (int)(row0 - grow * p.gate_div);      // position inside that gate row
-        const float * g = p.gate + grow * p.ldg + e.m;
-        float gv[32], xv[32];
+    const int c0 = j0 + (odd ? 16 : 0);
+    const int ncols = e.ncols - c0;
+    const long long base = (e.row_base + c0) * p.ldo + e.col;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            gv[j] = 0.f; xv[j] = 0.f;
-            if (j < ncols) { gv[j] = __ldg(g); xv[j] = dst[(long long)j * p.ldr]; }
-            if (++gpos == p.gate_div) { gpos = 0; g += p.ldg; }
-        }
+    for (int j = 0; j < 16; ++j)
+        if (j < ncols) put<Epi<EK>::bf16>(p.out, base + (long long)j * p.ldo, o[j]);
+}
+
+// TMA epilogue, STORE / SWIGLU: write one 32-token chunk into the staging buffer, laid out as
+// the output box [token][feature] (128 features; SwiGLU 64), f32 or bf16.
+template <int EK>
+__device__ __forceinline__ void stage_chunk(const EpiCtx & e, const uint32_t (&v)[32], int ml, int lane, uint8_t * sbuf) {
+    if (Epi<EK>::swiglu) {
+        const bool odd = lane & 1;
+        const int f = ml >> 1;                       // output feature within the tile
+        const int r0 = odd ? 16 : 0;                 // tokens of this lane
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-            if (j < ncols) dst[(long long)j * p.ldr] = xv[j] + gv[j] * (v[j] + e.bias);
-    } else if (p.out_bf16) {
-        __nv_bfloat16 * o = reinterpret_cast<__nv_bfloat16 *>(p.out) + row0 * p.ldo + e.col;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            float val = v[j] + e.bias;
-            if (p.act == ACT_SILU) val = silu_f(val);
-            if (j < ncols) o[(long long)j * p.ldo] = __float2bfloat16_rn(val);
+        for (int j = 0; j < 16; ++j) {
+            const float lo = __uint_as_float(v[j]), hi = __uint_as_float(v[j + 16]);
+            const float r = __shfl_xor_sync(0xffffffffu, odd ? lo : hi, 1);
+            const float h1 = odd ? r : lo, h3 = odd ? hi : r;
+            const float o = silu_f(h1) * h3;
+            if (Epi<EK>::bf16) reinterpret_cast<__nv_bfloat16 *>(sbuf)[(r0 + j) * 64 + f] = __float2bfloat16_rn(o);
+            else reinterpret_cast<float *>(sbuf)[(r0 + j) * 64 + f] = o;
         }
     } else {
-        float * o = reinterpret_cast<float *>(p.out) + row0 * p.ldo + e.col;
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-            float val = v[j] + e.bias;
-            if (p.act == ACT_SILU) val = silu_f(val);
-            if (j < ncols) o[(long long)j * p.ldo] = val;
+            float val = __uint_as_float(v[j]) + e.bias;
+            if (Epi<EK>::silu) val = silu_f(val);
+            if (Epi<EK>::bf16) reinterpret_cast<__nv_bfloat16 *>(sbuf)[j * 128 + ml] = __float2bfloat16_rn(val);
+            else reinterpret_cast<float *>(sbuf)[j * 128 + ml] = val;
         }
     }
 }
 
+// One 32-token chunk through the staging buffer: wait until the store that last read the
+// buffer is done, fill it, hand it to the TMA (thread 64 issues the stores: rows 0-15 and, if
+// inside the tile, rows 16-31).
+template <int EK>
+__device__ __forceinline__ void tma_chunk(const GemmParams & p, const CUtensorMap * tmO, const EpiCtx & e, int j0,
+                                          const uint32_t (&v)[32], int ml, int lane, uint8_t * ebuf, int & gc,
+                                          int c0o, int cb, int b, int t0) {
+    uint8_t * sbuf = ebuf + (gc & 1) * kEBufBytes;
+    if (gc >= 2 && threadIdx.x == 64) bulk_wait_read<1>();
+    epi_bar();
+    stage_chunk<EK>(e, v, ml, lane, sbuf);
+    fence_proxy_async_smem();
+    epi_bar();
+    if (threadIdx.x == 64) {
+        constexpr int rowb = (Epi<EK>::swiglu ? 64 : 128) * (Epi<EK>::bf16 ? 2 : 4);
+        tma_store_4d(tmO, sbuf, c0o, t0 + j0, b, cb);
+        if (j0 + 16 < p.BN) tma_store_4d(tmO, sbuf + 16 * rowb, c0o, t0 + j0 + 16, b, cb);
+        bulk_commit();
+    }
+    ++gc;
+}
+
+// TMA epilogue, GATE_RESID: request the residual (and per-token gate) tile of 16 tokens into
+// staging buffer g & 1 (residual [16][128] f32, gate behind it). Thread 64 only.
+__device__ __forceinline__ void gate_issue(const CUtensorMap * tmO, const CUtensorMap * tmG, bool gtile, uint64_t * ebar,
+                                           uint8_t * ebuf, int g, int m0, int t, int b) {
+    uint8_t * bb = ebuf + (g & 1) * kEBufBytes;
+    mbar_arrive_expect_tx(&ebar[g & 1], gtile ? 16384u : 8192u);
+    tma_load_4d(bb, tmO, &ebar[g & 1], m0, t, b, 0);
+    if (gtile) tma_load_4d(bb + 8192, tmG, &ebar[g & 1], m0, t, b, 0);
+}
+
+// GATE_RESID loads: gate and residual of 16 token columns of feature e.m. `g` / `gpos` walk the
+// gate rows (gate row = output row / gate_div) column by column.
+struct GateCursor {
+    const float * g;
+    int gpos;
+};
+__device__ __forceinline__ void gate_load16(const GemmParams & p, const EpiCtx & e, int c0, GateCursor & gc,
+                                            float (&gv)[16], float (&xv)[16]) {
+    const float * x = p.resid + (e.row_base + c0) * p.ldr + e.m;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        gv[j] = 0.f; xv[j] = 0.f;
+        if (e.m_ok && c0 + j < e.ncols) { gv[j] = __ldg(gc.g); xv[j] = x[(long long)j * p.ldr]; }
+        if (++gc.gpos == p.gate_div) { gc.gpos = 0; gc.g += p.ldg; }
+    }
+}
+__device__ __forceinline__ void gate_store16(const GemmParams & p, const EpiCtx & e, int c0, const uint32_t (&v)[16],
+                                             const float (&gv)[16], const float (&xv)[16]) {
+    if (!e.m_ok) return;
+    float * x = p.resid + (e.row_base + c0) * p.ldr + e.m;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+        if (c0 + j < e.ncols) x[(long long)j * p.ldr] = xv[j] + gv[j] * (__uint_as_float(v[j]) + e.bias);
+}
+
+// Split-K reduction + epilogue of one output tile by the CTA that completed it last.
+// Partials are [split][BN][128] floats. Warp w of the 4 epilogue warps takes rows j = w, w+4,
+// ...; lane l owns tile rows 4l..4l+3, so every access is a coalesced 512-byte row and the
+// loads of all splits are in flight together. Sum order is split 0, 1, 2, ... Outputs go out
+// as vectors when p.vec says the buffers allow it and every value of the vector is stored.
+template <int EK>
+__device__ __forceinline__ void store_one(const GemmParams & p, long long row, int m, float a, float bias) {
+    if (Epi<EK>::gate) {
+        float * dst = p.resid + row * p.ldr + m;
+        *dst += p.gate[(row / p.gate_div) * p.ldg + m] * (a + bias);
+        return;
+    }
+    float v = a + bias;
+    if (Epi<EK>::silu) v = silu_f(v);
+    const long long col = p.out_cblk ? (long long)(m / p.out_cblk) * p.out_cstride + m % p.out_cblk : m;
+    put<Epi<EK>::bf16>(p.out, row * p.ldo + col, v);
+}
+
+template <int EK>
+__device__ __forceinline__ void finish_row(const GemmParams & p, long long row, int mo, bool vec, const float4 & a4,
+                                           const float (&bias)[4], const float4 & g, const float4 & x0) {
+    const float a[4] = {a4.x, a4.y, a4.z, a4.w};
+    const long long col = p.out_cblk ? (long long)(mo / p.out_cblk) * p.out_cstride + mo % p.out_cblk : mo;
+    if (Epi<EK>::swiglu) {
+        const float o0 = silu_f(a[0]) * a[1], o1 = silu_f(a[2]) * a[3];
+        if (vec) {
+            if (Epi<EK>::bf16)
+                *reinterpret_cast<__nv_bfloat162 *>(reinterpret_cast<__nv_bfloat16 *>(p.out) + row * p.ldo + col) =
+                    __floats2bfloat162_rn(o0, o1);
+            else
+                *reinterpret_cast<float2 *>(reinterpret_cast<float *>(p.out) + row * p.ldo + col) = make_float2(o0, o1);
+        } else {
+            store_one<EK>(p, row, mo, o0, 0.f);
+            if (mo + 1 < p.m_valid) store_one<EK>(p, row, mo + 1, o1, 0.f);
+        }
+    } else if (!vec) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) if (mo + e < p.m_valid) store_one<EK>(p, row, mo + e, a[e], bias[e]);
+    } else if (Epi<EK>::gate) {
+        float4 x = x0;
+        x.x += g.x * (a[0] + bias[0]); x.y += g.y * (a[1] + bias[1]);
+        x.z += g.z * (a[2] + bias[2]); x.w += g.w * (a[3] + bias[3]);
+        *reinterpret_cast<float4 *>(p.resid + row * p.ldr + mo) = x;
+    } else {
+        float v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) { v[e] = a[e] + bias[e]; if (Epi<EK>::silu) v[e] = silu_f(v[e]); }
+        if (Epi<EK>::bf16) {
+            __nv_bfloat162 * o = reinterpret_cast<__nv_bfloat162 *>(reinterpret_cast<__nv_bfloat16 *>(p.out) + row * p.ldo + col);
+            o[0] = __floats2bfloat162_rn(v[0], v[1]);
+            o[1] = __floats2bfloat162_rn(v[2], v[3]);
+        } else {
+            *reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.out) + row * p.ldo + col) = make_float4(v[0], v[1], v[2], v[3]);
+        }
+    }
+}
+
+// Rows are taken 4 per warp at a time (j = j0 + 4r): their gate / residual loads and then,
+// split by split, their partial loads are all in flight together, so a group costs about one
+// memory round trip per split instead of one per row.
+template <int EK>
+__device__ __forceinline__ void reduce_tile(const GemmParams & p, const TileCoord & c, int ew, int lane) {
+    constexpr int R = 4;
+    const int ncols = min(p.BN, p.S - c.t0);
+    const size_t sstride = (size_t)p.BN * 128;                  // floats per split
+    const float * base = p.ws + (size_t)c.otile * p.splits * sstride + lane * 4;
+    // first output feature of this lane: SwiGLU rows (h1, h3, h1, h3) are features 2l, 2l + 1
+    const int nf = Epi<EK>::swiglu ? 2 : 4;
+    const int mo = Epi<EK>::swiglu ? c.mb * 64 + lane * 2 : c.mb * 128 + lane * 4;
+    if (mo >= p.m_valid) return;                                // no stored feature (no collectives below)
+    const bool vec = p.vec && mo + nf - 1 < p.m_valid;
+    float bias[4] = {0.f, 0.f, 0.f, 0.f};
+    if (!Epi<EK>::swiglu && p.bias) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) if (mo + e < p.m_valid) bias[e] = p.bias[mo + e];
+    }
+    const long long row0 = (long long)c.b * p.S + c.t0;
+    for (int j0 = ew; j0 < ncols; j0 += 4 * R) {
+        float4 acc[R], g[R], x[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+            g[r] = acc[r]; x[r] = acc[r];
+            const int j = j0 + 4 * r;
+            if (Epi<EK>::gate && vec && j < ncols) {
+                g[r] = __ldg(reinterpret_cast<const float4 *>(p.gate + ((row0 + j) / p.gate_div) * p.ldg + mo));
+                x[r] = *reinterpret_cast<const float4 *>(p.resid + (row0 + j) * p.ldr + mo);
+            }
+        }
+        for (int s = 0; s < p.splits; ++s) {
+            float4 part[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+                if (j0 + 4 * r < ncols)
+                    part[r] = __ldcg(reinterpret_cast<const float4 *>(base + s * sstride + (size_t)(j0 + 4 * r) * 128));
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+                if (j0 + 4 * r < ncols) {
+                    acc[r].x += part[r].x; acc[r].y += part[r].y; acc[r].z += part[r].z; acc[r].w += part[r].w;
+                }
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+            if (j0 + 4 * r < ncols) finish_row<EK>(p, row0 + j0 + 4 * r, mo, vec, acc[r], bias, g[r], x[r]);
+    }
+}
+
+// Split-K inside a cluster (one CTA per split, cluster rank = split). The tile's rows are cut
+// into per-rank slices of whole 16-row blocks; rank r finishes rows [lo(r), hi(r)).
+__device__ __forceinline__ int slice_lo(int r, int BN, int splits) { return 16 * (r * (BN >> 4) / splits); }
+__device__ __forceinline__ int slice_rows_max(int BN, int splits) { return 16 * (((BN >> 4) + splits - 1) / splits); }
+
+// This CTA's slice, 16 rows at a time: sum the ranks' partials in rank order (own rows from
+// `part`, the others from the receive slots the peers filled), apply the epilogue and write the
+// 16 rows out (TMA store from a staging buffer, or plain stores). Thread = tile row ml.
+template <int EK>
+__device__ __forceinline__ void finish_slice(const GemmParams & p, const CUtensorMap * tmO, const CUtensorMap * tmG,
+                                             const TileCoord & c, const EpiCtx & e, const float * part,
+                                             const float * recv, int rows_max, int rank, int lo, int hi, int ml,
+                                             int lane, uint8_t * ebuf, uint64_t * ebar, int & gs, int & gl) {
+    const bool tma = p.epi_tma;
+    const int m0 = Epi<EK>::swiglu ? c.mb * 64 : c.mb * 128;
+    const int cb = p.out_cblk ? m0 / p.out_cblk : 0;
+    const int c0o = m0 - cb * p.out_cblk;
+    const int nsteps = (hi - lo) >> 4;
+    const bool gtile = p.gate_div == 1;
+    GateCursor gcur{nullptr, 0};
+    if (Epi<EK>::gate) {
+        const long long r0 = e.row_base + lo;
+        const long long grow = r0 / p.gate_div;
+        gcur.g = p.gate + grow * p.ldg + e.m;
+        gcur.gpos = (int)(r0 - grow * p.gate_div);
+        if (tma && threadIdx.x == 64) {
+            bulk_wait_read<0>();
+            for (int k = 0; k < 2 && k < nsteps; ++k, ++gl)
+                gate_issue(tmO, tmG, gtile, ebar, ebuf, gl, m0, c.t0 + lo + 16 * k, c.b);
+        }
+    }
+    for (int k = 0; k < nsteps; ++k) {
+        const int r0 = lo + 16 * k;                           // first tile row (token) of this step
+        float acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+        for (int s = 0; s < p.splits; ++s) {
+            const float * src = s == rank ? part + (size_t)r0 * 128
+                                          : recv + ((size_t)(s < rank ? s : s - 1) * rows_max + (r0 - lo)) * 128;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[j] += src[j * 128 + ml];
+        }
+        if (Epi<EK>::gate) {
+            float gv[16];
+            if (!gtile || !tma) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    gv[j] = 0.f;
+                    if (e.m_ok && r0 + j < e.ncols) gv[j] = __ldg(gcur.g);
+                    if (++gcur.gpos == p.gate_div) { gcur.gpos = 0; gcur.g += p.ldg; }
+                }
+            }
+            if (tma) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&ebar[gs & 1], (gs >> 1) & 1, nullptr, p.err, DEV_TIMEOUT_ACC))) return;
+                float * xr = reinterpret_cast<float *>(ebuf + (gs & 1) * kEBufBytes);
+                const float * gr = xr + 16 * 128;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) xr[j * 128 + ml] += (gtile ? gr[j * 128 + ml] : gv[j]) * (acc[j] + e.bias);
+                fence_proxy_async_smem();
+                epi_bar();
+                if (threadIdx.x == 64) {
+                    tma_store_4d(tmO, xr, m0, c.t0 + r0, c.b, 0);
+                    bulk_commit();
+                    if (k + 2 < nsteps) {
+                        bulk_wait_read<0>();
+                        gate_issue(tmO, tmG, gtile, ebar, ebuf, gl, m0, c.t0 + r0 + 32, c.b);
+                        ++gl;
+                    }
+                }
+                ++gs;
+            } else if (e.m_ok) {
+                float * x = p.resid + (e.row_base + r0) * p.ldr + e.m;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (r0 + j < e.ncols) x[(long long)j * p.ldr] += gv[j] * (acc[j] + e.bias);
+            }
+            continue;
+        }
+        // STORE / SWIGLU: out row values of this thread's feature
+        float o[16];
+        bool mine = true;                                     // this thread holds an output value
+        if (Epi<EK>::swiglu) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const float r = __shfl_xor_sync(0xffffffffu, acc[j], 1);
+                o[j] = silu_f(acc[j]) * r;                    // valid on even lanes (h1 row)
+            }
+            mine = !(lane & 1);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                o[j] = acc[j] + e.bias;
+                if (Epi<EK>::silu) o[j] = silu_f(o[j]);
+            }
+        }
+        if (tma) {
+            uint8_t * sbuf = ebuf + (gs & 1) * kEBufBytes;
+            if (gs >= 2 && threadIdx.x == 64) bulk_wait_read<1>();
+            epi_bar();
+            const int fw = Epi<EK>::swiglu ? 64 : 128;
+            const int f = Epi<EK>::swiglu ? (ml >> 1) : ml;
+            if (mine) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    if (Epi<EK>::bf16) reinterpret_cast<__nv_bfloat16 *>(sbuf)[j * fw + f] = __float2bfloat16_rn(o[j]);
+                    else reinterpret_cast<float *>(sbuf)[j * fw + f] = o[j];
+                }
+            }
+            fence_proxy_async_smem();
+            epi_bar();
+            if (threadIdx.x == 64) {
+                tma_store_4d(tmO, sbuf, c0o, c.t0 + r0, c.b, cb);
+                bulk_commit();
+            }
+            ++gs;
+        } else if (mine && e.m_ok) {
+            const long long base = (e.row_base + r0) * p.ldo + e.col;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (r0 + j < e.ncols) put<Epi<EK>::bf16>(p.out, base + (long long)j * p.ldo, o[j]);
+        }
+    }
+}
+
+template <int EK>
 __global__ void __launch_bounds__(192, 1)
-gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmG, const GemmParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float * xbuf = reinterpret_cast<float *>(smem + kStages * kStageBytes);
-    uint64_t * full = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes + kXBytes);
+    uint8_t * ebuf = smem + kStages * kStageBytes;            // epilogue staging [2][kEBufBytes]
+    uint64_t * full = reinterpret_cast<uint64_t *>(ebuf + 2 * kEBufBytes);
     uint64_t * empty = full + kStages;
     uint64_t * acc_full = empty + kStages;     // [2]
     uint64_t * acc_empty = acc_full + 2;       // [2]
-    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+    uint64_t * ebar = acc_empty + 2;           // [2] residual / gate tile loads (GATE_RESID, TMA epilogue)
+    uint64_t * cbar = ebar + 2;                // [3] cluster split-K: slice rows received / own copies
+                                               //     landed at the peers / peers ready to receive
+    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(cbar + 3);
     volatile int * s_abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
     volatile int * s_last = s_abort + 1;       // split-K: this CTA reduces the tile
 
@@ -151,15 +471,28 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 4); }
+        for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 4); mbar_init(&ebar[s], 1); }
+        mbar_init(&cbar[0], 1);
+        for (int s = 1; s < 3; ++s) mbar_init(&cbar[s], p.csplit ? p.splits - 1 : 1);
         *s_abort = 0;
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) { tma_prefetch(&tmA); tma_prefetch(&tmB); }
+    if (threadIdx.x == 64 && p.epi_tma) { tma_prefetch(&tmO); if (Epi<EK>::gate && p.gate_div == 1) tma_prefetch(&tmG); }
     if (warp == 1) { tmem_alloc(tmem_slot, kTmemCols); tmem_relinquish(); }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // cluster split-K: every CTA's barriers are initialised before any peer arrives on them;
+    // cbar[0] then expects the bytes of this rank's slice from each of the other ranks
+    if (p.csplit) {
+        cluster_sync_all();
+        if (threadIdx.x == 64) {
+            const int r = (int)cluster_ctarank();
+            const int rows = slice_lo(r + 1, p.BN, p.splits) - slice_lo(r, p.BN, p.splits);
+            mbar_arrive_expect_tx(&cbar[0], (uint32_t)((p.splits - 1) * rows * 512));
+        }
+    }
     const uint32_t tmem = *tmem_slot;
     pdl_launch_dependents();
 
@@ -237,33 +570,185 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         pdl_wait();
         const int q = warp & 3;                       // TMEM lane quadrant of this warp
         const int ml = q * 32 + lane;                 // TMEM lane = weight row within the tile
-        const bool swiglu = p.mode == EPI_SWIGLU;
+        int gs = 0;                                   // staging-buffer uses so far (buffer gs & 1)
+        int gl = 0;                                   // thread 64: residual / gate loads issued
         int lt = 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++lt) {
             const TileCoord c = decode(p, t, nkb);
             const int buf = lt & 1;
+            EpiCtx e;
+            // output feature of this thread (SwiGLU: rows 2i / 2i + 1 are w1 / w3 of feature i)
+            e.m = Epi<EK>::swiglu ? c.mb * 64 + (ml >> 1) : c.mb * 128 + ml;
+            e.m_ok = e.m < p.m_valid;
+            e.bias = (p.bias && e.m_ok && !Epi<EK>::swiglu) ? p.bias[e.m] : 0.f;
+            e.ncols = min(p.BN, p.S - c.t0);
+            e.row_base = (long long)c.b * p.S + c.t0;
+            e.col = p.out_cblk ? (long long)(e.m / p.out_cblk) * p.out_cstride + e.m % p.out_cblk : e.m;
+            const bool tma = p.epi_tma && p.splits == 1;
+            const int m0 = Epi<EK>::swiglu ? c.mb * 64 : c.mb * 128;    // first output feature of the tile
+            const int cb = p.out_cblk ? m0 / p.out_cblk : 0;              // its column block (output map dim 3)
+            const int c0o = m0 - cb * p.out_cblk;
+            const int nsteps = p.BN >> 4;                                 // GATE_RESID: 16-token steps
+            const bool gtile = p.gate_div == 1;                           // per-token gate (else one per item)
+            // gate + residual of the first columns are fetched while the accumulator fills
+            GateCursor gcur{nullptr, 0};
+            float ga[16], xa[16], gb[16], xb[16];
+            if (Epi<EK>::gate && p.splits == 1) {
+                if (tma) {
+                    if (!gtile) {                                         // gate rows walked by a cursor
+                        const long long grow = e.row_base / p.gate_div;
+                        gcur.g = p.gate + grow * p.ldg + e.m;
+                        gcur.gpos = (int)(e.row_base - grow * p.gate_div);
+                    }
+                    if (threadIdx.x == 64) {
+                        bulk_wait_read<0>();
+                        for (int s2 = 0; s2 < 2 && s2 < nsteps; ++s2, ++gl)
+                            gate_issue(&tmO, &tmG, gtile, ebar, ebuf, gl, m0, c.t0 + 16 * s2, c.b);
+                    }
+                } else {
+                    const long long grow = e.row_base / p.gate_div;
+                    gcur.g = p.gate + grow * p.ldg + e.m;
+                    gcur.gpos = (int)(e.row_base - grow * p.gate_div);
+                    gate_load16(p, e, 0, gcur, ga, xa);
+                }
+            }
             // warp-uniform outcome: tcgen05.ld below is warp-collective
             if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (lt >> 1) & 1, s_abort, p.err, DEV_TIMEOUT_ACC)))
                 break;
             tc_fence_after();
             const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + buf * 256;
-            EpiCtx e;
-            // output feature of this thread (SwiGLU: lanes 0-63 carry h1 of features mb*64 + lane)
-            e.m = swiglu ? c.mb * 64 + ml : c.mb * 128 + ml;
-            e.m_ok = swiglu ? (q < 2 && e.m < p.m_valid) : (e.m < p.m_valid);
-            e.bias = (p.bias && e.m_ok && !swiglu) ? p.bias[e.m] : 0.f;
-            e.ncols = min(p.BN, p.S - c.t0);
-            e.row_base = (long long)c.b * p.S + c.t0;
-            e.col = p.out_cblk ? (long long)(e.m / p.out_cblk) * p.out_cstride + e.m % p.out_cblk : e.m;
             if (p.splits == 1) {
-                for (int j0 = 0; j0 < p.BN; j0 += 32) {
-                    float v[32];
-                    tmem_ld32(trow + j0, v);
-                    emit_chunk(p, e, j0, v, xbuf, q, lane, swiglu);
+                bool failed = false;
+                if (Epi<EK>::gate && tma) {
+                    // residual (+ gate) tiles of 16 tokens arrive by TMA two steps ahead; the
+                    // updated residual goes back by TMA store from the same buffer
+                    for (int s2 = 0; s2 < nsteps; ++s2, ++gs) {
+                        // no abort check: once issued, the load lands; all four warps agree
+                        if (!__all_sync(0xffffffffu, mbar_wait(&ebar[gs & 1], (gs >> 1) & 1, nullptr, p.err, DEV_TIMEOUT_ACC))) {
+                            failed = true;
+                            break;
+                        }
+                        float v[16], gv[16];
+                        if (!gtile) {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                gv[j] = 0.f;
+                                if (e.m_ok && 16 * s2 + j < e.ncols) gv[j] = __ldg(gcur.g);
+                                if (++gcur.gpos == p.gate_div) { gcur.gpos = 0; gcur.g += p.ldg; }
+                            }
+                        }
+                        tmem_ld16(trow + 16 * s2, v);
+                        float * xr = reinterpret_cast<float *>(ebuf + (gs & 1) * kEBufBytes);
+                        const float * gr = xr + 16 * 128;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const float g = gtile ? gr[j * 128 + ml] : gv[j];
+                            xr[j * 128 + ml] += g * (v[j] + e.bias);
+                        }
+                        fence_proxy_async_smem();
+                        epi_bar();
+                        if (threadIdx.x == 64) {
+                            tma_store_4d(&tmO, xr, m0, c.t0 + 16 * s2, c.b, 0);
+                            bulk_commit();
+                            if (s2 + 2 < nsteps) {
+                                bulk_wait_read<0>();
+                                gate_issue(&tmO, &tmG, gtile, ebar, ebuf, gl, m0, c.t0 + 16 * (s2 + 2), c.b);
+                                ++gl;
+                            }
+                        }
+                    }
+                } else if (Epi<EK>::gate) {
+                    // The next chunk's TMEM load and its gate / residual loads are in flight
+                    // while this chunk's results are stored.
+                    uint32_t va[16], vb[16];
+                    tmem_ld16_async(trow, va);
+                    tmem_wait_ld(va);
+                    for (int c0 = 0; c0 < p.BN; c0 += 32) {
+                        const bool nb = c0 + 16 < p.BN;
+                        if (nb) { gate_load16(p, e, c0 + 16, gcur, gb, xb); tmem_ld16_async(trow + c0 + 16, vb); }
+                        gate_store16(p, e, c0, va, ga, xa);
+                        if (!nb) break;
+                        tmem_wait_ld(vb);
+                        const bool na = c0 + 32 < p.BN;
+                        if (na) { gate_load16(p, e, c0 + 32, gcur, ga, xa); tmem_ld16_async(trow + c0 + 32, va); }
+                        gate_store16(p, e, c0 + 16, vb, gb, xb);
+                        if (!na) break;
+                        tmem_wait_ld(va);
+                    }
+                } else {
+                    // The next chunk's TMEM load is in flight while this chunk is written out.
+                    uint32_t va[32], vb[32];
+                    tmem_ld32_async(trow, va);
+                    tmem_wait_ld(va);
+                    for (int j0 = 0; j0 < p.BN; j0 += 64) {
+                        const bool nb = j0 + 32 < p.BN;
+                        if (nb) tmem_ld32_async(trow + j0 + 32, vb);
+                        if (tma) tma_chunk<EK>(p, &tmO, e, j0, va, ml, lane, ebuf, gs, c0o, cb, c.b, c.t0);
+                        else if (Epi<EK>::swiglu) emit_swiglu<EK>(p, e, j0, va, lane);
+                        else emit_store<EK>(p, e, j0, va);
+                        if (!nb) break;
+                        tmem_wait_ld(vb);
+                        const bool na = j0 + 64 < p.BN;
+                        if (na) tmem_ld32_async(trow + j0 + 64, va);
+                        if (tma) tma_chunk<EK>(p, &tmO, e, j0 + 32, vb, ml, lane, ebuf, gs, c0o, cb, c.b, c.t0);
+                        else if (Epi<EK>::swiglu) emit_swiglu<EK>(p, e, j0 + 32, vb, lane);
+                        else emit_store<EK>(p, e, j0 + 32, vb);
+                        if (!na) break;
+                        tmem_wait_ld(va);
+                    }
                 }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                if (failed) break;
+            } else if (p.csplit) {
+                // Split-K inside the cluster (one tile per CTA; the operand stages are idle now):
+                // partial tile -> own shared memory; the row slices the other ranks finish are
+                // pushed into their receive slots by bulk copies that complete on their barrier;
+                // then this CTA's slice is summed over all ranks and finished.
+                const int rank = (int)cluster_ctarank();
+                const int rows_max = slice_rows_max(p.BN, p.splits);
+                const int lo = slice_lo(rank, p.BN, p.splits), hi = slice_lo(rank + 1, p.BN, p.splits);
+                float * part = reinterpret_cast<float *>(smem);                  // [BN][128]
+                float * recv = part + (size_t)p.BN * 128;                         // [splits - 1][rows_max][128]
+                if (threadIdx.x == 64) {     // the MMAs are done: this CTA's stages may now be written by peers
+                    for (int d = 0; d < p.splits; ++d)
+                        if (d != rank) mbar_arrive_remote(mapa_shared(smem_u32(&cbar[2]), (uint32_t)d));
+                }
+                for (int j0 = 0; j0 < p.BN; j0 += 32) {
+                    float v[32];
+                    tmem_ld32(trow + j0, v);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (j0 + j < p.BN) part[(j0 + j) * 128 + ml] = v[j];
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                fence_proxy_async_smem();
+                epi_bar();
+                // push once every peer's stages are free (a timed-out wait sends nothing)
+                if (threadIdx.x == 64 && mbar_wait_cluster(&cbar[2], 0, p.err, DEV_TIMEOUT_CLUSTER)) {
+                    for (int d = 0; d < p.splits; ++d) {
+                        if (d == rank) continue;
+                        const int dlo = slice_lo(d, p.BN, p.splits), dhi = slice_lo(d + 1, p.BN, p.splits);
+                        if (dhi <= dlo) continue;
+                        const int slot = rank < d ? rank : rank - 1;          // this rank's slot at d
+                        const uint32_t dst = mapa_shared(smem_u32(recv + (size_t)slot * rows_max * 128), (uint32_t)d);
+                        bulk_copy_to_peer(dst, part + (size_t)dlo * 128, (uint32_t)(dhi - dlo) * 512u,
+                                          mapa_shared(smem_u32(&cbar[0]), (uint32_t)d));
+                    }
+                }
+                // the other ranks' rows of this slice have landed (byte count on cbar[0])
+                if (__all_sync(0xffffffffu, mbar_wait_cluster(&cbar[0], 0, p.err, DEV_TIMEOUT_CLUSTER))) {
+                    if (threadIdx.x == 64) {                                       // tell the senders
+                        for (int d = 0; d < p.splits; ++d)
+                            if (d != rank) mbar_arrive_remote(mapa_shared(smem_u32(&cbar[1]), (uint32_t)d));
+                    }
+                    finish_slice<EK>(p, &tmO, &tmG, c, e, part, recv, rows_max, rank, lo, hi, ml, lane, ebuf, ebar, gs, gl);
+                }
+                // this CTA's outgoing copies have landed at every peer before it exits
+                __all_sync(0xffffffffu, mbar_wait_cluster(&cbar[1], 0, p.err, DEV_TIMEOUT_CLUSTER));
             } else {
                 // Split-K, deterministic: every split stores its partial tile; the CTA that
                 // completes the tile last sums the partials in split order and runs the epilogue.
@@ -273,7 +758,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     tmem_ld32(trow + j0, v);
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
-                        if (j0 + j < p.BN) wsp[(size_t)(j0 + j) * 128] = v[j];
+                        if (j0 + j < p.BN) __stcg(wsp + (size_t)(j0 + j) * 128, v[j]);
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -284,23 +769,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 epi_bar();
                 if (*s_last) {
                     __threadfence();
-                    const float * base = p.ws + (size_t)c.otile * p.splits * p.BN * 128 + ml;
-                    for (int j0 = 0; j0 < p.BN; j0 += 32) {
-                        float v[32];
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) v[j] = 0.f;
-                        for (int s = 0; s < p.splits; ++s) {
-                            const float * src = base + ((size_t)s * p.BN + j0) * 128;
-#pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                if (j0 + j < p.BN) v[j] += src[(size_t)j * 128];
-                        }
-                        emit_chunk(p, e, j0, v, xbuf, q, lane, swiglu);
-                    }
+                    reduce_tile<EK>(p, c, q, lane);
                     if (threadIdx.x == 64) p.counters[c.otile] = 0;   // ready for the next launch
                 }
                 epi_bar();   // every thread has read s_last before the next tile rewrites it
             }
+        }
+        if (threadIdx.x == 64) {
+            // loads issued but not consumed (a wait gave up): let them land before the CTA exits
+            for (int g = gs; g < gl; ++g) {
+                const unsigned long long t_start = globaltimer();
+                while (!mbar_try_wait(&ebar[g & 1], (g >> 1) & 1) && globaltimer() - t_start < kWaitNs) {}
+            }
+            bulk_wait<0>();                           // TMA stores complete before exit
         }
     }
     tc_fence_before();
@@ -366,26 +847,77 @@ bool make_tmap_3d(CUtensorMap * m, const void * ptr, CUtensorMapDataType dt, int
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Tile / split choice from a small cost model of one SM's work per K block of 64: MMA about
-// 2*BN cycles, operand fill about (16 KB + 128 B * BN) / 96 B per cycle, whichever is larger,
-// plus a fixed cost per tile wave (pipeline fill, last epilogue) and, for split-K, the partial
-// tile round trip through the workspace. Split-K adds parallelism when there are fewer output
-// tiles than SMs; ws_floats / n_counters bound it.
+// Clusters of `cs` CTAs of this kernel that can be resident at once (0 if unknown), cached per
+// device. One CTA fills an SM, so this is set by how SMs group into GPCs.
+static int max_active_clusters(int cs) {
+    static int cache[64][9];
+    static bool done[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || cs < 1 || cs > 8) return 0;
+    if (!done[dev]) {
+        done[dev] = true;
+        cudaFuncSetAttribute(gemm_tc_kernel<EK_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        for (int k = 1; k <= 8; ++k) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((unsigned)(k * (sms / k)), 1, 1);
+            cfg.blockDim = dim3(192, 1, 1);
+            cfg.dynamicSmemBytes = kSmemBytes;
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeClusterDimension;
+            at[0].val.clusterDim.x = (unsigned)k; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = 1;
+            cfg.attrs = at;
+            cfg.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<EK_F32>, &cfg) != cudaSuccess) {
+                cudaGetLastError();
+                n = 0;
+            }
+            cache[dev][k] = n;
+        }
+    }
+    return cache[dev][cs];
+}
+
+// Tile / split choice from a cost model of the kernel's time in SM cycles, fitted to per-CTA
+// phase timestamps taken on B200. Small-N GEMMs here are bound by L2 -> SM operand traffic:
+// every CTA streams its weight tile (16 KB per K block of 64) and its token tile (128 B per
+// token per K block), and all CTAs together draw ~8 KB / cycle; a single SM draws ~100 B /
+// cycle, and its MMA needs 2 * BN cycles per K block. The last tile's epilogue is exposed
+// (~20 B / cycle of output). Split-K trades a reduction for parallelism: within one wave the
+// splits of a tile form a cluster and reduce through distributed shared memory (~2000 cycles
+// + the slice rows); beyond one wave they reduce through the global workspace, whose last-
+// arriving CTA was measured at ~40000 cycles.
 static void choose_tiles(int S, int nbatch, int mblocks, int nkb, int num_sms, int max_splits, long long ws_floats,
-                         int n_counters, int & BN, int & n_tiles, int & splits) {
+                         int n_counters, bool allow_cluster, int & BN, int & n_tiles, int & splits) {
     double best = 1e30;
     BN = 16; n_tiles = (S + 15) / 16; splits = 1;
     for (int bn = 16; bn <= 256; bn += 16) {
         const int nt = (S + bn - 1) / bn;
         if (nt > 1 && ((S + nt - 1) / nt + 15) / 16 * 16 < bn) continue;   // a smaller bn gives the same count
         const long long otiles = (long long)mblocks * nbatch * nt;
-        for (int sp = 1; sp <= std::max(1, max_splits); ++sp) {
-            if (sp > 1 && (nkb / sp < 4 || otiles > n_counters || otiles * sp * bn * 128 > ws_floats)) break;
+        for (int sp = 1; sp <= std::min(8, std::max(1, max_splits)); ++sp) {   // reducers sum <= 8 partials
+            if (sp > 1 && nkb / sp < 4) break;
             const long long tiles = otiles * sp;
+            bool cluster = allow_cluster && sp > 1 && tiles <= num_sms;
+            if (cluster) {   // partial tile + receive slots fit the operand stages; clusters co-resident
+                const int rows_max = 16 * (((bn >> 4) + sp - 1) / sp);
+                const int mac = max_active_clusters(sp);
+                cluster = (long long)bn * 512 + (long long)(sp - 1) * rows_max * 512 <= (long long)kStages * kStageBytes &&
+                          mac > 0 && otiles <= mac;
+            }
+            if (sp > 1 && !cluster && (otiles > n_counters || otiles * sp * bn * 128 > ws_floats)) continue;
             const long long waves = (tiles + num_sms - 1) / num_sms;
-            const double per_kb = std::max(2.0 * bn, (16384.0 + 128.0 * bn) / 96.0);
-            const double reduce = sp > 1 ? (double)bn * 128 * 4 * (sp + 1) / 64.0 : 0.0;   // bytes / (B/cycle)
-            const double cost = (double)waves * ((double)nkb / sp * per_kb + 2000.0 + reduce);
+            const double kb = (double)nkb / sp;                          // K blocks per tile
+            const double tile_bytes = kb * (16384.0 + 128.0 * bn);
+            const long long wave_tiles = std::min<long long>(tiles, num_sms);
+            const double t_sm = kb * 2.0 * bn + tile_bytes / 100.0;
+            const double t_l2 = (double)wave_tiles * tile_bytes / 8000.0;
+            const double epi = bn * 128.0 * 4.0 / 20.0;
+            const double reduce = sp == 1 ? 0.0 : cluster ? 2000.0 + bn * 512.0 * 2.0 / 100.0 : 40000.0;
+            const double cost = (double)waves * (std::max(t_sm, t_l2) + 3000.0) + epi + reduce;
             if (cost < best - 1e-9) { best = cost; BN = bn; n_tiles = nt; splits = sp; }
         }
     }
@@ -393,26 +925,38 @@ static void choose_tiles(int S, int nbatch, int mblocks, int nkb, int num_sms, i
 
 long long gemm_ws_floats(const GemmLaunch & L) {
     const GemmParams & p = L.p;
-    return p.splits > 1 ? (long long)p.mblocks * p.nbatch * p.n_tiles * p.splits * p.BN * 128 : 0;
+    return p.splits > 1 && !p.csplit ? (long long)p.mblocks * p.nbatch * p.n_tiles * p.splits * p.BN * 128 : 0;
 }
 
 bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pad, int swiglu, const void * X,
                int nbatch, int S, long long x_row_stride, long long x_batch_stride, int num_sms, int max_splits,
-               long long ws_floats, int n_counters) {
+               long long ws_floats, int n_counters, bool allow_cluster) {
     if (M % 128 || K_in % 64 || taps < 1 || S < 1 || nbatch < 1) return false;
     GemmParams & p = L.p;
     p = GemmParams{};
+    L.finalized = false;
     p.M = M; p.S = S; p.nbatch = nbatch; p.K_in = K_in; p.taps = taps; p.pad = pad;
     p.mblocks = M / 128;
     p.gate_div = 1;
     const int nkb = taps * (K_in / 64);
-    choose_tiles(S, nbatch, p.mblocks, nkb, num_sms, max_splits, ws_floats, n_counters, p.BN, p.n_tiles, p.splits);
+    choose_tiles(S, nbatch, p.mblocks, nkb, num_sms, max_splits, ws_floats, n_counters, allow_cluster, p.BN,
+                 p.n_tiles, p.splits);
     p.m_valid = swiglu ? M / 2 : M;
     {
         const char * o = getenv("TSD_TILE_ORDER");
         p.order = (o && *o == '1') ? 1 : 0;
     }
     const long long tiles = (long long)p.mblocks * nbatch * p.n_tiles * p.splits;
+    // one wave of split tiles: the splits of an output tile run as one cluster (rank = split,
+    // which m-block-major order makes consecutive)
+    {
+        const int rows_max = 16 * (((p.BN >> 4) + p.splits - 1) / p.splits);
+        const int mac = p.splits > 1 ? max_active_clusters(p.splits) : 0;
+        p.csplit = allow_cluster && p.splits > 1 && tiles <= num_sms && mac > 0 &&
+                   (long long)p.mblocks * nbatch * p.n_tiles <= mac &&
+                   (long long)p.BN * 512 + (long long)(p.splits - 1) * rows_max * 512 <= (long long)kStages * kStageBytes;
+    }
+    if (p.csplit) p.order = 0;
     L.grid = dim3((unsigned)std::min<long long>(tiles, num_sms), 1, 1);
     if (!make_tmap_2d(&L.tmA, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)taps * K_in, (uint64_t)M,
                       (uint64_t)taps * K_in * 2, 64, 128))
@@ -423,23 +967,108 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
     return true;
 }
 
-cudaError_t gemm_launch(const GemmLaunch & L, cudaStream_t st) {
-    static bool attr = false;
+static bool make_tmap_4d(CUtensorMap * m, const void * ptr, CUtensorMapDataType dt, int esize, const uint64_t (&d)[4],
+                         const uint64_t (&stride_bytes)[3], const uint32_t (&box)[4]) {
+    auto fn = encode_fn();
+    if (!fn || (reinterpret_cast<uintptr_t>(ptr) & 15) || (box[0] * esize) % 16) return false;
+    for (int i = 0; i < 3; ++i)
+        if (stride_bytes[i] % 16 || stride_bytes[i] >= (1ull << 40)) return false;
+    cuuint64_t dims[4] = {d[0], d[1], d[2], d[3]};
+    cuuint64_t strides[3] = {stride_bytes[0], stride_bytes[1], stride_bytes[2]};
+    cuuint32_t bx[4] = {box[0], box[1], box[2], box[3]};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    return fn(m, dt, 4, const_cast<void *>(ptr), dims, strides, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
+void gemm_finalize(GemmLaunch & L) {
+    GemmParams & p = L.p;
+    const auto al = [](const void * q, unsigned a) { return (reinterpret_cast<uintptr_t>(q) & (a - 1)) == 0; };
+    // vector accesses in the split-K reducer (4 consecutive features; 2 for SwiGLU), if aligned
+    const int nv = p.mode == EPI_SWIGLU ? 2 : 4;
+    const unsigned ob = (unsigned)nv * (p.out_bf16 ? 2u : 4u);
+    p.vec = p.mode == EPI_GATE_RESID
+                ? (al(p.resid, 16) && al(p.gate, 16) && p.ldr % 4 == 0 && p.ldg % 4 == 0)
+                : (al(p.out, ob) && p.ldo % nv == 0 && (p.out_cblk == 0 || (p.out_cblk % nv == 0 && p.out_cstride % nv == 0)));
+    // TMA epilogue: output (or residual / gate) as [features][S][nbatch][column blocks]; boxes of
+    // 128 (SwiGLU 64) features x 16 tokens. Tokens past S and features past m_valid are clipped.
+    p.epi_tma = 0;
+    const uint64_t S = (uint64_t)p.S, nb = (uint64_t)p.nbatch;
+    if (p.mode == EPI_GATE_RESID) {
+        const bool gtile = p.gate_div == 1;
+        {
+            const uint64_t d[4] = {(uint64_t)p.m_valid, S, nb, 1};
+            const uint64_t sr[3] = {(uint64_t)p.ldr * 4, S * p.ldr * 4, S * nb * p.ldr * 4};
+            const uint64_t sg[3] = {(uint64_t)p.ldg * 4, S * p.ldg * 4, S * nb * p.ldg * 4};
+            const uint32_t box[4] = {128, 16, 1, 1};
+            p.epi_tma = make_tmap_4d(&L.tmO, p.resid, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d, sr, box) &&
+                        (!gtile || make_tmap_4d(&L.tmG, p.gate, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d, sg, box));
+        }
+    } else {
+        const int es = p.out_bf16 ? 2 : 4;
+        const uint32_t fw = p.mode == EPI_SWIGLU ? 64 : 128;
+        const CUtensorMapDataType dt = p.out_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+        const uint32_t box[4] = {fw, 16, 1, 1};
+        if (p.out_cblk == 0) {
+            const uint64_t d[4] = {(uint64_t)p.m_valid, S, nb, 1};
+            const uint64_t st[3] = {(uint64_t)p.ldo * es, S * p.ldo * es, S * nb * p.ldo * es};
+            p.epi_tma = make_tmap_4d(&L.tmO, p.out, dt, es, d, st, box);
+        } else if (p.out_cblk % fw == 0 && p.m_valid % p.out_cblk == 0) {
+            const uint64_t d[4] = {(uint64_t)p.out_cblk, S, nb, (uint64_t)(p.m_valid / p.out_cblk)};
+            const uint64_t st[3] = {(uint64_t)p.ldo * es, S * p.ldo * es, (uint64_t)p.out_cstride * es};
+            p.epi_tma = make_tmap_4d(&L.tmO, p.out, dt, es, d, st, box);
+        }
+    }
+    if (getenv("TSD_NO_TMA_EPILOGUE")) p.epi_tma = 0;
+    L.finalized = true;
+}
+
+namespace {
+template <int EK> cudaError_t launch_kind(cudaLaunchConfig_t & cfg, const GemmLaunch & L, const GemmParams & p) {
+    static bool attr = false;   // per instance
     if (!attr) {
-        cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<EK>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        if (e != cudaSuccess) return e;
         attr = true;
     }
+    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<EK>, L.tmA, L.tmB, L.tmO, L.tmG, p);
+}
+}  // namespace
+
+cudaError_t gemm_launch(const GemmLaunch & L0, cudaStream_t st) {
+    GemmLaunch Lf;
+    if (!L0.finalized) { Lf = L0; gemm_finalize(Lf); }
+    const GemmLaunch & L = L0.finalized ? L0 : Lf;
+    const GemmParams & p = L.p;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = L.grid;
     cfg.blockDim = dim3(192, 1, 1);
     cfg.dynamicSmemBytes = kSmemBytes;
     cfg.stream = st;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute at[2];
+    int na = 0;
+    if (pdl_enabled()) {
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (p.csplit) {
+        at[na].id = cudaLaunchAttributeClusterDimension;
+        at[na].val.clusterDim.x = (unsigned)p.splits;
+        at[na].val.clusterDim.y = 1;
+        at[na].val.clusterDim.z = 1;
+        ++na;
+    }
     cfg.attrs = at;
-    cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, L.tmA, L.tmB, L.p);
+    cfg.numAttrs = na;
+    switch (p.mode) {
+        case EPI_GATE_RESID: return launch_kind<EK_GATE>(cfg, L, p);
+        case EPI_SWIGLU: return p.out_bf16 ? launch_kind<EK_SWIGLU_BF16>(cfg, L, p) : launch_kind<EK_SWIGLU_F32>(cfg, L, p);
+        default:
+            if (p.act == ACT_SILU) return p.out_bf16 ? launch_kind<EK_BF16_SILU>(cfg, L, p) : launch_kind<EK_F32_SILU>(cfg, L, p);
+            return p.out_bf16 ? launch_kind<EK_BF16>(cfg, L, p) : launch_kind<EK_F32>(cfg, L, p);
+    }
 }
 
 }  // namespace tsd

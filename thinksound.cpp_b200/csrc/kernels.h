@@ -40,15 +40,21 @@ struct GemmParams {
     int out_cblk; long long out_cstride;           // column blocking: feature m at (m / cblk) * cstride + m % cblk
     float * resid; long long ldr;
     const float * gate; long long ldg; int gate_div;   // gate row = out row / gate_div
-    float * ws;        // split-K partials [out tile][split][BN][128] (splits > 1)
+    float * ws;        // split-K partials [out tile][split][BN][128] (splits > 1 and not csplit)
     int * counters;    // per out tile arrival counters, zero between launches
     int * err;
+    // set by gemm_finalize:
+    int vec;           // output buffers allow the split-K reducer's vector accesses
+    int epi_tma;       // epilogue moves output (GATE_RESID: residual / gate) tiles with TMA
+    int csplit;        // split-K through the cluster's shared memory (one wave; cluster = the splits of a tile)
 };
 
 struct GemmLaunch {
-    CUtensorMap tmA, tmB;
+    CUtensorMap tmA, tmB;   // weights, activations
+    CUtensorMap tmO, tmG;   // epilogue: output (GATE_RESID: residual) and per-token gate tiles
     GemmParams p;
     dim3 grid;          // persistent: min(tiles, SMs) CTAs
+    bool finalized = false;
 };
 
 // Programmatic dependent launch on (default) unless TSD_NO_PDL is set to a non-zero value.
@@ -61,15 +67,20 @@ bool make_tmap_3d(CUtensorMap * m, const void * ptr, CUtensorMapDataType dt, int
                   uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
                   uint32_t b0, uint32_t b1, uint32_t b2);
 
-// Fill `L` for a GEMM; returns false on unsupported arguments. swiglu: W holds w1/w3 rows
-// interleaved in 64-row blocks and the output has M / 2 features. Split-K (max_splits > 1) is
-// used only if ws_floats / n_counters can hold the partials; the caller then sets p.ws and
-// p.counters (counters zeroed once; the kernel leaves them zero).
+// Fill `L` for a GEMM; returns false on unsupported arguments. swiglu: W rows alternate w1 / w3
+// (row 2f = w1 of feature f, row 2f + 1 = w3 of f) and the output has M / 2 features. Split-K (max_splits > 1) is
+// reduces through the cluster's shared memory when the split tiles fit one wave (unless
+// allow_cluster is false), else through a global workspace, used only if ws_floats / n_counters
+// can hold the partials; the caller then sets p.ws and p.counters (counters zeroed once; the
+// kernel leaves them zero).
 bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pad, int swiglu,
                const void * X, int nbatch, int S, long long x_row_stride, long long x_batch_stride,
-               int num_sms, int max_splits, long long ws_floats = 0, int n_counters = 0);
+               int num_sms, int max_splits, long long ws_floats = 0, int n_counters = 0, bool allow_cluster = true);
 // Workspace floats a planned launch needs (0 when it does not split K).
 long long gemm_ws_floats(const GemmLaunch & L);
+// After the epilogue fields of L.p are set: encode the epilogue tensor maps (TMA stores where the
+// output layout allows them, plain stores otherwise). gemm_launch finalizes a copy if needed.
+void gemm_finalize(GemmLaunch & L);
 cudaError_t gemm_launch(const GemmLaunch & L, cudaStream_t st);
 
 // ---------------------------------------------------------------------------------------------

@@ -7,7 +7,7 @@
 // weights are repacked once into the layouts the kernels read:
 //   * conv weights ggml [K, IC, OC] -> bf16 [OC][K*IC] (tap-major, one K-block per tap);
 //   * qkv rows f = 3c + j (split_qkv, mmdit.cpp:67-76) -> [Q rows | K rows | V rows];
-//   * SwiGLU w1 / w3 -> one matrix interleaved in 64-row blocks (w1 block, w3 block, ...);
+//   * SwiGLU w1 / w3 -> one matrix whose rows alternate (w1 row f, w3 row f, w1 row f + 1, ...);
 //   * every per-token adaLN weight (joint latent blocks, fused blocks, final layer) stacked
 //     into one matrix, so all of them run as one GEMM per forward;
 //   * F32 / F16 / Q8_0 projection weights are converted to bf16 for the tensor cores.
@@ -187,7 +187,7 @@ struct Finalizer {
         consumed.push_back(p + ".weight");
         return g;
     }
-    // SwiGLU pair: w1, w3 ([K_in, F] or [taps, K_in, F]) interleaved in 64-row blocks.
+    // SwiGLU pair: w1, w3 ([K_in, F] or [taps, K_in, F]) as one matrix with alternating rows.
     GW w13(const std::string & p, int taps, int pad) {
         GW g;
         const RawTensor * t1 = need(p + ".w1.weight");
@@ -200,8 +200,7 @@ struct Finalizer {
         g.w = reinterpret_cast<__nv_bfloat16 *>(m.dalloc((size_t)2 * F * taps * K_in * 2));
         if (!g.w) { rc = TSD_ERR_CUDA; return g; }
         std::vector<int> m1(2 * F, -2), m3(2 * F, -2);
-        for (int b = 0; b < F / 64; ++b)
-            for (int r = 0; r < 64; ++r) { m1[128 * b + r] = 64 * b + r; m3[128 * b + 64 + r] = 64 * b + r; }
+        for (int f = 0; f < F; ++f) { m1[2 * f] = f; m3[2 * f + 1] = f; }
         repack(g.w, (long long)taps * K_in, m1, t1, K_in, taps);
         repack(g.w, (long long)taps * K_in, m3, t3, K_in, taps);
         consumed.push_back(p + ".w1.weight");
