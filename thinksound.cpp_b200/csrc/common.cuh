@@ -324,6 +324,9 @@ __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepc
 
 // ---- numerics ----
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+// SiLU for values about to be rounded to bf16 (GEMM epilogues): the fast exponential and
+// division intrinsics (a few ulp of f32) are far below bf16 resolution.
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 // 2^x on the SFU (ex2.approx); used for the softmax exponent.
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;

@@ -58,7 +58,8 @@ struct Builder {
               int out_cblk = 0, long long out_cstride = 0) {
         if (rc) return;
         // Linear layers over a contiguous batch run as one long token sequence.
-        if (w.taps == 1 && xbs == (long long)S * xrs && nbatch > 1) { S *= nbatch; nbatch = 1; }
+        // (not the QKV projection: its epilogue stores per item, clipped at the stream's length)
+        if (mode != EPI_QKV && w.taps == 1 && xbs == (long long)S * xrs && nbatch > 1) { S *= nbatch; nbatch = 1; }
         GemmLaunch L;
         const int M = w.M;
         if (!gemm_plan(L, w.w, M, w.K_in, w.taps, w.pad, swiglu, X, nbatch, S, xrs, xbs, m.num_sms, max_splits,
@@ -76,6 +77,11 @@ struct Builder {
         p.resid = resid; p.ldr = ldr; p.gate = gate; p.ldg = ldg; p.gate_div = gate_div;
         p.ws = ws; p.counters = counters;
         p.err = m.d_err;
+        if (mode == EPI_QKV) {
+            p.q_out = qspec.q; p.k_out = qspec.k; p.v_out = qspec.v;
+            p.qg = qspec.qg; p.kg = qspec.kg; p.rope = qspec.rope;
+            p.hidden = m.H; p.nh = m.nh; p.Sj = qspec.Sj; p.s_off = qspec.s_off; p.s_item = qspec.s_item;
+        }
         gemm_finalize(L);
         const double n_tok = (double)nbatch * S, kdim = (double)w.taps * w.K_in;
         const double flops = 2.0 * (swiglu ? 2 * p.m_valid : p.m_valid) * n_tok * kdim;
@@ -85,6 +91,22 @@ struct Builder {
         snprintf(buf, sizeof buf, " M=%d N=%d K=%d taps=%d BN=%d grid=%ux%ux%u mode=%d%s", p.m_valid, nbatch * S,
                  w.taps * w.K_in, w.taps, p.BN, L.grid.x, L.grid.y, L.grid.z, mode, p.epi_tma ? " tma" : "");
         P.ops.back().label += buf;
+    }
+    // QKV projection whose epilogue applies the per-head RMSNorm (Q, K) and RoPE (rope != null)
+    // and writes fp16 Q / K / V head-major at this stream's offset in the joint sequence
+    // (replaces qk_norm_rope after a plain f32 QKV GEMM).
+    struct QkvSpec {
+        __half * q = nullptr, * k = nullptr, * v = nullptr;
+        const float * qg = nullptr, * kg = nullptr;
+        const float2 * rope = nullptr;
+        int Sj = 0, s_off = 0, s_item = 0;
+    } qspec;
+    void gemm_qkv(const StreamW & w, const void * X, int nbatch, int S, const float2 * rope, __half * Q, __half * K,
+                  __half * V, int Sj, int s_off) {
+        qspec.q = Q; qspec.k = K; qspec.v = V; qspec.qg = w.qg; qspec.kg = w.kg; qspec.rope = rope;
+        qspec.Sj = Sj; qspec.s_off = s_off; qspec.s_item = S;
+        gemm(w.qkv, X, nbatch, S, m.H, (long long)S * m.H, EPI_QKV, ACT_NONE, nullptr, 0, 0, nullptr, 0, nullptr, 0, 1, 0,
+             /*max_splits=*/1);
     }
     // Few-token GEMV over B items (chunks of 8 tokens).
     void gemv(const VW & w, const float * x, long long ldx, int N, int act, float * y, long long ldy, int y_bf16 = 0) {
@@ -128,7 +150,6 @@ struct Builder {
         auto * a1 = alloc<__nv_bfloat16>((size_t)B * maxS * H);
         auto * hbuf = alloc<__nv_bfloat16>((size_t)B * maxS * F);
         auto * xn = alloc<__nv_bfloat16>((size_t)B * maxS * H);
-        auto * qkv = alloc<float>((size_t)B * maxS * 3 * H);
         float * x_lat = alloc<float>((size_t)B * T * H);
         float * x_clip = alloc<float>((size_t)B * cS * H);
         float * x_text = alloc<float>((size_t)B * St * H);
@@ -153,6 +174,8 @@ struct Builder {
         auto * Kb = alloc<__half>((size_t)B * nh * Sj * 64);
         auto * Vb = alloc<__half>((size_t)B * nh * Sj * 64);
         auto * ao = alloc<__nv_bfloat16>((size_t)B * Sj * H);
+        auto * rope_lat = alloc<float2>((size_t)T * 32);     // RoPE (cos, sin): latent positions, scale 1
+        auto * rope_clip = alloc<float2>((size_t)cS * 32);   // clip positions, scale T / clip_S
         ws = alloc<float>((size_t)kWsFloats);
         counters = alloc<int>((size_t)kCounters);
         if (rc) return;
@@ -172,6 +195,13 @@ struct Builder {
         const float * const sync_pe = m.sync_pe;
         const int text_S = sh.text_S, t5_S = sh.t5_S;
         const float theta = m.hp.rope_theta;
+        // step-invariant RoPE tables, built once with the plan
+        if (rope_table(T, 1.0f, theta, rope_lat, 0) != cudaSuccess ||
+            rope_table(cS, (float)T / (float)cS, theta, rope_clip, 0) != cudaSuccess ||
+            cudaStreamSynchronize(0) != cudaSuccess) {
+            rc = TSD_ERR_CUDA;
+            return;
+        }
 
         op([err](cudaStream_t st) { return cudaMemsetAsync(err, 0, sizeof(int), st); }, OP_COPY, 0, 0, 0);
 
@@ -265,13 +295,7 @@ struct Builder {
                 const long long ld = lds[s], cs = css[s];
                 op([=](cudaStream_t st) { return ln_modulate(xs[s], B * S, H, mod, mod + cs, ld, s == 0, S, xn, st); });
                 if (i == 0 && s == 2) snap("text_xn", xn, (long long)B * S * H, 1);
-                gemm(w.qkv, xn, B, S, H, (long long)S * H, EPI_STORE, ACT_NONE, qkv, 0, 3 * H);
-                const float fs = (s == 1) ? (float)T / (float)cS : 1.0f;
-                const StreamW wc = w;
-                const int sofs = soff[s];
-                op([=](cudaStream_t st) {
-                    return qk_norm_rope(qkv, B, S, H, nh, wc.qg, wc.kg, s != 2, fs, theta, Qb, Kb, Vb, Sj, sofs, st);
-                });
+                gemm_qkv(w, xn, B, S, s == 0 ? rope_lat : s == 1 ? rope_clip : nullptr, Qb, Kb, Vb, Sj, soff[s]);
             }
             if (i == 0) {
                 snap("a0_q", Qb, (long long)B * Sj * H, 2, B, nh, Sj);
@@ -311,9 +335,7 @@ struct Builder {
             const float * mod = mod_lat + (w.ada_off / H) * BTH;
             const long long ld = H, cs = BTH;
             op([=](cudaStream_t st) { return ln_modulate(x_lat, B * T, H, mod, mod + cs, ld, 1, T, xn, st); });
-            gemm(w.qkv, xn, B, T, H, (long long)T * H, EPI_STORE, ACT_NONE, qkv, 0, 3 * H);
-            const StreamW wc = w;
-            op([=](cudaStream_t st) { return qk_norm_rope(qkv, B, T, H, nh, wc.qg, wc.kg, 1, 1.0f, theta, Qb, Kb, Vb, T, 0, st); });
+            gemm_qkv(w, xn, B, T, rope_lat, Qb, Kb, Vb, T, 0);
             op([AF](cudaStream_t st) { return attn_launch(AF, st); }, OP_ATTN, 4.0 * B * nh * 64.0 * T * T,
                6.0 * B * nh * 64.0 * T + 2.0 * B * T * H);
             gemm(w.l1, ao, B, T, H, (long long)T * H, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, x_lat, H, mod + 2 * cs, ld, 1);

@@ -19,37 +19,64 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 // One warp per row. Two-pass mean / variance (population), eps 1e-5, no affine.
+// One CTA per row (token): each thread keeps up to kLnVec float4 of the row in registers, so x is
+// read once; mean, then the sum of squared deviations (two passes over registers, as
+// ggml_norm computes them), then LN(x) * (1 + scale) + shift written bf16.
+constexpr int kLnVec = 4;
+__device__ __forceinline__ float block_sum(float v, float * red) {
+    v = warp_sum(v);
+    const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __syncthreads();                       // red[] free from a previous use
+    if ((threadIdx.x & 31) == 0) red[w] = v;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < nw; ++i) t += red[i];
+    return t;
+}
 __global__ void ln_modulate_kernel(const float * __restrict__ x, int rows, int H, const float * __restrict__ shift,
                                    const float * __restrict__ scale, long long ld_mod, int per_token, int rows_per_item,
                                    __nv_bfloat16 * __restrict__ y) {
+    __shared__ float red[32];
     pdl_launch_dependents();   // let the next kernel in the stream start its prologue
-    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (row >= rows) return;
-    const float4 * xr = reinterpret_cast<const float4 *>(x + (long long)row * H);
+    const int row = blockIdx.x;
     const int n4 = H >> 2;
-    float s = 0.f;
-    for (int i = lane; i < n4; i += 32) { const float4 v = xr[i]; s += (v.x + v.y) + (v.z + v.w); }
-    const float mean = warp_sum(s) / (float)H;
-    float ss = 0.f;
-    for (int i = lane; i < n4; i += 32) {
-        const float4 v = xr[i];
-        const float a = v.x - mean, b = v.y - mean, c = v.z - mean, d = v.w - mean;
-        ss += (a * a + b * b) + (c * c + d * d);
-    }
-    const float rstd = 1.0f / sqrtf(warp_sum(ss) / (float)H + 1e-5f);
+    const float4 * xr = reinterpret_cast<const float4 *>(x + (long long)row * H);
     const long long mrow = per_token ? row : row / rows_per_item;
     const float4 * sh = reinterpret_cast<const float4 *>(shift + mrow * ld_mod);
     const float4 * sc = reinterpret_cast<const float4 *>(scale + mrow * ld_mod);
+    float4 v[kLnVec], a[kLnVec], c[kLnVec];
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < kLnVec; ++k) {
+        const int i = threadIdx.x + k * blockDim.x;
+        if (i < n4) {
+            v[k] = xr[i]; a[k] = sh[i]; c[k] = sc[i];
+            s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+        }
+    }
+    const float mean = block_sum(s, red) / (float)H;
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < kLnVec; ++k) {
+        const int i = threadIdx.x + k * blockDim.x;
+        if (i < n4) {
+            const float d0 = v[k].x - mean, d1 = v[k].y - mean, d2 = v[k].z - mean, d3 = v[k].w - mean;
+            ss += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
+        }
+    }
+    const float rstd = 1.0f / sqrtf(block_sum(ss, red) / (float)H + 1e-5f);
     __nv_bfloat162 * yr = reinterpret_cast<__nv_bfloat162 *>(y + (long long)row * H);
-    for (int i = lane; i < n4; i += 32) {
-        const float4 v = xr[i], a = sh[i], c = sc[i];
-        const float o0 = ((v.x - mean) * rstd) * (c.x + 1.0f) + a.x;
-        const float o1 = ((v.y - mean) * rstd) * (c.y + 1.0f) + a.y;
-        const float o2 = ((v.z - mean) * rstd) * (c.z + 1.0f) + a.z;
-        const float o3 = ((v.w - mean) * rstd) * (c.w + 1.0f) + a.w;
-        yr[2 * i] = __floats2bfloat162_rn(o0, o1);
-        yr[2 * i + 1] = __floats2bfloat162_rn(o2, o3);
+#pragma unroll
+    for (int k = 0; k < kLnVec; ++k) {
+        const int i = threadIdx.x + k * blockDim.x;
+        if (i < n4) {
+            const float o0 = ((v[k].x - mean) * rstd) * (c[k].x + 1.0f) + a[k].x;
+            const float o1 = ((v[k].y - mean) * rstd) * (c[k].y + 1.0f) + a[k].y;
+            const float o2 = ((v[k].z - mean) * rstd) * (c[k].z + 1.0f) + a[k].z;
+            const float o3 = ((v[k].w - mean) * rstd) * (c[k].w + 1.0f) + a[k].w;
+            yr[2 * i] = __floats2bfloat162_rn(o0, o1);
+            yr[2 * i + 1] = __floats2bfloat162_rn(o2, o3);
+        }
     }
 }
 
@@ -84,6 +111,17 @@ __global__ void qk_norm_rope_kernel(const float * __restrict__ qkv, int B, int S
     *reinterpret_cast<__half2 *>(Q + o) = __floats2half2_rn(q.x, q.y);
     *reinterpret_cast<__half2 *>(K + o) = __floats2half2_rn(k.x, k.y);
     *reinterpret_cast<__half2 *>(V + o) = __floats2half2_rn(v.x, v.y);
+}
+
+// The angle expression of qk_norm_rope_kernel, tabulated once per plan for the QKV GEMM epilogue.
+__global__ void rope_table_kernel(int S, float fscale, float theta, float2 * __restrict__ tab) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= S * 32) return;
+    const int t = i >> 5, p = i & 31;
+    const float ang = fscale * ((float)t * powf(theta, -2.0f * (float)p / 64.0f));
+    float sn, cs;
+    sincosf(ang, &sn, &cs);
+    tab[i] = make_float2(cs, sn);
 }
 
 __global__ void latent_to_tokens_kernel(const float * __restrict__ lat, int B, int C, int T, __nv_bfloat16 * __restrict__ y) {
@@ -208,7 +246,12 @@ inline unsigned nblk(long long n, int bs) { return (unsigned)((n + bs - 1) / bs)
 cudaError_t ln_modulate(const float * x, int rows, int H, const float * shift, const float * scale, long long ld_mod,
                         int per_token, int rows_per_item, __nv_bfloat16 * y, cudaStream_t st) {
     if (H % 4 || (ld_mod % 4)) return cudaErrorInvalidValue;
-    ln_modulate_kernel<<<nblk(rows, 8), 256, 0, st>>>(x, rows, H, shift, scale, ld_mod, per_token, rows_per_item, y);
+    // threads: the row's float4 count spread over at most kLnVec per thread, whole warps, <= 1024
+    const int n4 = H / 4;
+    int threads = (n4 + kLnVec - 1) / kLnVec;
+    threads = (threads + 31) / 32 * 32;
+    if (threads > 1024 || (long long)threads * kLnVec < n4) return cudaErrorInvalidValue;
+    ln_modulate_kernel<<<rows, threads, 0, st>>>(x, rows, H, shift, scale, ld_mod, per_token, rows_per_item, y);
     return cudaGetLastError();
 }
 
@@ -217,6 +260,11 @@ cudaError_t qk_norm_rope(const float * qkv, int B, int S, int H, int nh, const f
     if (H != nh * 64) return cudaErrorInvalidValue;
     qk_norm_rope_kernel<<<nblk((long long)B * S * nh, 8), 256, 0, st>>>(qkv, B, S, H, nh, qg, kg, rope, fscale, theta, Q, K,
                                                                        V, Sj, s_off);
+    return cudaGetLastError();
+}
+
+cudaError_t rope_table(int S, float fscale, float theta, float2 * tab, cudaStream_t st) {
+    rope_table_kernel<<<nblk((long long)S * 32, 256), 256, 0, st>>>(S, fscale, theta, tab);
     return cudaGetLastError();
 }
 

@@ -68,13 +68,17 @@ __device__ __forceinline__ TileCoord decode(const GemmParams & p, int t, int nkb
 // straight-line epilogue (with every variant in one body, the skipped branches of a 32-way
 // unrolled loop made the executed path a sparse walk through tens of KB of code and the
 // epilogue warps stalled on instruction fetch).
-enum EpiKind : int { EK_F32 = 0, EK_BF16, EK_F32_SILU, EK_BF16_SILU, EK_SWIGLU_F32, EK_SWIGLU_BF16, EK_GATE, EK_COUNT };
+enum EpiKind : int { EK_F32 = 0, EK_BF16, EK_F32_SILU, EK_BF16_SILU, EK_SWIGLU_F32, EK_SWIGLU_BF16, EK_GATE, EK_QKV, EK_COUNT };
 template <int EK> struct Epi {
     static constexpr bool gate = EK == EK_GATE;
+    static constexpr bool qkv = EK == EK_QKV;
     static constexpr bool swiglu = EK == EK_SWIGLU_F32 || EK == EK_SWIGLU_BF16;
     static constexpr bool bf16 = EK == EK_BF16 || EK == EK_BF16_SILU || EK == EK_SWIGLU_BF16;
     static constexpr bool silu = EK == EK_F32_SILU || EK == EK_BF16_SILU;
 };
+
+// SiLU in the epilogue: the fast form where the result is rounded to bf16, exact f32 otherwise.
+template <bool BF16> __device__ __forceinline__ float silu_out(float x) { return BF16 ? silu_fast(x) : silu_f(x); }
 
 template <bool BF16> __device__ __forceinline__ void put(void * out, long long i, float v) {
     if (BF16) reinterpret_cast<__nv_bfloat16 *>(out)[i] = __float2bfloat16_rn(v);
@@ -100,7 +104,7 @@ __device__ __forceinline__ void emit_store(const GemmParams & p, const EpiCtx & 
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
         float val = __uint_as_float(v[j]) + e.bias;
-        if (Epi<EK>::silu) val = silu_f(val);
+        if (Epi<EK>::silu) val = silu_out<Epi<EK>::bf16>(val);
         if (j < ncols) put<Epi<EK>::bf16>(p.out, base + (long long)j * p.ldo, val);
     }
 }
@@ -118,7 +122,7 @@ __device__ __forceinline__ void emit_swiglu(const GemmParams & p, const EpiCtx &
         const float lo = __uint_as_float(w[j]), hi = __uint_as_float(w[j + 16]);
         const float r = __shfl_xor_sync(0xffffffffu, odd ? lo : hi, 1);
         const float h1 = odd ? r : lo, h3 = odd ? hi : r;
-        o[j] = silu_f(h1) * h3;
+        o[j] = silu_out<Epi<EK>::bf16>(h1) * h3;
     }
     if (!e.m_ok) return;
     const int c0 = j0 + (odd ? 16 : 0);
@@ -142,7 +146,7 @@ __device__ __forceinline__ void stage_chunk(const EpiCtx & e, const uint32_t (&v
             const float lo = __uint_as_float(v[j]), hi = __uint_as_float(v[j + 16]);
             const float r = __shfl_xor_sync(0xffffffffu, odd ? lo : hi, 1);
             const float h1 = odd ? r : lo, h3 = odd ? hi : r;
-            const float o = silu_f(h1) * h3;
+            const float o = silu_out<Epi<EK>::bf16>(h1) * h3;
             if (Epi<EK>::bf16) reinterpret_cast<__nv_bfloat16 *>(sbuf)[(r0 + j) * 64 + f] = __float2bfloat16_rn(o);
             else reinterpret_cast<float *>(sbuf)[(r0 + j) * 64 + f] = o;
         }
@@ -150,7 +154,7 @@ __device__ __forceinline__ void stage_chunk(const EpiCtx & e, const uint32_t (&v
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
             float val = __uint_as_float(v[j]) + e.bias;
-            if (Epi<EK>::silu) val = silu_f(val);
+            if (Epi<EK>::silu) val = silu_out<Epi<EK>::bf16>(val);
             if (Epi<EK>::bf16) reinterpret_cast<__nv_bfloat16 *>(sbuf)[j * 128 + ml] = __float2bfloat16_rn(val);
             else reinterpret_cast<float *>(sbuf)[j * 128 + ml] = val;
         }
@@ -187,6 +191,108 @@ __device__ __forceinline__ void gate_issue(const CUtensorMap * tmO, const CUtens
     mbar_arrive_expect_tx(&ebar[g & 1], gtile ? 16384u : 8192u);
     tma_load_4d(bb, tmO, &ebar[g & 1], m0, t, b, 0);
     if (gtile) tma_load_4d(bb + 8192, tmG, &ebar[g & 1], m0, t, b, 0);
+}
+
+// QKV: RMSNorm over each head's 64 features (Q, K), RoPE on feature pairs (2i, 2i+1), fp16
+// into the head-major joint Q / K / V. Thread = feature; a head spans this warp and warp q ^ 1.
+// For 32 token columns the per-token sums of squares are reduced across the warp's lanes by a
+// transposing butterfly (lane j ends with token j's sum, 31 shuffles), exchanged with the
+// partner warp through shared memory (`red`, two buffers used alternately by the chunks that
+// take the barrier: `nqk` counts those, so two uses of a buffer always have a barrier between
+// them), and broadcast.
+// The float operations follow qk_norm_rope_kernel: (x * rstd) * g, then x0 cos - x1 sin,
+// x0 sin + x1 cos.
+// (cos, sin) of pair d / 2 for the 32 token columns from j0 of the tile (RoPE table rows).
+__device__ __forceinline__ void rope_load(const GemmParams & p, const EpiCtx & e, const TileCoord & c, int j0, int d,
+                                          float2 (&cs)[32]) {
+    const float2 * r = p.rope + (long long)(c.t0 + j0) * 32 + (d >> 1);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        cs[j] = make_float2(1.f, 0.f);
+        if (j0 + j < e.ncols) cs[j] = __ldg(r + j * 32);
+    }
+}
+
+__device__ __forceinline__ void emit_qkv(const GemmParams & p, const EpiCtx & e, const TileCoord & c, int j0,
+                                         const uint32_t (&w)[32], int ml, int lane, int q, uint8_t * ebuf, int & nqk,
+                                         int & gs, const CUtensorMap * tmQ, const CUtensorMap * tmK,
+                                         const CUtensorMap * tmV, float2 (&cs)[32]) {
+    // reduction exchange in the upper half of staging buffer 0 (staging uses the lower 8 KB)
+    float * red = reinterpret_cast<float *>(ebuf + 8192);
+    const int f0 = c.mb * 128;
+    const int which = f0 / p.hidden;                    // 0 Q, 1 K, 2 V
+    const int cf = f0 - which * p.hidden + ml;          // head * 64 + d
+    const int h = cf >> 6, d = cf & 63;
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(w[j]) + e.bias;
+    if (which < 2) {
+        float a[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) a[j] = v[j] * v[j];
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            const bool up = lane & off;
+#pragma unroll
+            for (int i = 0; i < off; ++i) {
+                const float send = up ? a[i] : a[i + off];
+                const float keep = up ? a[i + off] : a[i];
+                a[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+            }
+        }
+        float * rr = red + (nqk++ & 1) * 128;           // [warp quadrant][token]
+        rr[q * 32 + lane] = a[0];
+        epi_bar();
+        const float tot = rr[q * 32 + lane] + rr[(q ^ 1) * 32 + lane];
+        float * rsd = red + 256 + q * 32;               // this warp's rstd per token (warp-private)
+        rsd[lane] = 1.0f / sqrtf(tot / 64.0f + 1e-6f);  // rstd of token `lane`
+        __syncwarp();
+        const float g = (which == 0 ? p.qg : p.kg)[d];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = (v[j] * rsd[j]) * g;
+        __syncwarp();                                   // rsd is rewritten by the next chunk
+        if (p.rope) {
+            // cs holds this chunk's (cos, sin), loaded during the previous chunk (or before the
+            // accumulator was ready); the next chunk's are requested right after use
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const float o = __shfl_xor_sync(0xffffffffu, v[j], 1);
+                v[j] = (d & 1) ? o * cs[j].y + v[j] * cs[j].x : v[j] * cs[j].x - o * cs[j].y;
+            }
+            if (j0 + 32 < p.BN) rope_load(p, e, c, j0 + 32, d, cs);
+        }
+    }
+    if (p.epi_tma) {
+        // this warp pair's head: [32 tokens][64] fp16 in the staging buffer, then two 16-token
+        // TMA boxes (the second only inside the tile); tokens past the stream's length are clipped
+        uint8_t * sbuf = ebuf + (gs & 1) * kEBufBytes;
+        if (gs >= 2 && threadIdx.x == 64) bulk_wait_read<1>();
+        epi_bar();
+        __half * hb = reinterpret_cast<__half *>(sbuf + (ml >> 6) * 4096);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) hb[j * 64 + d] = __float2half_rn(v[j]);
+        fence_proxy_async_smem();
+        epi_bar();
+        if (threadIdx.x == 64) {
+            const CUtensorMap * tm = which == 0 ? tmQ : which == 1 ? tmK : tmV;
+            const int h0 = (f0 - which * p.hidden) >> 6;
+            for (int hh = 0; hh < 2; ++hh) {
+                tma_store_4d(tm, sbuf + hh * 4096, 0, c.t0 + j0, h0 + hh, c.b);
+                if (j0 + 16 < p.BN) tma_store_4d(tm, sbuf + hh * 4096 + 2048, 0, c.t0 + j0 + 16, h0 + hh, c.b);
+            }
+            bulk_commit();
+        }
+        ++gs;
+        return;
+    }
+    __half * dst = which == 0 ? p.q_out : which == 1 ? p.k_out : p.v_out;
+    long long row = e.row_base + j0;
+    int b = (int)(row / p.s_item), t = (int)(row - (long long)b * p.s_item);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        if (j0 + j < e.ncols) dst[(((long long)b * p.nh + h) * p.Sj + p.s_off + t) * 64 + d] = __float2half_rn(v[j]);
+        if (++t == p.s_item) { t = 0; ++b; }
+    }
 }
 
 // GATE_RESID loads: gate and residual of 16 token columns of feature e.m. `g` / `gpos` walk the
@@ -227,7 +333,7 @@ __device__ __forceinline__ void store_one(const GemmParams & p, long long row, i
         return;
     }
     float v = a + bias;
-    if (Epi<EK>::silu) v = silu_f(v);
+    if (Epi<EK>::silu) v = silu_out<Epi<EK>::bf16>(v);
     const long long col = p.out_cblk ? (long long)(m / p.out_cblk) * p.out_cstride + m % p.out_cblk : m;
     put<Epi<EK>::bf16>(p.out, row * p.ldo + col, v);
 }
@@ -238,7 +344,7 @@ __device__ __forceinline__ void finish_row(const GemmParams & p, long long row, 
     const float a[4] = {a4.x, a4.y, a4.z, a4.w};
     const long long col = p.out_cblk ? (long long)(mo / p.out_cblk) * p.out_cstride + mo % p.out_cblk : mo;
     if (Epi<EK>::swiglu) {
-        const float o0 = silu_f(a[0]) * a[1], o1 = silu_f(a[2]) * a[3];
+        const float o0 = silu_out<Epi<EK>::bf16>(a[0]) * a[1], o1 = silu_out<Epi<EK>::bf16>(a[2]) * a[3];
         if (vec) {
             if (Epi<EK>::bf16)
                 *reinterpret_cast<__nv_bfloat162 *>(reinterpret_cast<__nv_bfloat16 *>(p.out) + row * p.ldo + col) =
@@ -260,7 +366,7 @@ __device__ __forceinline__ void finish_row(const GemmParams & p, long long row, 
     } else {
         float v[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) { v[e] = a[e] + bias[e]; if (Epi<EK>::silu) v[e] = silu_f(v[e]); }
+        for (int e = 0; e < 4; ++e) { v[e] = a[e] + bias[e]; if (Epi<EK>::silu) v[e] = silu_out<Epi<EK>::bf16>(v[e]); }
         if (Epi<EK>::bf16) {
             __nv_bfloat162 * o = reinterpret_cast<__nv_bfloat162 *>(reinterpret_cast<__nv_bfloat16 *>(p.out) + row * p.ldo + col);
             o[0] = __floats2bfloat162_rn(v[0], v[1]);
@@ -406,14 +512,14 @@ __device__ __forceinline__ void finish_slice(const GemmParams & p, const CUtenso
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const float r = __shfl_xor_sync(0xffffffffu, acc[j], 1);
-                o[j] = silu_f(acc[j]) * r;                    // valid on even lanes (h1 row)
+                o[j] = silu_out<Epi<EK>::bf16>(acc[j]) * r;                    // valid on even lanes (h1 row)
             }
             mine = !(lane & 1);
         } else {
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 o[j] = acc[j] + e.bias;
-                if (Epi<EK>::silu) o[j] = silu_f(o[j]);
+                if (Epi<EK>::silu) o[j] = silu_out<Epi<EK>::bf16>(o[j]);
             }
         }
         if (tma) {
@@ -448,7 +554,8 @@ __device__ __forceinline__ void finish_slice(const GemmParams & p, const CUtenso
 template <int EK>
 __global__ void __launch_bounds__(192, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmG, const GemmParams p) {
+               const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmG,
+               const __grid_constant__ CUtensorMap tmV, const GemmParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t * ebuf = smem + kStages * kStageBytes;            // epilogue staging [2][kEBufBytes]
@@ -478,7 +585,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) { tma_prefetch(&tmA); tma_prefetch(&tmB); }
-    if (threadIdx.x == 64 && p.epi_tma) { tma_prefetch(&tmO); if (Epi<EK>::gate && p.gate_div == 1) tma_prefetch(&tmG); }
+    if (threadIdx.x == 64 && p.epi_tma) {
+        tma_prefetch(&tmO);
+        if ((Epi<EK>::gate && p.gate_div == 1) || Epi<EK>::qkv) tma_prefetch(&tmG);
+        if (Epi<EK>::qkv) tma_prefetch(&tmV);
+    }
     if (warp == 1) { tmem_alloc(tmem_slot, kTmemCols); tmem_relinquish(); }
     tc_fence_before();
     __syncthreads();
@@ -571,6 +682,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int q = warp & 3;                       // TMEM lane quadrant of this warp
         const int ml = q * 32 + lane;                 // TMEM lane = weight row within the tile
         int gs = 0;                                   // staging-buffer uses so far (buffer gs & 1)
+        int nqk = 0;                                  // QKV: chunks that took the RMS exchange barrier
         int gl = 0;                                   // thread 64: residual / gate loads issued
         int lt = 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++lt) {
@@ -612,6 +724,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     gate_load16(p, e, 0, gcur, ga, xa);
                 }
             }
+            float2 rcs[32];                                               // QKV: RoPE (cos, sin) of a chunk
+            if (Epi<EK>::qkv && p.rope && c.mb * 128 < 2 * p.hidden)
+                rope_load(p, e, c, 0, (c.mb * 128 - (c.mb * 128 / p.hidden) * p.hidden + ml) & 63, rcs);
             // warp-uniform outcome: tcgen05.ld below is warp-collective
             if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (lt >> 1) & 1, s_abort, p.err, DEV_TIMEOUT_ACC)))
                 break;
@@ -676,25 +791,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         tmem_wait_ld(va);
                     }
                 } else {
-                    // The next chunk's TMEM load is in flight while this chunk is written out.
-                    uint32_t va[32], vb[32];
-                    tmem_ld32_async(trow, va);
-                    tmem_wait_ld(va);
-                    for (int j0 = 0; j0 < p.BN; j0 += 64) {
-                        const bool nb = j0 + 32 < p.BN;
-                        if (nb) tmem_ld32_async(trow + j0 + 32, vb);
-                        if (tma) tma_chunk<EK>(p, &tmO, e, j0, va, ml, lane, ebuf, gs, c0o, cb, c.b, c.t0);
-                        else if (Epi<EK>::swiglu) emit_swiglu<EK>(p, e, j0, va, lane);
-                        else emit_store<EK>(p, e, j0, va);
-                        if (!nb) break;
-                        tmem_wait_ld(vb);
-                        const bool na = j0 + 64 < p.BN;
-                        if (na) tmem_ld32_async(trow + j0 + 64, va);
-                        if (tma) tma_chunk<EK>(p, &tmO, e, j0 + 32, vb, ml, lane, ebuf, gs, c0o, cb, c.b, c.t0);
-                        else if (Epi<EK>::swiglu) emit_swiglu<EK>(p, e, j0 + 32, vb, lane);
-                        else emit_store<EK>(p, e, j0 + 32, vb);
-                        if (!na) break;
-                        tmem_wait_ld(va);
+                    // One call site per epilogue body keeps the instruction footprint small (a
+                    // TMEM load is ~50 cycles; prefetching it would double the inlined code).
+                    for (int j0 = 0; j0 < p.BN; j0 += 32) {
+                        uint32_t v[32];
+                        tmem_ld32_async(trow + j0, v);
+                        tmem_wait_ld(v);
+                        if (Epi<EK>::qkv) emit_qkv(p, e, c, j0, v, ml, lane, q, ebuf, nqk, gs, &tmO, &tmG, &tmV, rcs);
+                        else if (tma) tma_chunk<EK>(p, &tmO, e, j0, v, ml, lane, ebuf, gs, c0o, cb, c.b, c.t0);
+                        else if (Epi<EK>::swiglu) emit_swiglu<EK>(p, e, j0, v, lane);
+                        else emit_store<EK>(p, e, j0, v);
                     }
                 }
                 tc_fence_before();
@@ -995,7 +1101,18 @@ void gemm_finalize(GemmLaunch & L) {
     // 128 (SwiGLU 64) features x 16 tokens. Tokens past S and features past m_valid are clipped.
     p.epi_tma = 0;
     const uint64_t S = (uint64_t)p.S, nb = (uint64_t)p.nbatch;
-    if (p.mode == EPI_GATE_RESID) {
+    if (p.mode == EPI_QKV) {
+        // the stream's rows of Q / K / V: [item][head][token < s_item][64] fp16, token stride 64,
+        // head stride Sj * 64, item stride nh * Sj * 64, based at token s_off
+        const uint64_t d[4] = {64, (uint64_t)p.s_item, (uint64_t)p.nh, nb};
+        const uint64_t st[3] = {128, (uint64_t)p.Sj * 128, (uint64_t)p.nh * p.Sj * 128};
+        const uint32_t box[4] = {64, 16, 1, 1};
+        const long long off = (long long)p.s_off * 64;
+        p.epi_tma = p.nbatch * p.S == p.nbatch * p.s_item &&
+                    make_tmap_4d(&L.tmO, p.q_out + off, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, d, st, box) &&
+                    make_tmap_4d(&L.tmG, p.k_out + off, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, d, st, box) &&
+                    make_tmap_4d(&L.tmV, p.v_out + off, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, d, st, box);
+    } else if (p.mode == EPI_GATE_RESID) {
         const bool gtile = p.gate_div == 1;
         {
             const uint64_t d[4] = {(uint64_t)p.m_valid, S, nb, 1};
@@ -1032,7 +1149,7 @@ template <int EK> cudaError_t launch_kind(cudaLaunchConfig_t & cfg, const GemmLa
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<EK>, L.tmA, L.tmB, L.tmO, L.tmG, p);
+    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<EK>, L.tmA, L.tmB, L.tmO, L.tmG, L.tmV, p);
 }
 }  // namespace
 
@@ -1062,7 +1179,9 @@ cudaError_t gemm_launch(const GemmLaunch & L0, cudaStream_t st) {
     }
     cfg.attrs = at;
     cfg.numAttrs = na;
+    if (p.mode == EPI_QKV && p.splits != 1) return cudaErrorInvalidValue;
     switch (p.mode) {
+        case EPI_QKV: return launch_kind<EK_QKV>(cfg, L, p);
         case EPI_GATE_RESID: return launch_kind<EK_GATE>(cfg, L, p);
         case EPI_SWIGLU: return p.out_bf16 ? launch_kind<EK_SWIGLU_BF16>(cfg, L, p) : launch_kind<EK_SWIGLU_F32>(cfg, L, p);
         default:

@@ -18,7 +18,8 @@ namespace tsd {
 enum EpiMode : int {
     EPI_STORE = 0,       // out = act(acc + bias)                       (f32 or bf16)
     EPI_SWIGLU = 1,      // out = silu(acc_w1) * acc_w3                  (bf16)
-    EPI_GATE_RESID = 2,  // resid += gate * (acc + bias)                 (f32, split-K via atomics)
+    EPI_GATE_RESID = 2,  // resid += gate * (acc + bias)                 (f32)
+    EPI_QKV = 3,         // per-head RMSNorm (Q, K) + RoPE, fp16 head-major Q / K / V (no split-K)
 };
 enum Act : int { ACT_NONE = 0, ACT_SILU = 1 };
 
@@ -47,11 +48,17 @@ struct GemmParams {
     int vec;           // output buffers allow the split-K reducer's vector accesses
     int epi_tma;       // epilogue moves output (GATE_RESID: residual / gate) tiles with TMA
     int csplit;        // split-K through the cluster's shared memory (one wave; cluster = the splits of a tile)
+    // EPI_QKV: W rows are [Q | K | V] (H each, feature = head * 64 + d); out row = item * s_item + t
+    __half * q_out, * k_out, * v_out;   // [item][nh][Sj][64], this stream's tokens at s_off
+    const float * qg, * kg;             // RMSNorm gains [64]
+    const float2 * rope;                // (cos, sin) [s_item][32], or null (no RoPE)
+    int hidden, nh, Sj, s_off, s_item;
 };
 
 struct GemmLaunch {
     CUtensorMap tmA, tmB;   // weights, activations
     CUtensorMap tmO, tmG;   // epilogue: output (GATE_RESID: residual) and per-token gate tiles
+    CUtensorMap tmV;        // EPI_QKV: tmO / tmG / tmV = the stream's Q / K / V rows
     GemmParams p;
     dim3 grid;          // persistent: min(tiles, SMs) CTAs
     bool finalized = false;
@@ -118,6 +125,8 @@ cudaError_t ln_modulate(const float * x, int rows, int H, const float * shift, c
                         long long ld_mod, int per_token, int rows_per_item, __nv_bfloat16 * y, cudaStream_t st);
 // qkv f32 [B][S][3H] (Q|K|V column blocks) -> RMSNorm(q,k)*gain, RoPE (if fscale > 0), fp16
 // head-major at sequence offset s_off of joint buffers [B][nh][Sj][64].
+// (cos, sin) of the RoPE angles fscale * (pos * theta^(-2i/64)), pos < S, i < 32 (ggml rope NORMAL).
+cudaError_t rope_table(int S, float fscale, float theta, float2 * tab, cudaStream_t st);
 cudaError_t qk_norm_rope(const float * qkv, int B, int S, int H, int nh, const float * qg, const float * kg,
                          int rope, float fscale, float theta, __half * Q, __half * K, __half * V, int Sj, int s_off,
                          cudaStream_t st);
