@@ -197,6 +197,81 @@ def profile_case(wtype):
     return 0
 
 
+CFG5 = dict(prompts=64, steps=24, cfg=5.0)
+
+
+def run_cfg5(args, rank, world, local):
+    """batched 24-step Euler CFG sampling of 64 prompts (cond + uncond each),
+    T=194, BF16, random-init weights, per-prompt seeded inputs with the config-3 shapes; prompts
+    sharded over the ranks (no collective while sampling), latents gathered to rank 0. Timed per
+    run around the whole job (each rank's synchronous tsd_sample_batched call, then the gather),
+    max over ranks; value = prompts x steps / seconds (pair-steps/s, the same unit as config 3)."""
+    import datetime
+    import numpy as np
+    import torch
+    import __graft_entry__
+    __graft_entry__.load_package()
+    import tsd_b200.synth as synth
+    from tsd_b200 import dp, tsd
+
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device(dev))
+        pg = dist
+    hp = synth.DitHParams(**HP3)
+    W = make_device_weights(hp, seed=1234, device=dev)
+    model = tsd.DitModel.from_weights(hp, W, device=local)
+    del W
+    torch.cuda.empty_cache()
+    P, steps, cfg = CFG5["prompts"], CFG5["steps"], CFG5["cfg"]
+    lo, hi = dp.shard_range(P, rank, world)
+    items = [None] * P
+    for i in range(lo, hi):   # this rank's prompts only; prompt i always has seed 4242 + i
+        items[i] = synth.make_inputs(hp, **CFG3, seed=4242 + i)[0]
+
+    def sample_fn(it, n_steps, c):
+        return model.sample(it, n_steps, c)
+
+    if hi > lo:
+        sample_fn(items[lo:hi], 2, cfg)   # warm-up: builds the plan for this batch shape
+    times = []
+    out = None
+    for _ in range(max(1, args.runs)):
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        out = dp.sample_sharded(sample_fn, items, steps, cfg, rank, world, device=dev if pg else None)
+        torch.cuda.synchronize()
+        dt = torch.tensor([time.perf_counter() - t0], device=dev, dtype=torch.float64)
+        if pg:
+            pg.all_reduce(dt, op=pg.ReduceOp.MAX)
+        times.append(float(dt[0]))
+    best = min(times)
+    if rank == 0:
+        assert out is not None and out.shape == (P, hp.latent_dim, CFG3["T"]) and np.isfinite(out).all()
+        fl = synth.step_flops(hp, 2, **CFG3)
+        line = {
+            "metric": "DiT CFG sampling pair-steps/s (cfg5: 64 prompts x 24 Euler steps, CFG 5, 9 s, BF16)",
+            "value": P * steps / best, "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": 1,
+            "ms_per_step": best * 1000.0 / steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (per-prompt seeded inputs, random-init weights)",
+            "config": {"workload": "cfg5 batched sampling", "prompts": P, "prompts_per_gpu": hi - lo,
+                       "parallelism": f"dp{world} (prompts; latents gathered to rank 0)",
+                       "runs_s": times, "tflop_per_run": P * steps * fl["total"] / 1e12},
+            "timing": "host clock around each rank's synchronous sampling call + the gather, max over ranks",
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -205,6 +280,10 @@ def main():
     ap.add_argument("--pairs", type=int, default=1, help="CFG pairs per GPU (batch = 2 * pairs)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="cfg3", choices=["cfg3", "cfg5"],
+                    help="cfg3 (default): one flow step per CFG pair; cfg5: 64 prompts x 24 Euler steps, CFG 5, "
+                         "sharded over the ranks, latents gathered to rank 0")
+    ap.add_argument("--runs", type=int, default=2, help="cfg5: timed sampling runs")
     ap.add_argument("--profile-case", choices=["bf16", "q8_0"],
                     help="instead of the bench: one op-by-op forward of a 2 joint + 1 fused block model at "
                          "the config-3 widths (the small case the ncu captures are taken on)")
@@ -217,6 +296,8 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.workload == "cfg5":
+        return run_cfg5(args, rank, world, local)
 
     import torch
     import __graft_entry__
@@ -264,8 +345,10 @@ def main():
     tot_ms = float(prof["ms"].sum())
     # attention + projection path (SURVEY's "attn+proj": qkv GEMMs, attention, out-projection GEMMs)
     labels = prof["labels"]
+    # (QKV GEMMs carry mode=3: their epilogue applies the QK-RMSNorm + RoPE; linear1 = mode=2 with
+    # K = 3H (conv) or H (text))
     ap = [i for i, l in enumerate(labels)
-          if kinds[i] == 2 or (kinds[i] == 0 and (" K=1536 " in l and "mode=0" in l and "M=4608" in l
+          if kinds[i] == 2 or (kinds[i] == 0 and ("mode=3" in l
                                                     or ("mode=2" in l and (" K=4608 " in l or " K=1536 " in l))))]
     ap_ms = float(prof["ms"][ap].sum())
     ap_fl = float(prof["flops"][ap].sum())

@@ -8,7 +8,10 @@
 #include "runtime.h"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
+#include <map>
+#include <tuple>
 
 namespace tsd {
 
@@ -22,6 +25,11 @@ namespace {
 struct Builder {
     Model & m;
     Plan & P;
+    Builder(Model & m_, Plan & P_) : m(m_), P(P_) {
+        const char * a = getenv("TSD_AUTOTUNE");
+        autotune = a && *a == '1';
+        tune_log = getenv("TSD_DEBUG_PLAN") != nullptr;
+    }
     int rc = TSD_OK;
     std::string tag = "pre";   // label prefix of the ops being added
     // Split-K scratch shared by all GEMMs of the plan (they run one after another).
@@ -29,6 +37,39 @@ struct Builder {
     static constexpr int kCounters = 1 << 16;
     float * ws = nullptr;
     int * counters = nullptr;
+    // Optional plan-time autotuning of the GEMM tiling (TSD_AUTOTUNE=1): per distinct shape the
+    // cost model's best few (token tile, K splits) choices are timed on the plan's own buffers
+    // and the fastest kept. Off by default: the number of K splits sets the summation order, so
+    // timing-noise-driven choices would make results differ (at bf16 rounding level) from run to
+    // run; the model's choice is a fixed function of the shape. Decisions are kept process-wide
+    // so that all plans of one process agree. Inputs hold whatever the buffers hold at build time:
+    // the kernels' speed does not depend on the values, and every buffer they write is rewritten
+    // by the forward itself.
+    using TuneKey = std::tuple<int, int, int, int, int, int, int, int, int, int>;
+    static std::map<TuneKey, std::pair<int, int>> & tuned_cache() {
+        static std::map<TuneKey, std::pair<int, int>> c;
+        return c;
+    }
+    cudaStream_t tune_st = nullptr;
+    bool autotune = false, tune_log = false;
+    ~Builder() { if (tune_st) cudaStreamDestroy(tune_st); }
+
+    // Milliseconds per launch of L (1 warm-up, then 3 timed launches), or -1 on a launch error.
+    float time_gemm(const GemmLaunch & L) {
+        if (!tune_st && cudaStreamCreateWithFlags(&tune_st, cudaStreamNonBlocking) != cudaSuccess) return -1.f;
+        cudaEvent_t e0, e1;
+        if (cudaEventCreate(&e0) != cudaSuccess) return -1.f;
+        if (cudaEventCreate(&e1) != cudaSuccess) { cudaEventDestroy(e0); return -1.f; }
+        float ms = -1.f;
+        bool ok = gemm_launch(L, tune_st) == cudaSuccess && cudaEventRecord(e0, tune_st) == cudaSuccess;
+        for (int i = 0; ok && i < 3; ++i) ok = gemm_launch(L, tune_st) == cudaSuccess;
+        ok = ok && cudaEventRecord(e1, tune_st) == cudaSuccess && cudaEventSynchronize(e1) == cudaSuccess &&
+             cudaEventElapsedTime(&ms, e0, e1) == cudaSuccess;
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        if (!ok) { cudaGetLastError(); return -1.f; }
+        return ms / 3.f;
+    }
 
     template <class T> T * alloc(size_t n) {
         void * p = nullptr;
@@ -62,8 +103,16 @@ struct Builder {
         if (mode != EPI_QKV && w.taps == 1 && xbs == (long long)S * xrs && nbatch > 1) { S *= nbatch; nbatch = 1; }
         GemmLaunch L;
         const int M = w.M;
+        int force_bn = 0, force_sp = 0;
+        const TuneKey key{m.device, M, w.K_in, w.taps, nbatch, S, mode, act, out_bf16, max_splits};
+        auto & tuned = tuned_cache();
+        auto hit = autotune ? tuned.find(key) : tuned.end();
+        if (autotune && hit != tuned.end()) {
+            force_bn = hit->second.first;
+            force_sp = hit->second.second;
+        }
         if (!gemm_plan(L, w.w, M, w.K_in, w.taps, w.pad, swiglu, X, nbatch, S, xrs, xbs, m.num_sms, max_splits,
-                       kWsFloats, kCounters)) {
+                       kWsFloats, kCounters, true, force_bn, force_sp)) {
             fprintf(stderr, "tsd: gemm plan failed (M %d K %d taps %d S %d)\n", M, w.K_in, w.taps, S);
             rc = TSD_ERR_ARG;
             return;
@@ -83,6 +132,32 @@ struct Builder {
             p.hidden = m.H; p.nh = m.nh; p.Sj = qspec.Sj; p.s_off = qspec.s_off; p.s_item = qspec.s_item;
         }
         gemm_finalize(L);
+        if (autotune && hit == tuned.end()) {
+            int bns[6], sps[6];
+            const int nc = gemm_candidates(M, w.K_in, w.taps, nbatch, S, m.num_sms, max_splits, kWsFloats, kCounters,
+                                           true, 6, bns, sps);
+            float best = time_gemm(L);
+            std::pair<int, int> pick{L.p.BN, L.p.splits};
+            if (tune_log) fprintf(stderr, "tsd tune: M=%d K=%d taps=%d nb=%d S=%d mode=%d: model BN=%d sp=%d %.1f us", M,
+                                  w.K_in, w.taps, nbatch, S, mode, L.p.BN, L.p.splits, best * 1000.f);
+            for (int i = 1; i < nc; ++i) {
+                GemmLaunch C = L;
+                if (!gemm_plan(C, w.w, M, w.K_in, w.taps, w.pad, swiglu, X, nbatch, S, xrs, xbs, m.num_sms, max_splits,
+                               kWsFloats, kCounters, true, bns[i], sps[i]))
+                    continue;
+                const GemmParams & q = L.p;   // same epilogue, new tiling
+                GemmParams & cp = C.p;
+                const int BN = cp.BN, nt = cp.n_tiles, sp = cp.splits, cs = cp.csplit, order = cp.order, st = cp.stages;
+                cp = q;
+                cp.BN = BN; cp.n_tiles = nt; cp.splits = sp; cp.csplit = cs; cp.order = order; cp.stages = st;
+                gemm_finalize(C);
+                const float t = time_gemm(C);
+                if (tune_log) fprintf(stderr, " | BN=%d sp=%d %.1f us", BN, sp, t * 1000.f);
+                if (t > 0.f && (best < 0.f || t < best)) { best = t; pick = {BN, sp}; L = C; }
+            }
+            if (tune_log) fprintf(stderr, " -> BN=%d sp=%d\n", pick.first, pick.second);
+            tuned[key] = pick;
+        }
         const double n_tok = (double)nbatch * S, kdim = (double)w.taps * w.K_in;
         const double flops = 2.0 * (swiglu ? 2 * p.m_valid : p.m_valid) * n_tok * kdim;
         const double bytes = 2.0 * M * kdim + 2.0 * n_tok * w.K_in + n_tok * (mode == EPI_GATE_RESID ? 12.0 : (out_bf16 ? 2.0 : 4.0)) * p.m_valid;

@@ -20,6 +20,7 @@
 #include "kernels.h"
 
 #include <algorithm>
+#include <vector>
 #include <cstdio>
 #include <cstdlib>
 
@@ -27,13 +28,12 @@ namespace tsd {
 
 namespace {
 
-constexpr int kStages = 4;
+constexpr int kMaxStages = 8;              // operand ring depth: as many stages as fit the area
+constexpr int kStageArea = 4 * (128 * 128 + 256 * 128);   // 192 KB: 4 stages at BN = 256
 constexpr int kABytes = 128 * 128;          // 128 rows x 64 bf16
-constexpr int kBBytesMax = 256 * 128;       // 256 tokens x 64 bf16
-constexpr int kStageBytes = kABytes + kBBytesMax;
 constexpr int kTmemCols = 512;              // two 256-column fp32 accumulators
 constexpr int kEBufBytes = 16384;          // epilogue staging buffer (x2): 32 tokens x 128 f32
-constexpr int kSmemBytes = kStages * kStageBytes + 2 * kEBufBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int kSmemBytes = kStageArea + 2 * kEBufBytes + 1024 /*align*/ + 256 /*barriers*/;
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
@@ -558,10 +558,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                const __grid_constant__ CUtensorMap tmV, const GemmParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t * ebuf = smem + kStages * kStageBytes;            // epilogue staging [2][kEBufBytes]
+    uint8_t * ebuf = smem + kStageArea;                       // epilogue staging [2][kEBufBytes]
     uint64_t * full = reinterpret_cast<uint64_t *>(ebuf + 2 * kEBufBytes);
-    uint64_t * empty = full + kStages;
-    uint64_t * acc_full = empty + kStages;     // [2]
+    uint64_t * empty = full + kMaxStages;
+    uint64_t * acc_full = empty + kMaxStages;  // [2]
     uint64_t * acc_empty = acc_full + 2;       // [2]
     uint64_t * ebar = acc_empty + 2;           // [2] residual / gate tile loads (GATE_RESID, TMA epilogue)
     uint64_t * cbar = ebar + 2;                // [3] cluster split-K: slice rows received / own copies
@@ -575,9 +575,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int nkb = p.taps * kpt;
     const int num_tiles = p.mblocks * p.nbatch * p.n_tiles * p.splits;
     const uint32_t tx_bytes = (uint32_t)(kABytes + p.BN * 128);
+    const int sbytes = kABytes + p.BN * 128;    // one stage (multiple of 1024: SW128 atoms stay aligned)
+    const int nst = p.stages;                   // ring depth, <= kMaxStages, nst * sbytes <= kStageArea
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int s = 0; s < kMaxStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 4); mbar_init(&ebar[s], 1); }
         mbar_init(&cbar[0], 1);
         for (int s = 1; s < 3; ++s) mbar_init(&cbar[s], p.csplit ? p.splits - 1 : 1);
@@ -613,39 +615,42 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // Weight tiles of the first stages do not depend on earlier kernels: request them
             // before waiting for the predecessor grid; their activation tiles follow the wait.
             int pre = 0;
-            for (int t = blockIdx.x; t < num_tiles && pre < kStages; t += gridDim.x) {
+            for (int t = blockIdx.x; t < num_tiles && pre < nst; t += gridDim.x) {
                 const TileCoord c = decode(p, t, nkb);
-                for (int kb = c.kb_begin; kb < c.kb_end && pre < kStages; ++kb, ++pre) {
+                for (int kb = c.kb_begin; kb < c.kb_end && pre < nst; ++kb, ++pre) {
                     mbar_arrive_expect_tx(&full[pre], tx_bytes);
-                    tma_load_2d(smem + pre * kStageBytes, &tmA, &full[pre], kb * 64, c.mb * 128);
+                    tma_load_2d(smem + pre * sbytes, &tmA, &full[pre], kb * 64, c.mb * 128);
                 }
             }
             pdl_wait();
             int it = 0;
+            int s = 0;                 // ring slot of `it`, and the parity of its use (it / nst) & 1
+            uint32_t ph = 0;
             for (int t = blockIdx.x; t < num_tiles && !*s_abort; t += gridDim.x) {
                 const TileCoord c = decode(p, t, nkb);
                 for (int kb = c.kb_begin; kb < c.kb_end; ++kb, ++it) {
-                    const int s = it % kStages;
-                    uint8_t * sa = smem + s * kStageBytes;
+                    uint8_t * sa = smem + s * sbytes;
+                    const int cs = s;
+                    const uint32_t cph = ph;
+                    if (++s == nst) { s = 0; ph ^= 1; }
                     const int tap = kb / kpt, kc = kb - tap * kpt;
                     if (it < pre) {       // A already requested
-                        tma_load_3d(sa + kABytes, &tmB, &full[s], kc * 64, c.t0 + tap - p.pad, c.b);
+                        tma_load_3d(sa + kABytes, &tmB, &full[cs], kc * 64, c.t0 + tap - p.pad, c.b);
                         continue;
                     }
-                    if (it >= kStages &&
-                        !mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, s_abort, p.err, DEV_TIMEOUT_EMPTY))
+                    if (it >= nst && !mbar_wait(&empty[cs], cph ^ 1, s_abort, p.err, DEV_TIMEOUT_EMPTY))
                         break;
-                    mbar_arrive_expect_tx(&full[s], tx_bytes);
-                    tma_load_2d(sa, &tmA, &full[s], kb * 64, c.mb * 128);
-                    tma_load_3d(sa + kABytes, &tmB, &full[s], kc * 64, c.t0 + tap - p.pad, c.b);
+                    mbar_arrive_expect_tx(&full[cs], tx_bytes);
+                    tma_load_2d(sa, &tmA, &full[cs], kb * 64, c.mb * 128);
+                    tma_load_3d(sa + kABytes, &tmB, &full[cs], kc * 64, c.t0 + tap - p.pad, c.b);
                 }
             }
             if (*s_abort) {
                 // Let the copies still in flight land before the CTA exits.
                 const int issued = it > pre ? it : pre;
-                for (int i = (issued > kStages ? issued - kStages : 0); i < issued; ++i) {
+                for (int i = (issued > nst ? issued - nst : 0); i < issued; ++i) {
                     const unsigned long long t_start = globaltimer();
-                    while (!mbar_try_wait(&full[i % kStages], (i / kStages) & 1) && globaltimer() - t_start < kWaitNs) {}
+                    while (!mbar_try_wait(&full[i % nst], (i / nst) & 1) && globaltimer() - t_start < kWaitNs) {}
                 }
             }
         }
@@ -654,6 +659,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // ---------------- MMA issuer ----------------
             const uint32_t idesc = make_idesc_f16(128, p.BN, true);
             int it = 0, lt = 0;
+            int s = 0;                 // ring slot of `it` and the parity of its fill
+            uint32_t ph = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x, ++lt) {
                 const TileCoord c = decode(p, t, nkb);
@@ -662,16 +669,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 tc_fence_after();
                 const uint32_t dacc = tmem + buf * 256;
                 for (int kb = c.kb_begin; kb < c.kb_end; ++kb, ++it) {
-                    const int s = it % kStages;
-                    if (!mbar_wait(&full[s], (it / kStages) & 1, s_abort, p.err, DEV_TIMEOUT_FULL)) { ok = false; break; }
+                    const int cs = s;
+                    if (!mbar_wait(&full[cs], ph, s_abort, p.err, DEV_TIMEOUT_FULL)) { ok = false; break; }
+                    if (++s == nst) { s = 0; ph ^= 1; }
                     tc_fence_after();
-                    const uint32_t sa = smem_u32(smem + s * kStageBytes);
+                    const uint32_t sa = smem_u32(smem + cs * sbytes);
                     const uint64_t adesc = make_sdesc_sw128(sa);
                     const uint64_t bdesc = make_sdesc_sw128(sa + kABytes);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
                         umma_f16_ss(dacc, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb > c.kb_begin || kk > 0) ? 1u : 0u);
-                    umma_commit(&empty[s]);
+                    umma_commit(&empty[cs]);
                 }
                 umma_commit(&acc_full[buf]);
             }
@@ -990,16 +998,21 @@ static int max_active_clusters(int cs) {
 // Tile / split choice from a cost model of the kernel's time in SM cycles, fitted to per-CTA
 // phase timestamps taken on B200. Small-N GEMMs here are bound by L2 -> SM operand traffic:
 // every CTA streams its weight tile (16 KB per K block of 64) and its token tile (128 B per
-// token per K block), and all CTAs together draw ~8 KB / cycle; a single SM draws ~100 B /
+// token per K block), and all CTAs together draw ~5 KB / cycle (measured on the conv / long-K
+// shapes; short linear ones reach ~7); a single SM draws ~100 B /
 // cycle, and its MMA needs 2 * BN cycles per K block. The last tile's epilogue is exposed
 // (~20 B / cycle of output). Split-K trades a reduction for parallelism: within one wave the
 // splits of a tile form a cluster and reduce through distributed shared memory (~2000 cycles
 // + the slice rows); beyond one wave they reduce through the global workspace, whose last-
 // arriving CTA was measured at ~40000 cycles.
-static void choose_tiles(int S, int nbatch, int mblocks, int nkb, int num_sms, int max_splits, long long ws_floats,
-                         int n_counters, bool allow_cluster, int & BN, int & n_tiles, int & splits) {
-    double best = 1e30;
-    BN = 16; n_tiles = (S + 15) / 16; splits = 1;
+struct TileChoice {
+    double cost;
+    int BN, splits;
+};
+// Every feasible (BN, splits), cheapest first by the model.
+static std::vector<TileChoice> tile_choices(int S, int nbatch, int mblocks, int nkb, int num_sms, int max_splits,
+                                            long long ws_floats, int n_counters, bool allow_cluster) {
+    std::vector<TileChoice> out;
     for (int bn = 16; bn <= 256; bn += 16) {
         const int nt = (S + bn - 1) / bn;
         if (nt > 1 && ((S + nt - 1) / nt + 15) / 16 * 16 < bn) continue;   // a smaller bn gives the same count
@@ -1011,7 +1024,7 @@ static void choose_tiles(int S, int nbatch, int mblocks, int nkb, int num_sms, i
             if (cluster) {   // partial tile + receive slots fit the operand stages; clusters co-resident
                 const int rows_max = 16 * (((bn >> 4) + sp - 1) / sp);
                 const int mac = max_active_clusters(sp);
-                cluster = (long long)bn * 512 + (long long)(sp - 1) * rows_max * 512 <= (long long)kStages * kStageBytes &&
+                cluster = (long long)bn * 512 + (long long)(sp - 1) * rows_max * 512 <= (long long)kStageArea &&
                           mac > 0 && otiles <= mac;
             }
             if (sp > 1 && !cluster && (otiles > n_counters || otiles * sp * bn * 128 > ws_floats)) continue;
@@ -1020,13 +1033,30 @@ static void choose_tiles(int S, int nbatch, int mblocks, int nkb, int num_sms, i
             const double tile_bytes = kb * (16384.0 + 128.0 * bn);
             const long long wave_tiles = std::min<long long>(tiles, num_sms);
             const double t_sm = kb * 2.0 * bn + tile_bytes / 100.0;
-            const double t_l2 = (double)wave_tiles * tile_bytes / 8000.0;
+            const double t_l2 = (double)wave_tiles * tile_bytes / 5000.0;
             const double epi = bn * 128.0 * 4.0 / 20.0;
             const double reduce = sp == 1 ? 0.0 : cluster ? 2000.0 + bn * 512.0 * 2.0 / 100.0 : 40000.0;
             const double cost = (double)waves * (std::max(t_sm, t_l2) + 3000.0) + epi + reduce;
-            if (cost < best - 1e-9) { best = cost; BN = bn; n_tiles = nt; splits = sp; }
+            out.push_back({cost, bn, sp});
         }
     }
+    std::stable_sort(out.begin(), out.end(), [](const TileChoice & a, const TileChoice & b) { return a.cost < b.cost; });
+    return out;
+}
+
+int gemm_candidates(int M, int K_in, int taps, int nbatch, int S, int num_sms, int max_splits, long long ws_floats,
+                    int n_counters, bool allow_cluster, int max_out, int * bn, int * splits) {
+    if (M % 128 || K_in % 64 || taps < 1 || S < 1 || nbatch < 1) return 0;
+    const auto c = tile_choices(S, nbatch, M / 128, taps * (K_in / 64), num_sms, max_splits, ws_floats, n_counters,
+                                allow_cluster);
+    int n = 0;
+    for (const TileChoice & t : c) {
+        if (n >= max_out) break;
+        bn[n] = t.BN;
+        splits[n] = t.splits;
+        ++n;
+    }
+    return n;
 }
 
 long long gemm_ws_floats(const GemmLaunch & L) {
@@ -1036,7 +1066,7 @@ long long gemm_ws_floats(const GemmLaunch & L) {
 
 bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pad, int swiglu, const void * X,
                int nbatch, int S, long long x_row_stride, long long x_batch_stride, int num_sms, int max_splits,
-               long long ws_floats, int n_counters, bool allow_cluster) {
+               long long ws_floats, int n_counters, bool allow_cluster, int force_bn, int force_splits) {
     if (M % 128 || K_in % 64 || taps < 1 || S < 1 || nbatch < 1) return false;
     GemmParams & p = L.p;
     p = GemmParams{};
@@ -1045,8 +1075,24 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
     p.mblocks = M / 128;
     p.gate_div = 1;
     const int nkb = taps * (K_in / 64);
-    choose_tiles(S, nbatch, p.mblocks, nkb, num_sms, max_splits, ws_floats, n_counters, allow_cluster, p.BN,
-                 p.n_tiles, p.splits);
+    {
+        // the model's best choice, or the requested one if it is among the feasible choices
+        const auto c = tile_choices(S, nbatch, p.mblocks, nkb, num_sms, max_splits, ws_floats, n_counters, allow_cluster);
+        if (c.empty()) return false;
+        TileChoice t = c[0];
+        for (const TileChoice & x : c)
+            if (force_bn > 0 && x.BN == force_bn && x.splits == force_splits) t = x;
+        p.BN = t.BN;
+        p.n_tiles = (S + t.BN - 1) / t.BN;
+        p.splits = t.splits;
+        p.stages = std::min(kMaxStages, kStageArea / (kABytes + p.BN * 128));
+    }
+    if (getenv("TSD_DEBUG_PLAN")) {
+        fprintf(stderr, "tsd plan: M=%d K=%d taps=%d nbatch=%d S=%d -> BN=%d tiles/item=%d splits=%d | max active clusters",
+                M, K_in, taps, nbatch, S, p.BN, p.n_tiles, p.splits);
+        for (int k = 2; k <= 8; ++k) fprintf(stderr, " %d:%d", k, max_active_clusters(k));
+        fprintf(stderr, "\n");
+    }
     p.m_valid = swiglu ? M / 2 : M;
     {
         const char * o = getenv("TSD_TILE_ORDER");
@@ -1060,7 +1106,7 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
         const int mac = p.splits > 1 ? max_active_clusters(p.splits) : 0;
         p.csplit = allow_cluster && p.splits > 1 && tiles <= num_sms && mac > 0 &&
                    (long long)p.mblocks * nbatch * p.n_tiles <= mac &&
-                   (long long)p.BN * 512 + (long long)(p.splits - 1) * rows_max * 512 <= (long long)kStages * kStageBytes;
+                   (long long)p.BN * 512 + (long long)(p.splits - 1) * rows_max * 512 <= (long long)kStageArea;
     }
     if (p.csplit) p.order = 0;
     L.grid = dim3((unsigned)std::min<long long>(tiles, num_sms), 1, 1);

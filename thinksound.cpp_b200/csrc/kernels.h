@@ -34,6 +34,7 @@ struct GemmParams {
     int BN;            // token tile (multiple of 16, <= 256)
     int n_tiles;       // ceil(S / BN)
     int splits;        // split-K factor
+    int stages;        // operand ring depth (set by gemm_plan from BN)
     int mode, act;
     int m_valid;       // features >= m_valid are not stored (zero-padded weight rows)
     const float * bias;
@@ -82,7 +83,12 @@ bool make_tmap_3d(CUtensorMap * m, const void * ptr, CUtensorMapDataType dt, int
 // kernel leaves them zero).
 bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pad, int swiglu,
                const void * X, int nbatch, int S, long long x_row_stride, long long x_batch_stride,
-               int num_sms, int max_splits, long long ws_floats = 0, int n_counters = 0, bool allow_cluster = true);
+               int num_sms, int max_splits, long long ws_floats = 0, int n_counters = 0, bool allow_cluster = true,
+               int force_bn = 0, int force_splits = 0);
+// Up to max_out feasible (token tile, K splits) choices for a GEMM shape, best first by the cost
+// model; force_bn / force_splits in gemm_plan select one of them (plan-time autotuning).
+int gemm_candidates(int M, int K_in, int taps, int nbatch, int S, int num_sms, int max_splits, long long ws_floats,
+                    int n_counters, bool allow_cluster, int max_out, int * bn, int * splits);
 // Workspace floats a planned launch needs (0 when it does not split K).
 long long gemm_ws_floats(const GemmLaunch & L);
 // After the epilogue fields of L.p are set: encode the epilogue tensor maps (TMA stores where the
