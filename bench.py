@@ -29,6 +29,9 @@ sys.path.insert(0, REPO)
 CFG3 = dict(T=194, clip_S=72, sync_S=216, text_S=77, t5_S=128)
 HP3 = dict(hidden=1536, n_head=24, depth=21, fused_depth=14)
 METRIC = "DiT flow-steps/s at 9 s, CFG=2, BF16 (MM-DiT attn+proj TFLOP/s in roofline)"
+# ncu: dram__bytes_read.sum + dram__bytes_write.sum over the 36 GEMM launches of one forward of the
+# 2 joint + 1 fused block model at the cfg-3 shapes (1.2568 GB for 388.4 GFLOP, cold cache)
+GEMM_DRAM_BYTES_PER_FLOP = 0.0032358
 UNIT = "pair-steps/s"
 
 
@@ -406,11 +409,9 @@ def main():
                 cpu = {k: c[k] for k in ("value", "unit", "cores", "kind", "sample")}
             except Exception as ex:  # report, do not hide
                 cpu = {"value": None, "unit": UNIT, "cores": None, "kind": "port", "sample": f"failed: {ex}"}
-        traffic = None
-        tp = os.path.join(REPO, "profiles", "gemm_traffic.json")
-        if os.path.exists(tp):
-            traffic = json.load(open(tp)).get("dram_bytes_per_gemm_flop")
-            traffic = traffic * (g_fl / max(1, g_n)) if traffic else None
+        # DRAM bytes per GEMM launch: the ratio measured by ncu over all GEMM launches of one
+        # forward with the same shapes (profiles/gemm_tc_cfg3_b2.md), times an average launch's FLOPs
+        traffic = GEMM_DRAM_BYTES_PER_FLOP * (g_fl / max(1, g_n))
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
