@@ -89,6 +89,21 @@ def test_forward_weight_types(wtype, tol):
     assert oracle.rel_l2(flow[0], om.forward(items[0], mode=oracle.MODE_EXACT)) < tol
 
 
+@pytest.mark.parametrize("hidden,heads", [(128, 2), (256, 4)])
+def test_q8_gemm_dequantises_in_kernel_bit_identically(monkeypatch, hidden, heads):
+    """Planar Q8_0 projections are dequantised in shared memory by the GEMM's converter warps
+    (w = q * scale rounded to bf16); the result must equal the load-time bf16 widening exactly."""
+    hp = synth.DitHParams(hidden=hidden, n_head=heads, depth=3, fused_depth=1, ffn=2 * hidden)
+    W = synth.make_weights(hp, seed=31, wtype="q8_0")
+    items = synth.make_inputs(hp, seed=6, batch=2, **SHAPE)
+    monkeypatch.setenv("TSD_Q8_IN_KERNEL", "1")
+    in_kernel = tsd.DitModel.from_weights(hp, W).forward(items)
+    monkeypatch.delenv("TSD_Q8_IN_KERNEL")
+    at_load = tsd.DitModel.from_weights(hp, W).forward(items)
+    assert np.isfinite(in_kernel).all()
+    assert np.array_equal(in_kernel, at_load)
+
+
 def test_forward_from_gguf_equals_from_weights(tmp_path, small_bf16):
     hp, W, m, _ = small_bf16
     path = str(tmp_path / "dit.gguf")

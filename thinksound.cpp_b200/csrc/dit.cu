@@ -111,8 +111,9 @@ struct Builder {
             force_bn = hit->second.first;
             force_sp = hit->second.second;
         }
-        if (!gemm_plan(L, w.w, M, w.K_in, w.taps, w.pad, swiglu, X, nbatch, S, xrs, xbs, m.num_sms, max_splits,
-                       kWsFloats, kCounters, true, force_bn, force_sp)) {
+        const void * Wp = w.q ? static_cast<const void *>(w.q) : static_cast<const void *>(w.w);
+        if (!gemm_plan(L, Wp, M, w.K_in, w.taps, w.pad, swiglu, X, nbatch, S, xrs, xbs, m.num_sms, max_splits,
+                       kWsFloats, kCounters, true, force_bn, force_sp, w.qs)) {
             fprintf(stderr, "tsd: gemm plan failed (M %d K %d taps %d S %d)\n", M, w.K_in, w.taps, S);
             rc = TSD_ERR_ARG;
             return;
@@ -142,14 +143,16 @@ struct Builder {
                                   w.K_in, w.taps, nbatch, S, mode, L.p.BN, L.p.splits, best * 1000.f);
             for (int i = 1; i < nc; ++i) {
                 GemmLaunch C = L;
-                if (!gemm_plan(C, w.w, M, w.K_in, w.taps, w.pad, swiglu, X, nbatch, S, xrs, xbs, m.num_sms, max_splits,
-                               kWsFloats, kCounters, true, bns[i], sps[i]))
+                if (!gemm_plan(C, Wp, M, w.K_in, w.taps, w.pad, swiglu, X, nbatch, S, xrs, xbs, m.num_sms, max_splits,
+                               kWsFloats, kCounters, true, bns[i], sps[i], w.qs))
                     continue;
                 const GemmParams & q = L.p;   // same epilogue, new tiling
                 GemmParams & cp = C.p;
                 const int BN = cp.BN, nt = cp.n_tiles, sp = cp.splits, cs = cp.csplit, order = cp.order, st = cp.stages;
+                const int aq8 = cp.a_q8;
                 cp = q;
                 cp.BN = BN; cp.n_tiles = nt; cp.splits = sp; cp.csplit = cs; cp.order = order; cp.stages = st;
+                cp.a_q8 = aq8;
                 gemm_finalize(C);
                 const float t = time_gemm(C);
                 if (tune_log) fprintf(stderr, " | BN=%d sp=%d %.1f us", BN, sp, t * 1000.f);
@@ -160,11 +163,13 @@ struct Builder {
         }
         const double n_tok = (double)nbatch * S, kdim = (double)w.taps * w.K_in;
         const double flops = 2.0 * (swiglu ? 2 * p.m_valid : p.m_valid) * n_tok * kdim;
-        const double bytes = 2.0 * M * kdim + 2.0 * n_tok * w.K_in + n_tok * (mode == EPI_GATE_RESID ? 12.0 : (out_bf16 ? 2.0 : 4.0)) * p.m_valid;
+        const double bytes = (w.q ? 34.0 / 32.0 : 2.0) * M * kdim + 2.0 * n_tok * w.K_in +
+                             n_tok * (mode == EPI_GATE_RESID ? 12.0 : (out_bf16 ? 2.0 : 4.0)) * p.m_valid;
         op([L](cudaStream_t st) { return gemm_launch(L, st); }, OP_GEMM, flops, bytes);
         char buf[160];
-        snprintf(buf, sizeof buf, " M=%d N=%d K=%d taps=%d BN=%d grid=%ux%ux%u mode=%d%s", p.m_valid, nbatch * S,
-                 w.taps * w.K_in, w.taps, p.BN, L.grid.x, L.grid.y, L.grid.z, mode, p.epi_tma ? " tma" : "");
+        snprintf(buf, sizeof buf, " M=%d N=%d K=%d taps=%d BN=%d grid=%ux%ux%u mode=%d%s%s", p.m_valid, nbatch * S,
+                 w.taps * w.K_in, w.taps, p.BN, L.grid.x, L.grid.y, L.grid.z, mode, p.epi_tma ? " tma" : "",
+                 p.a_q8 ? " q8" : "");
         P.ops.back().label += buf;
     }
     // QKV projection whose epilogue applies the per-head RMSNorm (Q, K) and RoPE (rope != null)
@@ -187,12 +192,13 @@ struct Builder {
     void gemv(const VW & w, const float * x, long long ldx, int N, int act, float * y, long long ldy, int y_bf16 = 0) {
         if (rc) return;
         const VW wc = w;
-        op([wc, x, ldx, N, act, y, ldy, y_bf16](cudaStream_t st) {
+        int * const err = m.d_err;
+        op([wc, x, ldx, N, act, y, ldy, y_bf16, err](cudaStream_t st) {
             for (int n0 = 0; n0 < N; n0 += 8) {
                 const int nn = std::min(8, N - n0);
                 cudaError_t e = gemv_launch(wc.w, wc.type, wc.w2, wc.M, wc.K, x + n0 * ldx, ldx, nn, wc.bias, act,
                                             wc.type == GT_BF16, y_bf16 ? (void *)((__nv_bfloat16 *)y + n0 * ldy) : (void *)(y + n0 * ldy),
-                                            y_bf16, ldy, st);
+                                            y_bf16, ldy, st, err);
                 if (e != cudaSuccess) return e;
             }
             return cudaSuccess;

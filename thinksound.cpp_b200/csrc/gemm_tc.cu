@@ -32,6 +32,8 @@ constexpr int kMaxStages = 8;              // operand ring depth: as many stages
 constexpr int kStageArea = 4 * (128 * 128 + 256 * 128);   // 192 KB: 4 stages at BN = 256
 constexpr int kABytes = 128 * 128;          // 128 rows x 64 bf16
 constexpr int kTmemCols = 512;              // two 256-column fp32 accumulators
+constexpr int kQ8Bytes = 9216;             // Q8_0 A path, per stage: int8 tile 128 x 64 + scales 2 x 128 f16 (padded)
+constexpr int kThreads = 256;              // warps: 0 TMA, 1 MMA, 2-5 epilogue, 6-7 Q8_0 converters
 constexpr int kEBufBytes = 16384;          // epilogue staging buffer (x2): 32 tokens x 128 f32
 constexpr int kSmemBytes = kStageArea + 2 * kEBufBytes + 1024 /*align*/ + 256 /*barriers*/;
 
@@ -552,10 +554,10 @@ __device__ __forceinline__ void finish_slice(const GemmParams & p, const CUtenso
 }
 
 template <int EK>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmG,
-               const __grid_constant__ CUtensorMap tmV, const GemmParams p) {
+               const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmS, const GemmParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t * ebuf = smem + kStageArea;                       // epilogue staging [2][kEBufBytes]
@@ -566,7 +568,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint64_t * ebar = acc_empty + 2;           // [2] residual / gate tile loads (GATE_RESID, TMA epilogue)
     uint64_t * cbar = ebar + 2;                // [3] cluster split-K: slice rows received / own copies
                                                //     landed at the peers / peers ready to receive
-    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(cbar + 3);
+    uint64_t * rfull = cbar + 3;               // [kMaxStages] Q8_0: raw int8 tile + scales landed
+    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(rfull + kMaxStages);
     volatile int * s_abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
     volatile int * s_last = s_abort + 1;       // split-K: this CTA reduces the tile
 
@@ -574,12 +577,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int kpt = p.K_in >> 6;
     const int nkb = p.taps * kpt;
     const int num_tiles = p.mblocks * p.nbatch * p.n_tiles * p.splits;
-    const uint32_t tx_bytes = (uint32_t)(kABytes + p.BN * 128);
-    const int sbytes = kABytes + p.BN * 128;    // one stage (multiple of 1024: SW128 atoms stay aligned)
+    // one stage: A bf16 (SW128) | B bf16 (SW128) | Q8_0 path: int8 tile + scales; a multiple of
+    // 1024 bytes, so every stage's SW128 atoms stay aligned
+    const int sbytes = kABytes + p.BN * 128 + (p.a_q8 ? kQ8Bytes : 0);
+    const uint32_t b_bytes = (uint32_t)(p.BN * 128);
     const int nst = p.stages;                   // ring depth, <= kMaxStages, nst * sbytes <= kStageArea
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kMaxStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        // full: the producer's expect_tx (+ both converter warps' arrivals on the Q8_0 path)
+        for (int s = 0; s < kMaxStages; ++s) {
+            mbar_init(&full[s], p.a_q8 ? 3 : 1); mbar_init(&empty[s], 1); mbar_init(&rfull[s], 1);
+        }
         for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 4); mbar_init(&ebar[s], 1); }
         mbar_init(&cbar[0], 1);
         for (int s = 1; s < 3; ++s) mbar_init(&cbar[s], p.csplit ? p.splits - 1 : 1);
@@ -614,13 +622,29 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // ---------------- TMA producer ----------------
             // Weight tiles of the first stages do not depend on earlier kernels: request them
             // before waiting for the predecessor grid; their activation tiles follow the wait.
+            // bf16 weights land in the stage's A slot (on `full`, with the activation tile);
+            // Q8_0 weights land as int8 + scales (on `rfull`) for the converter warps.
+            const auto issue_a = [&](int st, int kb, const TileCoord & c) {
+                uint8_t * sa = smem + st * sbytes;
+                if (p.a_q8) {
+                    uint8_t * raw = sa + kABytes + p.BN * 128;
+                    mbar_arrive_expect_tx(&rfull[st], 128 * 64 + 2 * 128 * 2);
+                    tma_load_2d(raw, &tmA, &rfull[st], kb * 64, c.mb * 128);
+                    tma_load_2d(raw + 128 * 64, &tmS, &rfull[st], c.mb * 128, kb * 2);
+                } else {
+                    mbar_arrive_expect_tx(&full[st], kABytes + b_bytes);
+                    tma_load_2d(sa, &tmA, &full[st], kb * 64, c.mb * 128);
+                }
+            };
+            const auto issue_b = [&](int st, int kb, const TileCoord & c) {
+                const int tap = kb / kpt, kc = kb - tap * kpt;
+                if (p.a_q8) mbar_arrive_expect_tx(&full[st], b_bytes);
+                tma_load_3d(smem + st * sbytes + kABytes, &tmB, &full[st], kc * 64, c.t0 + tap - p.pad, c.b);
+            };
             int pre = 0;
             for (int t = blockIdx.x; t < num_tiles && pre < nst; t += gridDim.x) {
                 const TileCoord c = decode(p, t, nkb);
-                for (int kb = c.kb_begin; kb < c.kb_end && pre < nst; ++kb, ++pre) {
-                    mbar_arrive_expect_tx(&full[pre], tx_bytes);
-                    tma_load_2d(smem + pre * sbytes, &tmA, &full[pre], kb * 64, c.mb * 128);
-                }
+                for (int kb = c.kb_begin; kb < c.kb_end && pre < nst; ++kb, ++pre) issue_a(pre, kb, c);
             }
             pdl_wait();
             int it = 0;
@@ -629,28 +653,26 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             for (int t = blockIdx.x; t < num_tiles && !*s_abort; t += gridDim.x) {
                 const TileCoord c = decode(p, t, nkb);
                 for (int kb = c.kb_begin; kb < c.kb_end; ++kb, ++it) {
-                    uint8_t * sa = smem + s * sbytes;
                     const int cs = s;
                     const uint32_t cph = ph;
                     if (++s == nst) { s = 0; ph ^= 1; }
-                    const int tap = kb / kpt, kc = kb - tap * kpt;
                     if (it < pre) {       // A already requested
-                        tma_load_3d(sa + kABytes, &tmB, &full[cs], kc * 64, c.t0 + tap - p.pad, c.b);
+                        issue_b(cs, kb, c);
                         continue;
                     }
                     if (it >= nst && !mbar_wait(&empty[cs], cph ^ 1, s_abort, p.err, DEV_TIMEOUT_EMPTY))
                         break;
-                    mbar_arrive_expect_tx(&full[cs], tx_bytes);
-                    tma_load_2d(sa, &tmA, &full[cs], kb * 64, c.mb * 128);
-                    tma_load_3d(sa + kABytes, &tmB, &full[cs], kc * 64, c.t0 + tap - p.pad, c.b);
+                    issue_a(cs, kb, c);
+                    issue_b(cs, kb, c);
                 }
             }
             if (*s_abort) {
-                // Let the copies still in flight land before the CTA exits.
+                // Let the copies still in flight land before the CTA exits (one deadline for all).
                 const int issued = it > pre ? it : pre;
+                const unsigned long long t_start = globaltimer();
                 for (int i = (issued > nst ? issued - nst : 0); i < issued; ++i) {
-                    const unsigned long long t_start = globaltimer();
-                    while (!mbar_try_wait(&full[i % nst], (i / nst) & 1) && globaltimer() - t_start < kWaitNs) {}
+                    uint64_t * bar = p.a_q8 ? &rfull[i % nst] : &full[i % nst];
+                    while (!mbar_try_wait(bar, (i / nst) & 1) && globaltimer() - t_start < kWaitNs) {}
                 }
             }
         }
@@ -682,6 +704,60 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     umma_commit(&empty[cs]);
                 }
                 umma_commit(&acc_full[buf]);
+            }
+        }
+    } else if (warp >= 6) {
+        // ---------------- Q8_0 converters (warps 6, 7) ----------------
+        // Each stage's int8 tile (128 rows x 64, row-major) and its scales ([2 blocks][128 rows]
+        // f16) become the bf16 A tile in the 128-byte-swizzled layout TMA would have written:
+        // 16-byte chunk j of row r at r * 128 + ((j ^ (r & 7)) << 4). w = (float)q * scale,
+        // rounded to bf16 (the load-time conversion's arithmetic). Thread t: rows t and t + 64.
+        if (p.a_q8) {
+            const int t64 = (warp - 6) * 32 + lane;
+            int s = 0;
+            uint32_t ph = 0;
+            for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+                const TileCoord c = decode(p, t, nkb);
+                bool ok = true;
+                for (int kb = c.kb_begin; kb < c.kb_end; ++kb) {
+                    if (!mbar_wait(&rfull[s], ph, s_abort, p.err, DEV_TIMEOUT_FULL)) { ok = false; break; }
+                    uint8_t * sa = smem + s * sbytes;
+                    const uint8_t * raw = sa + kABytes + p.BN * 128;
+                    const __half * sc = reinterpret_cast<const __half *>(raw + 128 * 64);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int r = t64 + 64 * h;
+                        const float d0 = __half2float(sc[r]), d1 = __half2float(sc[128 + r]);
+                        const uint4 * qr = reinterpret_cast<const uint4 *>(raw + r * 64);
+#pragma unroll
+                        for (int jj = 0; jj < 4; ++jj) {              // 16 int8 -> two 8-weight chunks
+                            const uint4 u = qr[jj];
+                            const float d = jj < 2 ? d0 : d1;
+                            const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+                            uint32_t o[8];
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                const uint32_t word = w4[i >> 1];
+                                const int sh = (i & 1) * 16;
+                                const float lo = (float)(int8_t)((word >> sh) & 0xffu) * d;
+                                const float hi = (float)(int8_t)((word >> (sh + 8)) & 0xffu) * d;
+                                const __nv_bfloat162 bb = __floats2bfloat162_rn(lo, hi);
+                                o[i] = *reinterpret_cast<const uint32_t *>(&bb);
+                            }
+#pragma unroll
+                            for (int half = 0; half < 2; ++half) {
+                                const int j = jj * 2 + half;
+                                *reinterpret_cast<uint4 *>(sa + r * 128 + ((j ^ (r & 7)) << 4)) =
+                                    make_uint4(o[4 * half], o[4 * half + 1], o[4 * half + 2], o[4 * half + 3]);
+                            }
+                        }
+                    }
+                    fence_proxy_async_smem();       // the MMA reads the tile through the async proxy
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&full[s]);
+                    if (++s == nst) { s = 0; ph ^= 1; }
+                }
+                if (!ok) break;
             }
         }
     } else {
@@ -977,7 +1053,7 @@ static int max_active_clusters(int cs) {
         for (int k = 1; k <= 8; ++k) {
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3((unsigned)(k * (sms / k)), 1, 1);
-            cfg.blockDim = dim3(192, 1, 1);
+            cfg.blockDim = dim3(kThreads, 1, 1);
             cfg.dynamicSmemBytes = kSmemBytes;
             cudaLaunchAttribute at[1];
             at[0].id = cudaLaunchAttributeClusterDimension;
@@ -1066,8 +1142,10 @@ long long gemm_ws_floats(const GemmLaunch & L) {
 
 bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pad, int swiglu, const void * X,
                int nbatch, int S, long long x_row_stride, long long x_batch_stride, int num_sms, int max_splits,
-               long long ws_floats, int n_counters, bool allow_cluster, int force_bn, int force_splits) {
+               long long ws_floats, int n_counters, bool allow_cluster, int force_bn, int force_splits,
+               const void * q8_scales) {
     if (M % 128 || K_in % 64 || taps < 1 || S < 1 || nbatch < 1) return false;
+    if (q8_scales && taps != 1) return false;
     GemmParams & p = L.p;
     p = GemmParams{};
     L.finalized = false;
@@ -1085,7 +1163,8 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
         p.BN = t.BN;
         p.n_tiles = (S + t.BN - 1) / t.BN;
         p.splits = t.splits;
-        p.stages = std::min(kMaxStages, kStageArea / (kABytes + p.BN * 128));
+        p.a_q8 = q8_scales != nullptr;
+        p.stages = std::min(kMaxStages, kStageArea / (kABytes + p.BN * 128 + (p.a_q8 ? kQ8Bytes : 0)));
     }
     if (getenv("TSD_DEBUG_PLAN")) {
         fprintf(stderr, "tsd plan: M=%d K=%d taps=%d nbatch=%d S=%d -> BN=%d tiles/item=%d splits=%d | max active clusters",
@@ -1110,8 +1189,15 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
     }
     if (p.csplit) p.order = 0;
     L.grid = dim3((unsigned)std::min<long long>(tiles, num_sms), 1, 1);
-    if (!make_tmap_2d(&L.tmA, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)taps * K_in, (uint64_t)M,
-                      (uint64_t)taps * K_in * 2, 64, 128))
+    if (q8_scales) {
+        // int8 plane: 64 x 128 boxes (64-byte rows, no swizzle); scales: 128 rows x 2 blocks
+        if (!make_tmap_2d(&L.tmA, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K_in, (uint64_t)M, (uint64_t)K_in, 64,
+                          128) ||
+            !make_tmap_2d(&L.tmS, q8_scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)M, (uint64_t)K_in / 32,
+                          (uint64_t)M * 2, 128, 2))
+            return false;
+    } else if (!make_tmap_2d(&L.tmA, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)taps * K_in, (uint64_t)M,
+                             (uint64_t)taps * K_in * 2, 64, 128))
         return false;
     if (!make_tmap_3d(&L.tmB, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K_in, (uint64_t)S, (uint64_t)nbatch,
                       (uint64_t)x_row_stride * 2, (uint64_t)x_batch_stride * 2, 64, p.BN, 1))
@@ -1195,7 +1281,7 @@ template <int EK> cudaError_t launch_kind(cudaLaunchConfig_t & cfg, const GemmLa
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<EK>, L.tmA, L.tmB, L.tmO, L.tmG, L.tmV, p);
+    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<EK>, L.tmA, L.tmB, L.tmO, L.tmG, L.tmV, L.tmS, p);
 }
 }  // namespace
 
@@ -1206,7 +1292,7 @@ cudaError_t gemm_launch(const GemmLaunch & L0, cudaStream_t st) {
     const GemmParams & p = L.p;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = L.grid;
-    cfg.blockDim = dim3(192, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = kSmemBytes;
     cfg.stream = st;
     cudaLaunchAttribute at[2];

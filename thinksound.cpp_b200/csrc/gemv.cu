@@ -110,7 +110,7 @@ cudaError_t launch_wt(const void * W, const void * W2, int M, int K, const float
 
 cudaError_t gemv_launch(const void * W, int wtype, const void * W2, int M, int K, const float * x, long long ldx, int N,
                         const float * bias, int act, int round_bf16, void * y, int y_bf16, long long ldy,
-                        cudaStream_t st) {
+                        cudaStream_t st, int * /*err: these kernels have no waits*/) {
     if (N < 1 || N > kMaxN || K % 32 || (ldx & 3)) return cudaErrorInvalidValue;
     switch (wtype) {
         case 0: return launch_wt<0>(W, W2, M, K, x, ldx, N, bias, act, round_bf16, y, y_bf16, ldy, st);

@@ -35,6 +35,7 @@ struct GemmParams {
     int n_tiles;       // ceil(S / BN)
     int splits;        // split-K factor
     int stages;        // operand ring depth (set by gemm_plan from BN)
+    int a_q8;          // weights are planar Q8_0 (int8 [M][K] + f16 scales [K/32][M]), dequantised in smem
     int mode, act;
     int m_valid;       // features >= m_valid are not stored (zero-padded weight rows)
     const float * bias;
@@ -60,6 +61,7 @@ struct GemmLaunch {
     CUtensorMap tmA, tmB;   // weights, activations
     CUtensorMap tmO, tmG;   // epilogue: output (GATE_RESID: residual) and per-token gate tiles
     CUtensorMap tmV;        // EPI_QKV: tmO / tmG / tmV = the stream's Q / K / V rows
+    CUtensorMap tmS;        // planar Q8_0 weights: the scale plane (tmA then maps the int8 plane)
     GemmParams p;
     dim3 grid;          // persistent: min(tiles, SMs) CTAs
     bool finalized = false;
@@ -75,7 +77,9 @@ bool make_tmap_3d(CUtensorMap * m, const void * ptr, CUtensorMapDataType dt, int
                   uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
                   uint32_t b0, uint32_t b1, uint32_t b2);
 
-// Fill `L` for a GEMM; returns false on unsupported arguments. swiglu: W rows alternate w1 / w3
+// Fill `L` for a GEMM; returns false on unsupported arguments. W: bf16 [M][taps*K_in], or with
+// q8_scales, the int8 plane of planar Q8_0 weights (taps == 1) and q8_scales = [K_in/32][M] f16.
+// swiglu: W rows alternate w1 / w3
 // (row 2f = w1 of feature f, row 2f + 1 = w3 of f) and the output has M / 2 features. Split-K (max_splits > 1) is
 // reduces through the cluster's shared memory when the split tiles fit one wave (unless
 // allow_cluster is false), else through a global workspace, used only if ws_floats / n_counters
@@ -84,7 +88,7 @@ bool make_tmap_3d(CUtensorMap * m, const void * ptr, CUtensorMapDataType dt, int
 bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pad, int swiglu,
                const void * X, int nbatch, int S, long long x_row_stride, long long x_batch_stride,
                int num_sms, int max_splits, long long ws_floats = 0, int n_counters = 0, bool allow_cluster = true,
-               int force_bn = 0, int force_splits = 0);
+               int force_bn = 0, int force_splits = 0, const void * q8_scales = nullptr);
 // Up to max_out feasible (token tile, K splits) choices for a GEMM shape, best first by the cost
 // model; force_bn / force_splits in gemm_plan select one of them (plan-time autotuning).
 int gemm_candidates(int M, int K_in, int taps, int nbatch, int S, int num_sms, int max_splits, long long ws_floats,
@@ -104,7 +108,7 @@ cudaError_t gemm_launch(const GemmLaunch & L, cudaStream_t st);
 // ---------------------------------------------------------------------------------------------
 cudaError_t gemv_launch(const void * W, int wtype, const void * W2, int M, int K, const float * x,
                         long long ldx, int N, const float * bias, int act, int round_bf16,
-                        void * y, int y_bf16, long long ldy, cudaStream_t st);
+                        void * y, int y_bf16, long long ldy, cudaStream_t st, int * err = nullptr);
 
 // ---------------------------------------------------------------------------------------------
 // Attention (tcgen05): O = softmax(Q K^T * scale) V per (batch, head); Q, K, V fp16

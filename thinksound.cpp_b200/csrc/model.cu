@@ -15,6 +15,8 @@
 // their stored type for the weight-streaming GEMV.
 #include "runtime.h"
 
+#include <initializer_list>
+
 #include <cstring>
 #include <fstream>
 
@@ -59,6 +61,27 @@ __global__ void repack_kernel(__nv_bfloat16 * dst, long long dst_ld, const int *
     float v = 0.f;
     if (sr >= 0) v = load_elem(src, src_type, (long long)sr * kt + (long long)ic * taps + tap);
     dst[(long long)r * dst_ld + kk] = __float2bfloat16_rn(v);
+}
+
+// Q8_0 rows -> the GEMM's planar form: q[r][k] = quant of source row rowmap[r], qs[k/32][r] = its
+// block scale (rowmap -1: zero row, -2: untouched). One thread per (row, 32-block).
+__global__ void repack_q8_kernel(int8_t * q, __half * qs, long long qs_ld, const int * rowmap, int rows,
+                                 const uint8_t * src, int K) {
+    const int nb = K / 32;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)rows * nb) return;
+    const int r = (int)(i / nb), b = (int)(i - (long long)r * nb);
+    const int sr = rowmap ? rowmap[r] : r;
+    if (sr == -2) return;
+    int8_t * dq = q + (long long)r * K + b * 32;
+    if (sr < 0) {
+        for (int e = 0; e < 32; ++e) dq[e] = 0;
+        qs[(long long)b * qs_ld + r] = __float2half(0.f);
+        return;
+    }
+    const uint8_t * blk = src + ((long long)sr * nb + b) * 34;
+    for (int e = 0; e < 32; ++e) dq[e] = (int8_t)blk[2 + e];
+    qs[(long long)b * qs_ld + r] = *reinterpret_cast<const __half *>(blk);
 }
 
 __global__ void to_f32_kernel(const void * src, int type, long long n, float * dst) {
@@ -138,6 +161,36 @@ struct Finalizer {
         if (!d || cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) { rc = TSD_ERR_CUDA; return nullptr; }
         return d;
     }
+    // Planar Q8_0 for the GEMM (TSD_Q8_IN_KERNEL=1) when every source is Q8_0 with one tap (the
+    // reference quantises only 2-D weights; convolution weights stay F32): the weights stay resident
+    // at 34 bytes per 32 and the GEMM's converter warps dequantise each tile in shared memory.
+    // Default: widen to bf16 at load (the converter warps cannot keep up with the tensor core, so
+    // the in-kernel path trades speed for 47% less weight memory; results are identical).
+    bool q8_gemm(std::initializer_list<const RawTensor *> ts, int taps, int K_in) {
+        const char * e = getenv("TSD_Q8_IN_KERNEL");
+        if (!(e && *e == '1') || taps != 1 || K_in % 64) return false;
+        for (const RawTensor * t : ts)
+            if (!t || t->type != GT_Q8_0) return false;
+        return true;
+    }
+    bool alloc_q8(GW & g, long long rows, int K) {
+        g.q = reinterpret_cast<int8_t *>(m.dalloc((size_t)rows * K));
+        g.qs = reinterpret_cast<__half *>(m.dalloc((size_t)rows * (K / 32) * 2));
+        if (!g.q || !g.qs) { rc = TSD_ERR_CUDA; return false; }
+        return true;
+    }
+    bool repack_q8(int8_t * q, __half * qs, long long qs_ld, const std::vector<int> & rowmap, const RawTensor * t, int K) {
+        int * dmap = nullptr;
+        if (cudaMalloc(&dmap, rowmap.size() * 4) != cudaSuccess) { rc = TSD_ERR_CUDA; return false; }
+        cudaMemcpy(dmap, rowmap.data(), rowmap.size() * 4, cudaMemcpyHostToDevice);
+        const long long n = (long long)rowmap.size() * (K / 32);
+        repack_q8_kernel<<<(unsigned)((n + 255) / 256), 256>>>(q, qs, qs_ld, dmap, (int)rowmap.size(),
+                                                               reinterpret_cast<const uint8_t *>(t->d), K);
+        cudaError_t e = cudaDeviceSynchronize();
+        cudaFree(dmap);
+        if (e != cudaSuccess) { rc = TSD_ERR_CUDA; return false; }
+        return true;
+    }
     bool repack(__nv_bfloat16 * dst, long long dst_ld, const std::vector<int> & rowmap, const RawTensor * t, int K_in,
                 int taps) {
         int * dmap = nullptr;
@@ -160,11 +213,16 @@ struct Finalizer {
         if (taps > 1 && t->ne[0] != taps) { fprintf(stderr, "tsd: %s: kernel size %lld != %d\n", p.c_str(), (long long)t->ne[0], taps); rc = TSD_ERR_ARG; return g; }
         const int Mp = (M + 127) / 128 * 128;
         g.M = Mp; g.K_in = K_in; g.taps = taps; g.pad = pad; g.m_valid = M;
-        g.w = reinterpret_cast<__nv_bfloat16 *>(m.dalloc((size_t)Mp * taps * K_in * 2));
-        if (!g.w) { rc = TSD_ERR_CUDA; return g; }
         std::vector<int> map(Mp);
         for (int r = 0; r < Mp; ++r) map[r] = r < M ? r : -1;
-        repack(g.w, (long long)taps * K_in, map, t, K_in, taps);
+        if (q8_gemm({t}, taps, K_in)) {
+            if (!alloc_q8(g, Mp, K_in)) return g;
+            repack_q8(g.q, g.qs, Mp, map, t, K_in);
+        } else {
+            g.w = reinterpret_cast<__nv_bfloat16 *>(m.dalloc((size_t)Mp * taps * K_in * 2));
+            if (!g.w) { rc = TSD_ERR_CUDA; return g; }
+            repack(g.w, (long long)taps * K_in, map, t, K_in, taps);
+        }
         if (has_bias) g.bias = bias_f32(p + ".bias", nullptr, Mp);
         consumed.push_back(p + ".weight");
         return g;
@@ -180,9 +238,14 @@ struct Finalizer {
         for (int j = 0; j < 3; ++j)
             for (int c = 0; c < H; ++c) map[j * H + c] = 3 * c + j;
         g.M = 3 * H; g.K_in = H; g.taps = 1; g.pad = 0; g.m_valid = 3 * H;
-        g.w = reinterpret_cast<__nv_bfloat16 *>(m.dalloc((size_t)3 * H * H * 2));
-        if (!g.w) { rc = TSD_ERR_CUDA; return g; }
-        repack(g.w, H, map, t, H, 1);
+        if (q8_gemm({t}, 1, H)) {
+            if (!alloc_q8(g, 3 * H, H)) return g;
+            repack_q8(g.q, g.qs, 3 * H, map, t, H);
+        } else {
+            g.w = reinterpret_cast<__nv_bfloat16 *>(m.dalloc((size_t)3 * H * H * 2));
+            if (!g.w) { rc = TSD_ERR_CUDA; return g; }
+            repack(g.w, H, map, t, H, 1);
+        }
         g.bias = bias_f32(p + ".bias", &map);
         consumed.push_back(p + ".weight");
         return g;
@@ -197,12 +260,18 @@ struct Finalizer {
         const int K_in = (int)(taps == 1 ? t1->ne[0] : t1->ne[1]);
         if (F % 64) { fprintf(stderr, "tsd: %s: FFN width %d not a multiple of 64\n", p.c_str(), F); rc = TSD_ERR_UNSUPPORTED; return g; }
         g.M = 2 * F; g.K_in = K_in; g.taps = taps; g.pad = pad; g.m_valid = 2 * F;
-        g.w = reinterpret_cast<__nv_bfloat16 *>(m.dalloc((size_t)2 * F * taps * K_in * 2));
-        if (!g.w) { rc = TSD_ERR_CUDA; return g; }
         std::vector<int> m1(2 * F, -2), m3(2 * F, -2);
         for (int f = 0; f < F; ++f) { m1[2 * f] = f; m3[2 * f + 1] = f; }
-        repack(g.w, (long long)taps * K_in, m1, t1, K_in, taps);
-        repack(g.w, (long long)taps * K_in, m3, t3, K_in, taps);
+        if (q8_gemm({t1, t3}, taps, K_in)) {
+            if (!alloc_q8(g, 2 * F, K_in)) return g;
+            repack_q8(g.q, g.qs, 2 * F, m1, t1, K_in);
+            repack_q8(g.q, g.qs, 2 * F, m3, t3, K_in);
+        } else {
+            g.w = reinterpret_cast<__nv_bfloat16 *>(m.dalloc((size_t)2 * F * taps * K_in * 2));
+            if (!g.w) { rc = TSD_ERR_CUDA; return g; }
+            repack(g.w, (long long)taps * K_in, m1, t1, K_in, taps);
+            repack(g.w, (long long)taps * K_in, m3, t3, K_in, taps);
+        }
         consumed.push_back(p + ".w1.weight");
         consumed.push_back(p + ".w3.weight");
         return g;
@@ -341,14 +410,21 @@ struct Finalizer {
             }
         // rows is a multiple of 128 because H is.
         M.ada_lat.M = (int)rows; M.ada_lat.K_in = M.H; M.ada_lat.taps = 1; M.ada_lat.m_valid = (int)rows;
-        M.ada_lat.w = reinterpret_cast<__nv_bfloat16 *>(M.dalloc((size_t)rows * M.H * 2));
-        if (!M.ada_lat.w) { rc = TSD_ERR_CUDA; return; }
+        bool ada_q8 = !ada.empty();
+        for (const auto & a : ada) ada_q8 = ada_q8 && q8_gemm({need(a.name + ".weight")}, 1, M.H);
+        if (ada_q8) {
+            if (!alloc_q8(M.ada_lat, rows, M.H)) return;
+        } else {
+            M.ada_lat.w = reinterpret_cast<__nv_bfloat16 *>(M.dalloc((size_t)rows * M.H * 2));
+            if (!M.ada_lat.w) { rc = TSD_ERR_CUDA; return; }
+        }
         std::vector<float> hb((size_t)rows, 0.f);
         for (const auto & a : ada) {
             const RawTensor * t = need(a.name + ".weight");
             std::vector<int> map(a.rows);
             for (int r = 0; r < a.rows; ++r) map[r] = r;
-            repack(M.ada_lat.w + a.off * M.H, M.H, map, t, M.H, 1);
+            if (ada_q8) repack_q8(M.ada_lat.q + a.off * M.H, M.ada_lat.qs + a.off, rows, map, t, M.H);
+            else repack(M.ada_lat.w + a.off * M.H, M.H, map, t, M.H, 1);
             consumed.push_back(a.name + ".weight");
             const RawTensor * b = need(a.name + ".bias");
             if (!b || b->type != GT_F32 || b->host.empty()) { rc = rc ? rc : TSD_ERR_UNSUPPORTED; return; }

@@ -36,9 +36,13 @@ struct RawTensor {
     int64_t n() const { return ne[0] * ne[1] * ne[2] * ne[3]; }
 };
 
-// A projection weight repacked for the tcgen05 GEMM: bf16 [M][taps*K_in], tap-major columns.
+// A projection weight repacked for the tcgen05 GEMM: bf16 [M][taps*K_in], tap-major columns; or,
+// for a Q8_0 source (single tap), planar Q8_0 that the GEMM dequantises in shared memory:
+// q [M][K_in] int8 and qs [K_in/32][M] f16 scales (transposed so a tile's scales are one TMA box).
 struct GW {
     __nv_bfloat16 * w = nullptr;
+    int8_t * q = nullptr;
+    __half * qs = nullptr;
     int M = 0, K_in = 0, taps = 1, pad = 0, m_valid = 0;
     float * bias = nullptr;
 };
