@@ -224,7 +224,8 @@ def run_cfg5(args, rank, world, local):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device(dev))
         pg = dist
-    hp = synth.DitHParams(**HP3)
+    # learned empties (the uncond pass's text / T5 features) as long as the config's sequences
+    hp = synth.DitHParams(**HP3, text_seq=CFG3["text_S"], t5_seq=CFG3["t5_S"])
     W = make_device_weights(hp, seed=1234, device=dev)
     model = tsd.DitModel.from_weights(hp, W, device=local)
     del W
