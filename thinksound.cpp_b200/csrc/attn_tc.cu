@@ -9,9 +9,13 @@
 // One CTA per (128-query tile, batch*head). Warp 0: TMA (Q once, K/V 128-row chunks through a
 // 3-stage ring). Warp 1: TMEM owner + MMA issuer: S_j = Q K_j^T into one of two 128-column
 // TMEM buffers, O += P_j V_j into a 64-column TMEM accumulator (V as an MN-major operand).
-// Warps 2-5: online softmax, one query row per thread (TMEM lane), P_j written fp16 into a
-// 128-B-swizzled shared tile, O rescaled in TMEM when the running max moves, final 1/l scale
-// and bf16 token-major store out[b][t][h*64 + d].
+// Warps 2-9: online softmax, two warps per TMEM lane quadrant: a query row (TMEM lane) is shared
+// by two threads, each taking 64 of a chunk's 128 key columns. Only the running max is
+// exchanged (once per chunk, through shared memory); each half keeps its own running sum under
+// the common max and the two are added at the end. P_j is written fp16 into a 128-B-swizzled
+// shared tile (one 64-key sub-tile per half), O is rescaled in TMEM (32 of its 64 columns per
+// half) when the max moves, and the final 1/l scale and bf16 token-major store
+// out[b][t][h*64 + d] are split the same way.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -25,8 +29,10 @@ constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kTileBytes;
 constexpr int kOffV = kOffK + kStages * kTileBytes;
 constexpr int kOffP = kOffV + kStages * kTileBytes;  // 2 sub-tiles (kv 0-63, 64-127)
-constexpr int kOffBar = kOffP + 2 * kTileBytes;
+constexpr int kOffRed = kOffP + 2 * kTileBytes;    // [3][2 halves][128 rows] f32: maxima (2 parities), sums
+constexpr int kOffBar = kOffRed + 3 * 2 * 128 * 4;
 constexpr int kSmemBytes = kOffBar + 256 + 1024;
+constexpr int kThreads = 320;                        // warps: 0 TMA, 1 MMA, 2-9 softmax
 constexpr uint32_t kTmemCols = 512;                  // S0 @0, S1 @128, O @256
 constexpr uint32_t kColO = 256;
 
@@ -38,7 +44,9 @@ struct AttnArgs {
     float scale_log2;
 };
 
-__global__ void __launch_bounds__(192, 1)
+__device__ __forceinline__ void soft_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+__global__ void __launch_bounds__(kThreads, 1)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
     pdl_launch_dependents();   // let the next kernel in the stream start its prologue
@@ -64,8 +72,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
         for (int s = 0; s < kStages; ++s) { mbar_init(&kv_full[s], 1); mbar_init(&kv_empty[s], 1); }
-        for (int s = 0; s < 2; ++s) { mbar_init(&s_full[s], 1); mbar_init(&s_free[s], 128); }
-        mbar_init(p_full, 128);
+        for (int s = 0; s < 2; ++s) { mbar_init(&s_full[s], 1); mbar_init(&s_free[s], 256); }
+        mbar_init(p_full, 256);
         mbar_init(pv_done, 1);
         *s_abort = 0;
         fence_mbar_init();
@@ -137,88 +145,90 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             if (!ok) umma_commit(pv_done);   // lets no waiter depend on MMAs that were never issued
         }
     } else {
-        // ---------------- softmax + epilogue (warps 2..5) ----------------
+        // ---------------- softmax + epilogue (warps 2..9) ----------------
         const int q = warp & 3;
+        const int half = (warp - 2) >> 2;             // key columns half * 64 .. + 63 of each chunk
         const int r = q * 32 + lane;                   // query row within the tile (TMEM lane)
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-        uint8_t * prow = smem + kOffP + r * 128;
+        uint8_t * prow = smem + kOffP + half * kTileBytes + r * 128;
+        float * red = reinterpret_cast<float *>(smem + kOffRed);
         float m_run = -INFINITY, l_run = 0.f;
         bool ok = true;
         for (int j = 0; j < nchunks; ++j) {
-            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, s_abort, a.err, DEV_TIMEOUT_ATTN))) { ok = false; break; }
+            // no shared abort flag in these waits: every warp gives up only on its own deadline,
+            // so all eight take the same branch around the named barrier below
+            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, nullptr, a.err, DEV_TIMEOUT_ATTN))) { ok = false; break; }
             tc_fence_after();
-            float sv[128];
+            float sv[64];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 float tmp[32];
-                tmem_ld32(lane_base + (j & 1) * 128 + c * 32, tmp);
+                tmem_ld32(lane_base + (j & 1) * 128 + half * 64 + c * 32, tmp);
 #pragma unroll
                 for (int i = 0; i < 32; ++i) sv[c * 32 + i] = tmp[i];
             }
             tc_fence_before();
             mbar_arrive(&s_free[j & 1]);
-            const int valid = S - j * kKV;            // columns >= valid are padding keys
-            float mx = m_run;
+            const int valid = S - j * kKV - half * 64;  // columns >= valid are padding keys
+            float mx = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < 128; ++i) {
+            for (int i = 0; i < 64; ++i) {
                 sv[i] = (i < valid) ? sv[i] * a.scale_log2 : -INFINITY;
                 mx = fmaxf(mx, sv[i]);
             }
+            float * rm = red + ((j & 1) * 2) * 128;     // this chunk's maxima [half][row]
+            rm[half * 128 + r] = mx;
+            soft_bar();
+            mx = fmaxf(fmaxf(mx, rm[(half ^ 1) * 128 + r]), m_run);
             const float alpha = ex2_approx(m_run - mx);   // 0 on the first chunk
             float rs = 0.f;
 #pragma unroll
-            for (int i = 0; i < 128; ++i) { sv[i] = ex2_approx(sv[i] - mx); rs += sv[i]; }
+            for (int i = 0; i < 64; ++i) { sv[i] = ex2_approx(sv[i] - mx); rs += sv[i]; }
             l_run = l_run * alpha + rs;
             m_run = mx;
             if (j > 0) {
-                // PV_{j-1} done: O is stable (rescale it) and the P tile is free.
-                if (!__all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, s_abort, a.err, DEV_TIMEOUT_ATTN))) { ok = false; break; }
+                // PV_{j-1} done: O is stable (rescale this half's 32 columns) and P is free.
+                if (!__all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, nullptr, a.err, DEV_TIMEOUT_ATTN))) { ok = false; break; }
                 tc_fence_after();
+                float o[32];
+                tmem_ld32(lane_base + kColO + half * 32, o);
 #pragma unroll
-                for (int c = 0; c < 2; ++c) {
-                    float o[32];
-                    tmem_ld32(lane_base + kColO + c * 32, o);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                    tmem_st32(lane_base + kColO + c * 32, o);
-                }
+                for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                tmem_st32(lane_base + kColO + half * 32, o);
             }
-            // P (fp16) into the 128-B swizzled K-major tile: row r, 16-B chunk ch -> ch ^ (r & 7)
+            // P (fp16) into this half's 128-B swizzled K-major sub-tile: row r, 16-B chunk ch -> ch ^ (r & 7)
 #pragma unroll
-            for (int sub = 0; sub < 2; ++sub) {
+            for (int ch = 0; ch < 8; ++ch) {
+                uint4 u;
+                __half2 * h2 = reinterpret_cast<__half2 *>(&u);
 #pragma unroll
-                for (int ch = 0; ch < 8; ++ch) {
-                    const int c0 = sub * 64 + ch * 8;
-                    uint4 u;
-                    __half2 * h2 = reinterpret_cast<__half2 *>(&u);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) h2[e] = __floats2half2_rn(sv[c0 + 2 * e], sv[c0 + 2 * e + 1]);
-                    *reinterpret_cast<uint4 *>(prow + sub * kTileBytes + ((ch ^ (r & 7)) << 4)) = u;
-                }
+                for (int e = 0; e < 4; ++e) h2[e] = __floats2half2_rn(sv[ch * 8 + 2 * e], sv[ch * 8 + 2 * e + 1]);
+                *reinterpret_cast<uint4 *>(prow + ((ch ^ (r & 7)) << 4)) = u;
             }
             fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(p_full);
         }
-        if (ok && __all_sync(0xffffffffu, mbar_wait(pv_done, (nchunks - 1) & 1, s_abort, a.err, DEV_TIMEOUT_ATTN))) {
+        if (ok && __all_sync(0xffffffffu, mbar_wait(pv_done, (nchunks - 1) & 1, nullptr, a.err, DEV_TIMEOUT_ATTN))) {
+            // both halves' sums under the common max
+            float * rl = red + 4 * 128;
+            rl[half * 128 + r] = l_run;
+            soft_bar();
+            const float inv = 1.0f / (l_run + rl[(half ^ 1) * 128 + r]);
             tc_fence_after();
             const int t = q0 + r;
-            const float inv = 1.0f / l_run;
             const int b = bh / a.nh, h = bh % a.nh;
+            float o[32];
+            tmem_ld32(lane_base + kColO + half * 32, o);
+            if (t < S) {
+                __nv_bfloat16 * dst = a.out + ((long long)b * S + t) * a.ldo + h * kHD + half * 32;
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                float o[32];
-                tmem_ld32(lane_base + kColO + c * 32, o);
-                if (t < S) {
-                    __nv_bfloat16 * dst = a.out + ((long long)b * S + t) * a.ldo + h * kHD + c * 32;
+                for (int e = 0; e < 4; ++e) {
+                    uint4 u;
+                    __nv_bfloat162 * p2 = reinterpret_cast<__nv_bfloat162 *>(&u);
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        uint4 u;
-                        __nv_bfloat162 * p2 = reinterpret_cast<__nv_bfloat162 *>(&u);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) p2[i] = __floats2bfloat162_rn(o[e * 8 + 2 * i] * inv, o[e * 8 + 2 * i + 1] * inv);
-                        *reinterpret_cast<uint4 *>(dst + e * 8) = u;
-                    }
+                    for (int i = 0; i < 4; ++i) p2[i] = __floats2bfloat162_rn(o[e * 8 + 2 * i] * inv, o[e * 8 + 2 * i + 1] * inv);
+                    *reinterpret_cast<uint4 *>(dst + e * 8) = u;
                 }
             }
         }
@@ -255,7 +265,7 @@ cudaError_t attn_launch(const AttnLaunch & L, cudaStream_t st) {
     a.S = L.S; a.nh = L.nh; a.ldo = L.ldo; a.out = reinterpret_cast<__nv_bfloat16 *>(L.out); a.err = L.err;
     a.scale_log2 = L.scale * 1.4426950408889634f;
     dim3 grid((L.S + kQT - 1) / kQT, L.B * L.nh);
-    attn_tc_kernel<<<grid, 192, kSmemBytes, st>>>(L.tmQ, L.tmK, L.tmV, a);
+    attn_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(L.tmQ, L.tmK, L.tmV, a);
     return cudaGetLastError();
 }
 
