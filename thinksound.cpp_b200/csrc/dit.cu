@@ -17,6 +17,9 @@ namespace tsd {
 
 Plan::~Plan() {
     if (graph) cudaGraphExecDestroy(graph);
+    for (cudaStream_t q : side)
+        if (q) cudaStreamDestroy(q);
+    for (cudaEvent_t e : events) cudaEventDestroy(e);
     for (void * p : allocs) cudaFree(p);
 }
 
@@ -35,8 +38,11 @@ struct Builder {
     // Split-K scratch shared by all GEMMs of the plan (they run one after another).
     static constexpr long long kWsFloats = 8ll << 20;   // 32 MB of partial tiles
     static constexpr int kCounters = 1 << 16;
-    float * ws = nullptr;
+    float * ws = nullptr;                  // per lane: concurrent GEMMs must not share split-K scratch
     int * counters = nullptr;
+    float * ws_lane[1 + kSideLanes] = {};
+    int * counters_lane[1 + kSideLanes] = {};
+    int lane = 0;                          // lane of the ops being added
     // Optional plan-time autotuning of the GEMM tiling (TSD_AUTOTUNE=1): per distinct shape the
     // cost model's best few (token tile, K splits) choices are timed on the plan's own buffers
     // and the fastest kept. Off by default: the number of K splits sets the summation order, so
@@ -85,7 +91,18 @@ struct Builder {
         Op o;
         o.fn = std::move(fn);
         o.kind = kind; o.flops = flops; o.bytes = bytes; o.launches = launches;
+        o.lane = lane;
         o.label = tag + (kind == OP_GEMM ? " gemm" : kind == OP_GEMV ? " gemv" : kind == OP_ATTN ? " attn" : kind == OP_COPY ? " copy" : " elem");
+        P.ops.push_back(std::move(o));
+    }
+    // Lane markers (see Op): fork lets the side lanes start after everything lane 0 has queued,
+    // join makes lane 0 wait for everything the side lanes have queued.
+    void mark(int sync) {
+        Op o;
+        o.sync = sync;
+        o.kind = OP_COPY;
+        o.launches = 0;
+        o.label = sync == 1 ? "fork" : "join";
         P.ops.push_back(std::move(o));
     }
     void snap(const char * name, const void * ptr, long long n, int kind = 0, int B = 0, int nh = 0, int S = 0) {
@@ -125,7 +142,7 @@ struct Builder {
         p.out = out; p.out_bf16 = out_bf16; p.ldo = ldo;
         p.out_cblk = out_cblk; p.out_cstride = out_cstride;
         p.resid = resid; p.ldr = ldr; p.gate = gate; p.ldg = ldg; p.gate_div = gate_div;
-        p.ws = ws; p.counters = counters;
+        p.ws = ws_lane[lane]; p.counters = counters_lane[lane];
         p.err = m.d_err;
         if (mode == EPI_QKV) {
             p.q_out = qspec.q; p.k_out = qspec.k; p.v_out = qspec.v;
@@ -231,6 +248,10 @@ struct Builder {
         auto * a1 = alloc<__nv_bfloat16>((size_t)B * maxS * H);
         auto * hbuf = alloc<__nv_bfloat16>((size_t)B * maxS * F);
         auto * xn = alloc<__nv_bfloat16>((size_t)B * maxS * H);
+        // per-lane copies for the joint blocks, whose three streams run on their own lanes
+        __nv_bfloat16 * xn_l[3] = {xn, alloc<__nv_bfloat16>((size_t)B * maxS * H), alloc<__nv_bfloat16>((size_t)B * maxS * H)};
+        __nv_bfloat16 * hb_l[3] = {hbuf, alloc<__nv_bfloat16>((size_t)B * maxS * F), alloc<__nv_bfloat16>((size_t)B * maxS * F)};
+        __nv_bfloat16 * a1_l[3] = {a1, alloc<__nv_bfloat16>((size_t)B * maxS * H), alloc<__nv_bfloat16>((size_t)B * maxS * H)};
         float * x_lat = alloc<float>((size_t)B * T * H);
         float * x_clip = alloc<float>((size_t)B * cS * H);
         float * x_text = alloc<float>((size_t)B * St * H);
@@ -257,12 +278,16 @@ struct Builder {
         auto * ao = alloc<__nv_bfloat16>((size_t)B * Sj * H);
         auto * rope_lat = alloc<float2>((size_t)T * 32);     // RoPE (cos, sin): latent positions, scale 1
         auto * rope_clip = alloc<float2>((size_t)cS * 32);   // clip positions, scale T / clip_S
-        ws = alloc<float>((size_t)kWsFloats);
-        counters = alloc<int>((size_t)kCounters);
+        ws = alloc<float>((size_t)kWsFloats * (1 + kSideLanes));
+        counters = alloc<int>((size_t)kCounters * (1 + kSideLanes));
         if (rc) return;
-        if (cudaMemset(counters, 0, sizeof(int) * kCounters) != cudaSuccess) { rc = TSD_ERR_CUDA; return; }
+        if (cudaMemset(counters, 0, sizeof(int) * kCounters * (1 + kSideLanes)) != cudaSuccess) { rc = TSD_ERR_CUDA; return; }
+        for (int l = 0; l <= kSideLanes; ++l) {
+            ws_lane[l] = ws + (size_t)l * kWsFloats;
+            counters_lane[l] = counters + (size_t)l * kCounters;
+        }
         P.counters = counters;
-        P.n_counters = kCounters;
+        P.n_counters = kCounters * (1 + kSideLanes);
         int * err = m.d_err;
         // Per-token adaLN output is column-blocked: chunk k of the stacked weight rows is one
         // contiguous [B*T][H] plane at mod_lat + k * BTH (row stride H), so each block's
@@ -286,6 +311,10 @@ struct Builder {
 
         op([err](cudaStream_t st) { return cudaMemsetAsync(err, 0, sizeof(int), st); }, OP_COPY, 0, 0, 0);
 
+        // The input projections are independent chains: audio, t-embed and sync on lane 0, clip
+        // on lane 1, text on lane 2 (each lane with its own a1 / hbuf), joined before the
+        // conditioning vectors that combine them.
+        mark(1);
         // ---- audio_input_proj (mmdit.cpp:150-155) ----
         tag = "pre.audio";
         op([=](cudaStream_t st) { return latent_to_tokens(lat_in, B, L, T, lat_tok, st); });
@@ -302,11 +331,13 @@ struct Builder {
         snap("t_emb", te, (long long)B * H);
         // ---- clip (mmdit.cpp:164-167) ----
         tag = "pre.clip";
+        lane = 1;
         op([=](cudaStream_t st) { return cast_f32_bf16(clip_in, (long long)B * cS * clip_dim, clip_tok, st); });
-        gemm(m.cp0, clip_tok, B, cS, m.clip_dim, (long long)cS * m.clip_dim, EPI_STORE, ACT_SILU, a1, 1, H);
-        gemm(m.cp13, a1, B, cS, H, (long long)cS * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 1);
-        gemm(m.cp2, hbuf, B, cS, F, (long long)cS * F, EPI_STORE, ACT_NONE, x_clip, 0, H);
+        gemm(m.cp0, clip_tok, B, cS, m.clip_dim, (long long)cS * m.clip_dim, EPI_STORE, ACT_SILU, a1_l[1], 1, H);
+        gemm(m.cp13, a1_l[1], B, cS, H, (long long)cS * H, EPI_SWIGLU, ACT_NONE, hb_l[1], 1, F, nullptr, 0, nullptr, 0, 1, 1);
+        gemm(m.cp2, hb_l[1], B, cS, F, (long long)cS * F, EPI_STORE, ACT_NONE, x_clip, 0, H);
         snap("clip_pp", x_clip, (long long)B * cS * H);
+        lane = 0;
         // ---- sync (mmdit.cpp:168-177) ----
         tag = "pre.sync";
         op([=](cudaStream_t st) { return sync_prep(sync_in, B, yS, sync_dim, sync_pe, sync_tok, st); });
@@ -315,13 +346,16 @@ struct Builder {
         gemm(m.sp2, hbuf, B, yS, F, (long long)yS * F, EPI_STORE, ACT_NONE, sync_out, 0, H);
         // ---- text (mmdit.cpp:178-183) ----
         tag = "pre.text";
+        lane = 2;
         op([=](cudaStream_t st) {
             return text_prep(text_in, text_S, text_dim, t5_in, t5_S, t5_dim, B, text_tok, st);
         });
-        gemm(m.tp0, text_tok, B, St, m.t5_dim, (long long)St * m.t5_dim, EPI_STORE, ACT_SILU, a1, 1, H);
-        gemm(m.tp13, a1, B, St, H, (long long)St * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 1);
-        gemm(m.tp2, hbuf, B, St, F, (long long)St * F, EPI_STORE, ACT_NONE, x_text, 0, H);
+        gemm(m.tp0, text_tok, B, St, m.t5_dim, (long long)St * m.t5_dim, EPI_STORE, ACT_SILU, a1_l[2], 1, H);
+        gemm(m.tp13, a1_l[2], B, St, H, (long long)St * H, EPI_SWIGLU, ACT_NONE, hb_l[2], 1, F, nullptr, 0, nullptr, 0, 1, 1);
+        gemm(m.tp2, hb_l[2], B, St, F, (long long)St * F, EPI_STORE, ACT_NONE, x_text, 0, H);
         snap("text_pp", x_text, (long long)B * St * H);
+        lane = 0;
+        mark(2);
         // ---- conditioning vectors (mmdit.cpp:184-200) ----
         tag = "pre.cond";
         gemv(m.tcp, P.gtext_in, m.text_dim, B, ACT_NONE, text_fc, H);
@@ -357,6 +391,10 @@ struct Builder {
             rc = TSD_ERR_ARG;
             return;
         }
+        // The three streams of a joint block are independent except at the attention: stream s
+        // runs on lane s (its own CUDA stream in the captured graph), joined before the
+        // attention and forked after it.
+        mark(1);
         for (int i = 0; i < n_joint; ++i) {
             const auto & blk = m.joint[i];
             const float * mods[3];
@@ -364,6 +402,8 @@ struct Builder {
             for (int s = 0; s < 3; ++s) {
                 const StreamW & w = blk[s];
                 const int S = Ss[s];
+                lane = s;
+                __nv_bfloat16 * const xn = xn_l[s];
                 tag = "j" + std::to_string(i) + (s == 0 ? ".lat" : s == 1 ? ".clip" : ".text");
                 if (s == 0) { mods[s] = mod_lat + (w.ada_off / H) * BTH; lds[s] = H; css[s] = BTH; }
                 else {
@@ -383,14 +423,20 @@ struct Builder {
                 snap("a0_k", Kb, (long long)B * Sj * H, 2, B, nh, Sj);
                 snap("a0_v", Vb, (long long)B * Sj * H, 2, B, nh, Sj);
             }
+            lane = 0;
+            mark(2);
             tag = "j" + std::to_string(i);
             op([AJ](cudaStream_t st) { return attn_launch(AJ, st); }, OP_ATTN, 4.0 * B * nh * 64.0 * Sj * Sj,
                6.0 * B * nh * 64.0 * Sj + 2.0 * B * Sj * H);
             if (i == 0) snap("a0_out", ao, (long long)B * Sj * H, 1);
+            mark(1);
             for (int s = 0; s < 3; ++s) {
                 const StreamW & w = blk[s];
                 if (w.pre_only) continue;
                 const int S = Ss[s];
+                lane = s;
+                __nv_bfloat16 * const xn = xn_l[s];
+                __nv_bfloat16 * const hbuf = hb_l[s];
                 tag = "j" + std::to_string(i) + (s == 0 ? ".lat" : s == 1 ? ".clip" : ".text");
                 const float * mod = mods[s];
                 const long long ld = lds[s], cs = css[s];
@@ -402,12 +448,15 @@ struct Builder {
                 gemm(w.w2, hbuf, B, S, F, (long long)S * F, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, xs[s], H, mod + 5 * cs,
                      ld, gdiv);
             }
+            lane = 0;
             if (i == 0) {
                 snap("jb0_lat", x_lat, (long long)B * T * H);
                 snap("jb0_clip", x_clip, (long long)B * cS * H);
                 snap("jb0_text", x_text, (long long)B * St * H);
             }
         }
+        lane = 0;
+        mark(2);
         snap("after_joint", x_lat, (long long)B * T * H);
         // ---- fused blocks (mmdit.cpp:274-282) ----
         int fi = 0;
@@ -478,7 +527,7 @@ int plan_profile(Model & m, Plan & p, cudaStream_t st, std::vector<float> & ms) 
     int rc = TSD_OK;
     cudaError_t ce = cudaEventRecord(ev[0], st);
     for (size_t i = 0; i < p.ops.size() && ce == cudaSuccess; ++i) {
-        ce = p.ops[i].fn(st);
+        if (p.ops[i].fn) ce = p.ops[i].fn(st);     // lane markers have no work
         if (ce == cudaSuccess) ce = cudaEventRecord(ev[i + 1], st);
     }
     if (ce == cudaSuccess) ce = cudaEventSynchronize(ev.back());
@@ -497,7 +546,7 @@ int plan_run(Model & m, Plan & p, cudaStream_t st, tsd_dbg_fn dbg, void * ud) {
     if (dbg) {
         std::vector<float> h;
         for (const Op & o : p.ops) {
-            TSD_CUDA_TRY(o.fn(st));
+            if (o.fn) TSD_CUDA_TRY(o.fn(st));
             if (!o.snaps.empty()) {
                 TSD_CUDA_TRY(cudaStreamSynchronize(st));
                 for (const Snap & s : o.snaps) {
@@ -514,14 +563,38 @@ int plan_run(Model & m, Plan & p, cudaStream_t st, tsd_dbg_fn dbg, void * ud) {
         TSD_CUDA_TRY(cudaStreamIsCapturing(st, &cs));
         const bool can_capture = (st != nullptr) && cs == cudaStreamCaptureStatusNone;
         if (!can_capture) {
-            for (const Op & o : p.ops) TSD_CUDA_TRY(o.fn(st));
+            for (const Op & o : p.ops)
+                if (o.fn) TSD_CUDA_TRY(o.fn(st));
             return TSD_OK;
+        }
+        // side lanes and one event per fork / two per join, created once per plan
+        size_t need_ev = 0;
+        for (const Op & o : p.ops) need_ev += o.sync == 1 ? 1 : o.sync == 2 ? kSideLanes : 0;
+        for (int l = 0; l < kSideLanes; ++l)
+            if (!p.side[l]) TSD_CUDA_TRY(cudaStreamCreateWithFlags(&p.side[l], cudaStreamNonBlocking));
+        while (p.events.size() < need_ev) {
+            cudaEvent_t ev;
+            TSD_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+            p.events.push_back(ev);
         }
         cudaGraph_t g;
         TSD_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
         cudaError_t e = cudaSuccess;
+        size_t ev = 0;
         for (const Op & o : p.ops) {
-            e = o.fn(st);
+            if (o.sync == 1) {            // fork: side lanes continue after lane 0's work so far
+                e = cudaEventRecord(p.events[ev], st);
+                for (int l = 0; e == cudaSuccess && l < kSideLanes; ++l) e = cudaStreamWaitEvent(p.side[l], p.events[ev], 0);
+                ++ev;
+            } else if (o.sync == 2) {     // join: lane 0 continues after the side lanes' work
+                for (int l = 0; e == cudaSuccess && l < kSideLanes; ++l) {
+                    e = cudaEventRecord(p.events[ev + l], p.side[l]);
+                    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, p.events[ev + l], 0);
+                }
+                ev += kSideLanes;
+            } else {
+                e = o.fn(o.lane == 0 ? st : p.side[o.lane - 1]);
+            }
             if (e != cudaSuccess) break;
         }
         cudaError_t e2 = cudaStreamEndCapture(st, &g);

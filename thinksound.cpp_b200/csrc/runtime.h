@@ -110,7 +110,13 @@ struct Op {
     int kind = OP_ELEM;
     int launches = 1;          // kernel launches the op issues
     double flops = 0, bytes = 0;   // algorithmic work of the op
+    // Graph replay only: the op's lane (0 = the caller's stream, 1..kSideLanes = side streams).
+    // Marker ops (fn empty): sync 1 = fork (side lanes wait for lane 0), 2 = join (lane 0 waits
+    // for the side lanes). Op-by-op execution runs everything in order on one stream.
+    int lane = 0;
+    int sync = 0;
 };
+constexpr int kSideLanes = 2;
 
 struct Shape {
     int B, T, clip_S, sync_S, text_S, t5_S;
@@ -131,6 +137,8 @@ struct Plan {
     std::vector<void *> allocs;
     cudaGraphExec_t graph = nullptr;
     cudaStream_t graph_stream = nullptr;
+    cudaStream_t side[kSideLanes] = {};        // side lanes of the captured graph
+    std::vector<cudaEvent_t> events;           // fork / join events (capture only)
     ~Plan();
 };
 
