@@ -152,6 +152,33 @@ def test_sampler_batched_prompts(small_bf16):
         assert oracle.rel_l2(lat[p], single[0]) < 1e-2
 
 
+def test_sampler_step_loop_equals_forward_calls(small_bf16):
+    """After step 0 the sampler replays the forward without its conditioning-only ops (clip /
+    sync / text projections, global MLP) and reuses their step-0 results. Stepping by hand with
+    full forward calls of the same cond / uncond pair (mmdit.cpp:344-376) must give the same
+    latent, up to the rounding of the CFG + Euler update done here in numpy."""
+    import dataclasses
+    hp, W, m, _ = small_bf16
+    x = synth.make_inputs(hp, seed=77, batch=1, **SHAPE)[0]
+    steps, cfg = 4, 5.0
+    lat = m.sample([x], steps=steps, cfg=cfg)[0]
+    es = W["empty_string_feat"].dequant().reshape(-1, hp.text_dim)[:SHAPE["text_S"]]
+    et = W["empty_t5_feat"].dequant().reshape(-1, hp.t5_dim)[:SHAPE["t5_S"]]
+    cur = np.asarray(x.latent, np.float32).copy()
+    for s in range(steps):
+        tc, tp = np.float32(1 - s / steps), np.float32(1 - (s + 1) / steps)
+        cond = dataclasses.replace(x, latent=cur, t=float(tc))
+        unc = dataclasses.replace(x, latent=cur, text_f=es, t5=et, gtext=np.zeros_like(x.gtext), t=float(tc))
+        fc, fu = m.forward([cond, unc])
+        cur = cur + (tp - tc) * (fu + (fc - fu) * np.float32(cfg)).T
+    assert oracle.rel_l2(lat, cur) < 1e-5
+    # a second prompt through the same plan recomputes its own conditioning at step 0
+    y = synth.make_inputs(hp, seed=78, batch=1, **SHAPE)[0]
+    m.sample([x], steps=2, cfg=cfg)
+    assert np.array_equal(m.sample([y], steps=2, cfg=cfg), m.sample([y], steps=2, cfg=cfg))
+    assert oracle.rel_l2(m.sample([y], steps=2, cfg=cfg)[0], m.sample([x], steps=2, cfg=cfg)[0]) > 1e-3
+
+
 def test_bad_shapes_are_rejected(small_bf16):
     hp, W, m, _ = small_bf16
     items = synth.make_inputs(hp, seed=1, batch=1, T=20, clip_S=8, sync_S=20, text_S=77, t5_S=9)  # sync_S % 8 != 0

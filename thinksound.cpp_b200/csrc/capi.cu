@@ -314,21 +314,25 @@ int tsd_sample_batched(tsd_model * h, int P, const float * noise, int64_t T, con
         TSD_CUDA_TRY(cudaMemcpyAsync(p->gtext_in, g2.data(), g2.size() * 4, cudaMemcpyHostToDevice, st));
         TSD_CUDA_TRY(cudaStreamSynchronize(st));
     }
-    float * x = nullptr, * f0 = nullptr, * tbuf = nullptr;
+    // Every step's timestep vector is staged up front, so the step loop only enqueues work.
+    std::vector<float> t_host((size_t)steps * B);
+    for (int s = 0; s < steps; ++s)
+        for (int i = 0; i < B; ++i) t_host[(size_t)s * B + i] = 1.0f - (float)s / steps;
+    float * x = nullptr, * f0 = nullptr, * t_all = nullptr;
     TSD_CUDA_TRY(cudaMalloc(&x, (size_t)P * L * T * 4));
+    if (cudaMalloc(&t_all, t_host.size() * 4) != cudaSuccess) { cudaFree(x); return TSD_ERR_CUDA; }
     if (flow0) cudaMalloc(&f0, (size_t)P * L * T * 4);
-    cudaMallocHost(&tbuf, (size_t)B * 4);
     rc = TSD_OK;
     cudaError_t e = cudaMemcpyAsync(x, noise, (size_t)P * L * T * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(t_all, t_host.data(), t_host.size() * 4, cudaMemcpyHostToDevice, st);
     for (int s = 0; s < steps && e == cudaSuccess && rc == TSD_OK; ++s) {
         const float t_curr = 1.0f - (float)s / steps, t_prev = 1.0f - (float)(s + 1) / steps;
-        e = cudaStreamSynchronize(st);      // tbuf is reused: the previous step's copy must be done
-        if (e != cudaSuccess) break;
-        for (int i = 0; i < B; ++i) tbuf[i] = t_curr;
-        e = cudaMemcpyAsync(p->t_in, tbuf, (size_t)B * 4, cudaMemcpyHostToDevice, st);
+        e = cudaMemcpyAsync(p->t_in, t_all + (size_t)s * B, (size_t)B * 4, cudaMemcpyDeviceToDevice, st);
         if (e == cudaSuccess) e = dup_latent(x, P, (int)L, (int)T, p->lat_in, st);
         if (e != cudaSuccess) break;
-        rc = plan_run(m, *p, st, nullptr, nullptr);
+        // the conditioning inputs were staged once above: steps after the first reuse the
+        // conditioning-only results (clip / sync / text projections, global MLP) of step 0
+        rc = plan_run(m, *p, st, nullptr, nullptr, s > 0);
         if (rc) break;
         e = cfg_euler(p->flow, P, (int)T, (int)L, cfg, t_prev - t_curr, x, (s == 0) ? f0 : nullptr, st);
     }
@@ -338,8 +342,8 @@ int tsd_sample_batched(tsd_model * h, int P, const float * noise, int64_t T, con
     if (e != cudaSuccess) fprintf(stderr, "tsd: sample: %s\n", cudaGetErrorString(e));
     cudaStreamSynchronize(st);
     cudaFree(x);
+    cudaFree(t_all);
     if (f0) cudaFree(f0);
-    cudaFreeHost(tbuf);
     return rc;
 }
 

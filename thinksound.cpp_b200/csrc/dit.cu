@@ -16,7 +16,8 @@
 namespace tsd {
 
 Plan::~Plan() {
-    if (graph) cudaGraphExecDestroy(graph);
+    for (cudaGraphExec_t g : graph)
+        if (g) cudaGraphExecDestroy(g);
     for (cudaStream_t q : side)
         if (q) cudaStreamDestroy(q);
     for (cudaEvent_t e : events) cudaEventDestroy(e);
@@ -43,6 +44,7 @@ struct Builder {
     float * ws_lane[1 + kSideLanes] = {};
     int * counters_lane[1 + kSideLanes] = {};
     int lane = 0;                          // lane of the ops being added
+    bool inv = false;                      // the ops being added are conditioning-only
     // Optional plan-time autotuning of the GEMM tiling (TSD_AUTOTUNE=1): per distinct shape the
     // cost model's best few (token tile, K splits) choices are timed on the plan's own buffers
     // and the fastest kept. Off by default: the number of K splits sets the summation order, so
@@ -92,6 +94,7 @@ struct Builder {
         o.fn = std::move(fn);
         o.kind = kind; o.flops = flops; o.bytes = bytes; o.launches = launches;
         o.lane = lane;
+        o.invariant = inv;
         o.label = tag + (kind == OP_GEMM ? " gemm" : kind == OP_GEMV ? " gemv" : kind == OP_ATTN ? " attn" : kind == OP_COPY ? " copy" : " elem");
         P.ops.push_back(std::move(o));
     }
@@ -104,6 +107,10 @@ struct Builder {
         o.launches = 0;
         o.label = sync == 1 ? "fork" : "join";
         P.ops.push_back(std::move(o));
+    }
+    void copy(void * dst, const void * src, size_t bytes) {
+        op([=](cudaStream_t st) { return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, st); }, OP_COPY, 0,
+           2.0 * bytes);
     }
     void snap(const char * name, const void * ptr, long long n, int kind = 0, int B = 0, int nh = 0, int S = 0) {
         if (!P.ops.empty()) P.ops.back().snaps.push_back(Snap{name, ptr, n, kind, B, nh, S});
@@ -255,6 +262,8 @@ struct Builder {
         float * x_lat = alloc<float>((size_t)B * T * H);
         float * x_clip = alloc<float>((size_t)B * cS * H);
         float * x_text = alloc<float>((size_t)B * St * H);
+        float * x_clip0 = alloc<float>((size_t)B * cS * H);     // projected clip / text tokens: kept
+        float * x_text0 = alloc<float>((size_t)B * St * H);     // across replays, copied into x_clip / x_text
         float * sync_out = alloc<float>((size_t)B * yS * H);
         float * temb = alloc<float>((size_t)B * H);
         float * te1 = alloc<float>((size_t)B * H);
@@ -313,7 +322,10 @@ struct Builder {
 
         // The input projections are independent chains: audio, t-embed and sync on lane 0, clip
         // on lane 1, text on lane 2 (each lane with its own a1 / hbuf), joined before the
-        // conditioning vectors that combine them.
+        // conditioning vectors that combine them. The clip, sync and text chains and the global
+        // conditioning MLP depend on the conditioning inputs only (marked `inv`): their results
+        // (x_clip0, x_text0, sync_out, gcm) are written by nothing else, so a replay with the same
+        // conditioning may skip them; the per-step copies into the residual streams stay.
         mark(1);
         // ---- audio_input_proj (mmdit.cpp:150-155) ----
         tag = "pre.audio";
@@ -332,41 +344,51 @@ struct Builder {
         // ---- clip (mmdit.cpp:164-167) ----
         tag = "pre.clip";
         lane = 1;
+        inv = true;
         op([=](cudaStream_t st) { return cast_f32_bf16(clip_in, (long long)B * cS * clip_dim, clip_tok, st); });
         gemm(m.cp0, clip_tok, B, cS, m.clip_dim, (long long)cS * m.clip_dim, EPI_STORE, ACT_SILU, a1_l[1], 1, H);
         gemm(m.cp13, a1_l[1], B, cS, H, (long long)cS * H, EPI_SWIGLU, ACT_NONE, hb_l[1], 1, F, nullptr, 0, nullptr, 0, 1, 1);
-        gemm(m.cp2, hb_l[1], B, cS, F, (long long)cS * F, EPI_STORE, ACT_NONE, x_clip, 0, H);
-        snap("clip_pp", x_clip, (long long)B * cS * H);
+        gemm(m.cp2, hb_l[1], B, cS, F, (long long)cS * F, EPI_STORE, ACT_NONE, x_clip0, 0, H);
+        snap("clip_pp", x_clip0, (long long)B * cS * H);
+        inv = false;
+        copy(x_clip, x_clip0, (size_t)B * cS * H * sizeof(float));
         lane = 0;
         // ---- sync (mmdit.cpp:168-177) ----
         tag = "pre.sync";
+        inv = true;
         op([=](cudaStream_t st) { return sync_prep(sync_in, B, yS, sync_dim, sync_pe, sync_tok, st); });
         gemm(m.sp0, sync_tok, B, yS, m.sync_dim, (long long)yS * m.sync_dim, EPI_STORE, ACT_SILU, a1, 1, H);
         gemm(m.sp13, a1, B, yS, H, (long long)yS * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 1);
         gemm(m.sp2, hbuf, B, yS, F, (long long)yS * F, EPI_STORE, ACT_NONE, sync_out, 0, H);
+        inv = false;
         // ---- text (mmdit.cpp:178-183) ----
         tag = "pre.text";
         lane = 2;
+        inv = true;
         op([=](cudaStream_t st) {
             return text_prep(text_in, text_S, text_dim, t5_in, t5_S, t5_dim, B, text_tok, st);
         });
         gemm(m.tp0, text_tok, B, St, m.t5_dim, (long long)St * m.t5_dim, EPI_STORE, ACT_SILU, a1_l[2], 1, H);
         gemm(m.tp13, a1_l[2], B, St, H, (long long)St * H, EPI_SWIGLU, ACT_NONE, hb_l[2], 1, F, nullptr, 0, nullptr, 0, 1, 1);
-        gemm(m.tp2, hb_l[2], B, St, F, (long long)St * F, EPI_STORE, ACT_NONE, x_text, 0, H);
-        snap("text_pp", x_text, (long long)B * St * H);
+        gemm(m.tp2, hb_l[2], B, St, F, (long long)St * F, EPI_STORE, ACT_NONE, x_text0, 0, H);
+        snap("text_pp", x_text0, (long long)B * St * H);
+        inv = false;
+        copy(x_text, x_text0, (size_t)B * St * H * sizeof(float));
         lane = 0;
         mark(2);
         // ---- conditioning vectors (mmdit.cpp:184-200) ----
         tag = "pre.cond";
+        inv = true;
         gemv(m.tcp, P.gtext_in, m.text_dim, B, ACT_NONE, text_fc, H);
         snap("text_fc", text_fc, (long long)B * H);
-        op([=](cudaStream_t st) { return seq_mean(x_clip, B, cS, H, cmean, st); });
+        op([=](cudaStream_t st) { return seq_mean(x_clip0, B, cS, H, cmean, st); });
         gemv(m.ccp, cmean, H, B, ACT_NONE, clip_fc, H);
         snap("clip_fc", clip_fc, (long long)B * H);
         op([=](cudaStream_t st) { return add_vec(clip_fc, text_fc, B * H, gsum, st); });
         gemv(m.gc13, gsum, H, B, ACT_NONE, gch, F);
         gemv(m.gc2, gch, F, B, ACT_NONE, gcm, H);
         snap("gcmlp", gcm, (long long)B * H);
+        inv = false;
         op([=](cudaStream_t st) { return add_vec(gcm, te, B * H, gc, st); });
         snap("global_c", gc, (long long)B * H);
         op([=](cudaStream_t st) { return build_extended(sync_out, yS, gc, B, T, H, ext, sext, sgc, st); });
@@ -542,7 +564,8 @@ int plan_profile(Model & m, Plan & p, cudaStream_t st, std::vector<float> & ms) 
     return rc;
 }
 
-int plan_run(Model & m, Plan & p, cudaStream_t st, tsd_dbg_fn dbg, void * ud) {
+int plan_run(Model & m, Plan & p, cudaStream_t st, tsd_dbg_fn dbg, void * ud, bool reuse_cond) {
+    (void)m;
     if (dbg) {
         std::vector<float> h;
         for (const Op & o : p.ops) {
@@ -557,14 +580,15 @@ int plan_run(Model & m, Plan & p, cudaStream_t st, tsd_dbg_fn dbg, void * ud) {
         }
         return TSD_OK;
     }
-    if (!p.graph || p.graph_stream != st) {
-        if (p.graph) { cudaGraphExecDestroy(p.graph); p.graph = nullptr; }
+    const int gi = reuse_cond ? 1 : 0;
+    if (!p.graph[gi] || p.graph_stream[gi] != st) {
+        if (p.graph[gi]) { cudaGraphExecDestroy(p.graph[gi]); p.graph[gi] = nullptr; }
         cudaStreamCaptureStatus cs;
         TSD_CUDA_TRY(cudaStreamIsCapturing(st, &cs));
         const bool can_capture = (st != nullptr) && cs == cudaStreamCaptureStatusNone;
         if (!can_capture) {
             for (const Op & o : p.ops)
-                if (o.fn) TSD_CUDA_TRY(o.fn(st));
+                if (o.fn && !(reuse_cond && o.invariant)) TSD_CUDA_TRY(o.fn(st));
             return TSD_OK;
         }
         // side lanes and one event per fork / two per join, created once per plan
@@ -592,7 +616,7 @@ int plan_run(Model & m, Plan & p, cudaStream_t st, tsd_dbg_fn dbg, void * ud) {
                     if (e == cudaSuccess) e = cudaStreamWaitEvent(st, p.events[ev + l], 0);
                 }
                 ev += kSideLanes;
-            } else {
+            } else if (!(reuse_cond && o.invariant)) {
                 e = o.fn(o.lane == 0 ? st : p.side[o.lane - 1]);
             }
             if (e != cudaSuccess) break;
@@ -603,12 +627,12 @@ int plan_run(Model & m, Plan & p, cudaStream_t st, tsd_dbg_fn dbg, void * ud) {
             fprintf(stderr, "tsd: graph capture failed: %s\n", cudaGetErrorString(e != cudaSuccess ? e : e2));
             return TSD_ERR_CUDA;
         }
-        e = cudaGraphInstantiate(&p.graph, g, 0);
+        e = cudaGraphInstantiate(&p.graph[gi], g, 0);
         cudaGraphDestroy(g);
         TSD_CUDA_TRY(e);
-        p.graph_stream = st;
+        p.graph_stream[gi] = st;
     }
-    TSD_CUDA_TRY(cudaGraphLaunch(p.graph, st));
+    TSD_CUDA_TRY(cudaGraphLaunch(p.graph[gi], st));
     return TSD_OK;
 }
 

@@ -115,6 +115,10 @@ struct Op {
     // for the side lanes). Op-by-op execution runs everything in order on one stream.
     int lane = 0;
     int sync = 0;
+    // Conditioning-only: the op reads only the staged clip / sync / text / global inputs (or
+    // other conditioning-only ops' outputs) and writes buffers nothing else writes, so a replay
+    // with unchanged conditioning inputs may skip it (the sampler's steps after the first).
+    bool invariant = false;
 };
 constexpr int kSideLanes = 2;
 
@@ -135,16 +139,19 @@ struct Plan {
     int n_counters = 0;
     std::vector<Op> ops;
     std::vector<void *> allocs;
-    cudaGraphExec_t graph = nullptr;
-    cudaStream_t graph_stream = nullptr;
+    // [0] every op; [1] without the conditioning-only ops (Op::invariant)
+    cudaGraphExec_t graph[2] = {};
+    cudaStream_t graph_stream[2] = {};
     cudaStream_t side[kSideLanes] = {};        // side lanes of the captured graph
     std::vector<cudaEvent_t> events;           // fork / join events (capture only)
     ~Plan();
 };
 
 int plan_build(Model & m, const Shape & sh, std::unique_ptr<Plan> & out);
-// Enqueue the forward (inputs already in the plan's buffers).
-int plan_run(Model & m, Plan & p, cudaStream_t st, tsd_dbg_fn dbg, void * ud);
+// Enqueue the forward (inputs already in the plan's buffers). reuse_cond: the conditioning
+// inputs (clip_in, sync_in, text_in, t5_in, gtext_in) are unchanged since the last full run of
+// this plan, whose conditioning-only results are reused instead of recomputed.
+int plan_run(Model & m, Plan & p, cudaStream_t st, tsd_dbg_fn dbg, void * ud, bool reuse_cond = false);
 // Run the forward op by op with CUDA events around each op; per-op milliseconds.
 int plan_profile(Model & m, Plan & p, cudaStream_t st, std::vector<float> & ms);
 
