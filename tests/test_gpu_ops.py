@@ -147,6 +147,56 @@ def test_gemm_split_k_store_and_swiglu(mode):
     assert int(counters.abs().sum()) == 0
 
 
+@pytest.mark.parametrize("M,K,taps,nb,S,mode,splits", [
+    (1536, 1536, 3, 2, 194, tsd.EPI_GATE_RESID, 2),  # linear1 / w2 shape class: pair tiles + cluster split-K
+    (4608, 256, 1, 1, 388, tsd.EPI_STORE, 1),        # QKV-like: one pair tile per CTA pair
+    (2048, 256, 3, 2, 194, tsd.EPI_SWIGLU, 1),       # w1/w3 SwiGLU conv
+    (512, 128, 1, 1, 3000, tsd.EPI_STORE, 1),        # many pair tiles per pair (TMEM double buffer)
+    (1536, 2048, 3, 2, 194, tsd.EPI_STORE, 4),       # cluster split-K of pair tiles, plain store
+])
+def test_gemm_cta_pairs_match_single_ctas(monkeypatch, capfd, M, K, taps, nb, S, mode, splits):
+    """CTA pairs (cta_group::2: 256 weight rows per pair, each CTA loading half of the token
+    tile) give the single-CTA kernel's results."""
+    W = rnd(M, taps * K, scale=0.03)
+    X = rnd(nb, S, K)
+    bias = torch.randn(M, device=DEV) if mode != tsd.EPI_SWIGLU else None
+    gate = torch.randn(nb * S, M, device=DEV)
+    x0 = torch.randn(nb, S, M, device=DEV)
+    ws = torch.empty(8 << 20, device=DEV)
+    counters = torch.zeros(1 << 16, device=DEV, dtype=torch.int32)
+    Fo = M // 2 if mode == tsd.EPI_SWIGLU else M
+    outs = {}
+    monkeypatch.setenv("TSD_DEBUG_PLAN", "1")
+    for no_pair in ("1", "0"):
+        monkeypatch.setenv("TSD_NO_PAIR", no_pair)
+        if no_pair == "0":
+            monkeypatch.setenv("TSD_FORCE_PAIR", "1")     # the model's best pair tiling, even if single CTAs win
+        capfd.readouterr()
+        if mode == tsd.EPI_GATE_RESID:
+            out = x0.clone()
+            tsd.op_gemm(W, M, K, taps, taps // 2, X, nb, S, K, S * K, mode, 0, bias, None, 0, 0, resid=out, ldr=M,
+                        gate=gate, ldg=M, gate_div=1, max_splits=splits, ws=ws, counters=counters)
+        else:
+            out = torch.empty(nb, S, Fo, device=DEV, dtype=torch.bfloat16 if mode == tsd.EPI_SWIGLU else torch.float32)
+            tsd.op_gemm(W, M, K, taps, taps // 2, X, nb, S, K, S * K, mode, 0, bias, out,
+                        1 if mode == tsd.EPI_SWIGLU else 0, Fo, max_splits=splits, ws=ws, counters=counters)
+        torch.cuda.synchronize()
+        err = capfd.readouterr().err
+        assert ("pair=1" in err) == (no_pair == "0"), err
+        outs[no_pair] = out.float()
+    acc = ref_gemm(W, X, taps, taps // 2)
+    if mode == tsd.EPI_SWIGLU:
+        ref, tol = torch.nn.functional.silu(acc[..., 0::2]) * acc[..., 1::2], 4e-3
+    elif mode == tsd.EPI_GATE_RESID:
+        ref, tol = x0 + gate.view(nb, S, M) * (acc + bias), 1e-5
+    else:
+        ref, tol = acc + bias, 1e-5
+    assert rel(outs["1"], ref) < tol and rel(outs["0"], ref) < tol
+    # the two tilings may split K differently (a different f32 summation order)
+    assert rel(outs["0"], outs["1"]) < (2e-3 if mode == tsd.EPI_SWIGLU else 1e-5)
+    assert int(counters.abs().sum()) == 0
+
+
 def test_gemm_strided_slice_of_joint_buffer():
     """linear1 reads its stream's rows out of the joint attention output [B][Sj][H]."""
     H, B, Sj, off, S = 128, 2, 300, 194, 72

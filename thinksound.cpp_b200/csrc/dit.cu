@@ -54,8 +54,8 @@ struct Builder {
     // the kernels' speed does not depend on the values, and every buffer they write is rewritten
     // by the forward itself.
     using TuneKey = std::tuple<int, int, int, int, int, int, int, int, int, int>;
-    static std::map<TuneKey, std::pair<int, int>> & tuned_cache() {
-        static std::map<TuneKey, std::pair<int, int>> c;
+    static std::map<TuneKey, std::tuple<int, int, int>> & tuned_cache() {
+        static std::map<TuneKey, std::tuple<int, int, int>> c;
         return c;
     }
     cudaStream_t tune_st = nullptr;
@@ -127,17 +127,16 @@ struct Builder {
         if (mode != EPI_QKV && w.taps == 1 && xbs == (long long)S * xrs && nbatch > 1) { S *= nbatch; nbatch = 1; }
         GemmLaunch L;
         const int M = w.M;
-        int force_bn = 0, force_sp = 0;
+        int force_bn = 0, force_sp = 0, force_pair = -1;
         const TuneKey key{m.device, M, w.K_in, w.taps, nbatch, S, mode, act, out_bf16, max_splits};
         auto & tuned = tuned_cache();
         auto hit = autotune ? tuned.find(key) : tuned.end();
         if (autotune && hit != tuned.end()) {
-            force_bn = hit->second.first;
-            force_sp = hit->second.second;
+            std::tie(force_bn, force_sp, force_pair) = hit->second;
         }
         const void * Wp = w.q ? static_cast<const void *>(w.q) : static_cast<const void *>(w.w);
         if (!gemm_plan(L, Wp, M, w.K_in, w.taps, w.pad, swiglu, X, nbatch, S, xrs, xbs, m.num_sms, max_splits,
-                       kWsFloats, kCounters, true, force_bn, force_sp, w.qs)) {
+                       kWsFloats, kCounters, true, force_bn, force_sp, w.qs, force_pair)) {
             fprintf(stderr, "tsd: gemm plan failed (M %d K %d taps %d S %d)\n", M, w.K_in, w.taps, S);
             rc = TSD_ERR_ARG;
             return;
@@ -158,31 +157,31 @@ struct Builder {
         }
         gemm_finalize(L);
         if (autotune && hit == tuned.end()) {
-            int bns[6], sps[6];
+            int bns[8], sps[8], prs[8];
             const int nc = gemm_candidates(M, w.K_in, w.taps, nbatch, S, m.num_sms, max_splits, kWsFloats, kCounters,
-                                           true, 6, bns, sps);
+                                           true, 8, bns, sps, prs);
             float best = time_gemm(L);
-            std::pair<int, int> pick{L.p.BN, L.p.splits};
-            if (tune_log) fprintf(stderr, "tsd tune: M=%d K=%d taps=%d nb=%d S=%d mode=%d: model BN=%d sp=%d %.1f us", M,
-                                  w.K_in, w.taps, nbatch, S, mode, L.p.BN, L.p.splits, best * 1000.f);
+            std::tuple<int, int, int> pick{L.p.BN, L.p.splits, L.p.pair};
+            if (tune_log) fprintf(stderr, "tsd tune: M=%d K=%d taps=%d nb=%d S=%d mode=%d: model BN=%d sp=%d pair=%d %.1f us", M,
+                                  w.K_in, w.taps, nbatch, S, mode, L.p.BN, L.p.splits, L.p.pair, best * 1000.f);
             for (int i = 1; i < nc; ++i) {
                 GemmLaunch C = L;
                 if (!gemm_plan(C, Wp, M, w.K_in, w.taps, w.pad, swiglu, X, nbatch, S, xrs, xbs, m.num_sms, max_splits,
-                               kWsFloats, kCounters, true, bns[i], sps[i], w.qs))
+                               kWsFloats, kCounters, true, bns[i], sps[i], w.qs, prs[i]))
                     continue;
                 const GemmParams & q = L.p;   // same epilogue, new tiling
                 GemmParams & cp = C.p;
                 const int BN = cp.BN, nt = cp.n_tiles, sp = cp.splits, cs = cp.csplit, order = cp.order, st = cp.stages;
-                const int aq8 = cp.a_q8;
+                const int aq8 = cp.a_q8, pr = cp.pair, kpb = cp.kpb;
                 cp = q;
                 cp.BN = BN; cp.n_tiles = nt; cp.splits = sp; cp.csplit = cs; cp.order = order; cp.stages = st;
-                cp.a_q8 = aq8;
+                cp.a_q8 = aq8; cp.pair = pr; cp.kpb = kpb;   // the tiling fields that go with C's tensor maps
                 gemm_finalize(C);
                 const float t = time_gemm(C);
-                if (tune_log) fprintf(stderr, " | BN=%d sp=%d %.1f us", BN, sp, t * 1000.f);
-                if (t > 0.f && (best < 0.f || t < best)) { best = t; pick = {BN, sp}; L = C; }
+                if (tune_log) fprintf(stderr, " | BN=%d sp=%d pair=%d %.1f us", BN, sp, pr, t * 1000.f);
+                if (t > 0.f && (best < 0.f || t < best)) { best = t; pick = {BN, sp, pr}; L = C; }
             }
-            if (tune_log) fprintf(stderr, " -> BN=%d sp=%d\n", pick.first, pick.second);
+            if (tune_log) fprintf(stderr, " -> BN=%d sp=%d pair=%d\n", std::get<0>(pick), std::get<1>(pick), std::get<2>(pick));
             tuned[key] = pick;
         }
         const double n_tok = (double)nbatch * S, kdim = (double)w.taps * w.K_in;

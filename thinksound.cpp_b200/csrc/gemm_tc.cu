@@ -42,13 +42,16 @@ __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: 
 struct TileCoord { int mb, b, t0, kb_begin, kb_end, split, otile; };
 
 // Tile t -> (m-block, batch item, first token, K range). Consecutive t share the m-block.
-__device__ __forceinline__ TileCoord decode(const GemmParams & p, int t, int nkb) {
+// CTA pairs walk pair tiles: tile t covers m-blocks 2 * (t / per_mb) + {0, 1}, `prank` picks
+// this CTA's.
+__device__ __forceinline__ TileCoord decode(const GemmParams & p, int t, int nkb, int prank = 0) {
     TileCoord c;
     int nt;
     if (p.order == 0) {           // m-block-major: consecutive tiles share the weight tile
         const int per_mb = p.nbatch * p.n_tiles * p.splits;
         c.mb = t / per_mb;
         const int rem = t - c.mb * per_mb;
+        if (p.pair) c.mb = 2 * c.mb + prank;
         nt = rem / p.splits;
         c.split = rem - nt * p.splits;
     } else {                      // token-tile-major: consecutive tiles share the activation tile
@@ -553,7 +556,9 @@ __device__ __forceinline__ void finish_slice(const GemmParams & p, const CUtenso
     }
 }
 
-template <int EK>
+// PAIR: the CTA-pair form (cta_group::2). A kernel holding cta_group::2 instructions must be
+// launched in clusters of an even size, so the single-CTA form is a separate instance.
+template <int EK, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmG,
@@ -576,11 +581,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kpt = p.K_in >> 6;
     const int nkb = p.taps * kpt;
-    const int num_tiles = p.mblocks * p.nbatch * p.n_tiles * p.splits;
-    // one stage: A bf16 (SW128) | B bf16 (SW128) | Q8_0 path: int8 tile + scales; a multiple of
-    // 1024 bytes, so every stage's SW128 atoms stay aligned
-    const int sbytes = kABytes + p.BN * 128 + (p.a_q8 ? kQ8Bytes : 0);
-    const uint32_t b_bytes = (uint32_t)(p.BN * 128);
+    const int kpb = p.kpb;                       // K blocks per stage (a K step); kpt % kpb == 0
+    const int nks = nkb / kpb;                   // K steps; tile K ranges are in K steps
+    // CTA pairs: consecutive cluster ranks 2j (leader) and 2j + 1 share pair tiles
+    const uint32_t crank = (PAIR || p.csplit) ? cluster_ctarank() : 0u;
+    const int prank = PAIR ? (int)(crank & 1u) : 0;           // this CTA's half of the pair tile
+    const uint32_t lead = crank & ~1u;                           // cluster rank of the pair leader
+    const int srank = PAIR ? (int)(crank >> 1) : (int)crank;   // cluster split-K: this CTA's split
+    const int tile0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int tstep = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const int num_tiles = (PAIR ? p.mblocks >> 1 : p.mblocks) * p.nbatch * p.n_tiles * p.splits;
+    const int bh = PAIR ? p.BN >> 1 : p.BN;                   // token rows of B this CTA loads
+    // one stage: kpb A atoms (bf16 128 x 64, SW128) | kpb B atoms (bh x 64) | Q8_0 path (kpb = 1):
+    // int8 tile + scales; a multiple of 1024 bytes, so every stage's SW128 atoms stay aligned
+    const uint32_t b_bytes = (uint32_t)(bh * 128);                   // one B atom
+    const int sbytes = kpb * (kABytes + (int)b_bytes) + (p.a_q8 ? kQ8Bytes : 0);
     const int nst = p.stages;                   // ring depth, <= kMaxStages, nst * sbytes <= kStageArea
 
     if (threadIdx.x == 0) {
@@ -588,7 +603,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int s = 0; s < kMaxStages; ++s) {
             mbar_init(&full[s], p.a_q8 ? 3 : 1); mbar_init(&empty[s], 1); mbar_init(&rfull[s], 1);
         }
-        for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 4); mbar_init(&ebar[s], 1); }
+        // acc_empty: the four epilogue warps (of both CTAs of a pair, on the leader's)
+        for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], PAIR ? 8 : 4); mbar_init(&ebar[s], 1); }
         mbar_init(&cbar[0], 1);
         for (int s = 1; s < 3; ++s) mbar_init(&cbar[s], p.csplit ? p.splits - 1 : 1);
         *s_abort = 0;
@@ -600,94 +616,130 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if ((Epi<EK>::gate && p.gate_div == 1) || Epi<EK>::qkv) tma_prefetch(&tmG);
         if (Epi<EK>::qkv) tma_prefetch(&tmV);
     }
-    if (warp == 1) { tmem_alloc(tmem_slot, kTmemCols); tmem_relinquish(); }
+    if (warp == 1) {
+        if constexpr (PAIR) { tmem_alloc_pair(tmem_slot, kTmemCols); tmem_relinquish_pair(); }
+        else { tmem_alloc(tmem_slot, kTmemCols); tmem_relinquish(); }
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    // cluster split-K: every CTA's barriers are initialised before any peer arrives on them;
-    // cbar[0] then expects the bytes of this rank's slice from each of the other ranks
-    if (p.csplit) {
-        cluster_sync_all();
-        if (threadIdx.x == 64) {
-            const int r = (int)cluster_ctarank();
-            const int rows = slice_lo(r + 1, p.BN, p.splits) - slice_lo(r, p.BN, p.splits);
-            mbar_arrive_expect_tx(&cbar[0], (uint32_t)((p.splits - 1) * rows * 512));
-        }
+    // pairs / cluster split-K: every CTA's barriers are initialised before any other CTA of the
+    // cluster signals them; cbar[0] then expects the bytes of this split's slice from each of
+    // the other splits
+    if (p.csplit || PAIR) cluster_sync_all();
+    if (p.csplit && threadIdx.x == 64) {
+        const int rows = slice_lo(srank + 1, p.BN, p.splits) - slice_lo(srank, p.BN, p.splits);
+        mbar_arrive_expect_tx(&cbar[0], (uint32_t)((p.splits - 1) * rows * 512));
     }
     const uint32_t tmem = *tmem_slot;
     pdl_launch_dependents();
 
-    if (warp == 0) {
-        if (lane == 0) {
-            // ---------------- TMA producer ----------------
-            // Weight tiles of the first stages do not depend on earlier kernels: request them
-            // before waiting for the predecessor grid; their activation tiles follow the wait.
-            // bf16 weights land in the stage's A slot (on `full`, with the activation tile);
-            // Q8_0 weights land as int8 + scales (on `rfull`) for the converter warps.
-            const auto issue_a = [&](int st, int kb, const TileCoord & c) {
-                uint8_t * sa = smem + st * sbytes;
-                if (p.a_q8) {
-                    uint8_t * raw = sa + kABytes + p.BN * 128;
-                    mbar_arrive_expect_tx(&rfull[st], 128 * 64 + 2 * 128 * 2);
-                    tma_load_2d(raw, &tmA, &rfull[st], kb * 64, c.mb * 128);
-                    tma_load_2d(raw + 128 * 64, &tmS, &rfull[st], c.mb * 128, kb * 2);
-                } else {
-                    mbar_arrive_expect_tx(&full[st], kABytes + b_bytes);
-                    tma_load_2d(sa, &tmA, &full[st], kb * 64, c.mb * 128);
-                }
-            };
-            const auto issue_b = [&](int st, int kb, const TileCoord & c) {
-                const int tap = kb / kpt, kc = kb - tap * kpt;
-                if (p.a_q8) mbar_arrive_expect_tx(&full[st], b_bytes);
-                tma_load_3d(smem + st * sbytes + kABytes, &tmB, &full[st], kc * 64, c.t0 + tap - p.pad, c.b);
-            };
-            int pre = 0;
-            for (int t = blockIdx.x; t < num_tiles && pre < nst; t += gridDim.x) {
-                const TileCoord c = decode(p, t, nkb);
-                for (int kb = c.kb_begin; kb < c.kb_end && pre < nst; ++kb, ++pre) issue_a(pre, kb, c);
+    // ---------------- TMA producers ----------------
+    // A TMA instruction costs its issuing thread ~300 cycles whatever the box size, and an
+    // integer division ~120, against 310-520 cycles of MMAs per K block: one thread issuing both
+    // tiles of every K block (and dividing to find the conv tap) bound the mainloop. So a stage
+    // holds kpb = 2 K blocks where K allows (one 3-D / 4-D box per operand per stage), the weight
+    // tiles (A) are issued by two threads (warps 0 and 7, alternate stages) and the activation
+    // tiles (B) by a third (warp 6), each walking K by increments. On the Q8_0 path warps 6-7
+    // convert and warp 0 issues everything. Weight tiles of the first stages do not depend on
+    // earlier kernels: they are requested before the wait for the predecessor grid.
+    // role bit 1: A (weights; arms `full` with the stage's bytes), bit 2: B (activations);
+    // A of K step `it` is issued by the part with it % a_parts == a_part.
+    const auto produce = [&](const int role, const int a_part, const int a_parts) {
+        const bool do_a = role & 1, do_b = role & 2;
+        const uint32_t stage_tx = (uint32_t)kpb * (kABytes + b_bytes) * (PAIR ? 2u : 1u);
+        const auto issue_a = [&](int st, int kb, int ya) {
+            uint8_t * sa = smem + st * sbytes;
+            if (p.a_q8) {
+                uint8_t * raw = sa + kABytes + p.BN * 128;
+                mbar_arrive_expect_tx(&rfull[st], 128 * 64 + 2 * 128 * 2);
+                tma_load_2d(raw, &tmA, &rfull[st], kb * 64, ya);
+                tma_load_2d(raw + 128 * 64, &tmS, &rfull[st], ya, kb * 2);
+            } else if constexpr (PAIR) {
+                // both CTAs' tiles count on the leader's barrier, which the leader arms
+                if (prank == 0) mbar_arrive_expect_tx(&full[st], stage_tx);
+                tma_load_3d_pair(sa, &tmA, mapa_shared(smem_u32(&full[st]), lead), 0, ya, kb);
+            } else {
+                mbar_arrive_expect_tx(&full[st], stage_tx);
+                tma_load_3d(sa, &tmA, &full[st], 0, ya, kb);
             }
-            pdl_wait();
-            int it = 0;
-            int s = 0;                 // ring slot of `it`, and the parity of its use (it / nst) & 1
-            uint32_t ph = 0;
-            for (int t = blockIdx.x; t < num_tiles && !*s_abort; t += gridDim.x) {
-                const TileCoord c = decode(p, t, nkb);
-                for (int kb = c.kb_begin; kb < c.kb_end; ++kb, ++it) {
-                    const int cs = s;
-                    const uint32_t cph = ph;
-                    if (++s == nst) { s = 0; ph ^= 1; }
-                    if (it < pre) {       // A already requested
-                        issue_b(cs, kb, c);
-                        continue;
-                    }
-                    if (it >= nst && !mbar_wait(&empty[cs], cph ^ 1, s_abort, p.err, DEV_TIMEOUT_EMPTY))
-                        break;
-                    issue_a(cs, kb, c);
-                    issue_b(cs, kb, c);
-                }
-            }
-            if (*s_abort) {
-                // Let the copies still in flight land before the CTA exits (one deadline for all).
-                const int issued = it > pre ? it : pre;
-                const unsigned long long t_start = globaltimer();
-                for (int i = (issued > nst ? issued - nst : 0); i < issued; ++i) {
-                    uint64_t * bar = p.a_q8 ? &rfull[i % nst] : &full[i % nst];
-                    while (!mbar_try_wait(bar, (i / nst) & 1) && globaltimer() - t_start < kWaitNs) {}
-                }
+        };
+        const auto issue_b = [&](int st, int kc, int yb, int b) {
+            uint8_t * sb = smem + st * sbytes + kpb * kABytes;
+            if (p.a_q8) mbar_arrive_expect_tx(&full[st], b_bytes);
+            if constexpr (PAIR)
+                tma_load_4d_pair(sb, &tmB, mapa_shared(smem_u32(&full[st]), lead), 0, yb, kc, b);
+            else
+                tma_load_4d(sb, &tmB, &full[st], 0, yb, kc, b);
+        };
+        const int amask = a_parts - 1;                       // a_parts is 1 or 2
+        int pre = 0;
+        if (do_a) {
+            for (int t = tile0; t < num_tiles && pre < nst; t += tstep) {
+                const TileCoord c = decode(p, t, nks, prank);
+                for (int ks = c.kb_begin; ks < c.kb_end && pre < nst; ++ks, ++pre)
+                    if ((pre & amask) == a_part) issue_a(pre, ks * kpb, c.mb * 128);
             }
         }
+        if (do_b) pdl_wait();
+        int it = 0;
+        int s = 0;                 // ring slot of `it`, and the parity of its use (it / nst) & 1
+        uint32_t ph = 0;
+        for (int t = tile0; t < num_tiles && !*s_abort; t += tstep) {
+            const TileCoord c = decode(p, t, nks, prank);
+            const int kb0 = c.kb_begin * kpb;
+            const int tap = kb0 / kpt;                       // conv tap and K block within it
+            int kc = kb0 - tap * kpt;
+            int yb = c.t0 + prank * bh + tap - p.pad;        // first token row of the B tile
+            const int ya = c.mb * 128;
+            bool ok = true;
+            for (int ks = c.kb_begin; ks < c.kb_end; ++ks, ++it) {
+                const int cs = s;
+                const uint32_t cph = ph;
+                if (++s == nst) { s = 0; ph ^= 1; }
+                const bool a_now = do_a && it >= pre && (it & amask) == a_part;   // first stages went out early
+                if (it >= nst && (a_now || do_b) && !mbar_wait(&empty[cs], cph ^ 1, s_abort, p.err, DEV_TIMEOUT_EMPTY)) {
+                    ok = false;
+                    break;
+                }
+                if (a_now) issue_a(cs, ks * kpb, ya);
+                if (do_b) issue_b(cs, kc, yb, c.b);
+                kc += kpb;
+                if (kc == kpt) { kc = 0; ++yb; }              // next tap: the token window moves by one
+            }
+            if (!ok) break;
+        }
+        if (*s_abort && !PAIR) {
+            // Let this thread's copies still in flight land before the CTA exits (one deadline).
+            const int issued = it > pre ? it : pre;
+            const unsigned long long t_start = globaltimer();
+            for (int i = (issued > nst ? issued - nst : 0); i < issued; ++i) {
+                uint64_t * bar = (p.a_q8 && do_a) ? &rfull[i % nst] : &full[i % nst];
+                while (!mbar_try_wait(bar, (i / nst) & 1) && globaltimer() - t_start < kWaitNs) {}
+            }
+        }
+    };
+
+    if (warp == 0) {
+        if (lane == 0) produce(p.a_q8 ? 3 : 1, 0, p.a_q8 ? 1 : 2);
     } else if (warp == 1) {
-        if (lane == 0) {
-            // ---------------- MMA issuer ----------------
-            const uint32_t idesc = make_idesc_f16(128, p.BN, true);
+        if (lane == 0 && prank == 0) {
+            // ---------------- MMA issuer (a pair's leader issues for both CTAs) ----------------
+            const uint32_t idesc = make_idesc_f16(PAIR ? 256 : 128, p.BN, true);
+            const uint16_t pmask = (uint16_t)(3u << lead);
             int it = 0, lt = 0;
             int s = 0;                 // ring slot of `it` and the parity of its fill
             uint32_t ph = 0;
             bool ok = true;
-            for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x, ++lt) {
-                const TileCoord c = decode(p, t, nkb);
+            for (int t = tile0; ok && t < num_tiles; t += tstep, ++lt) {
+                const TileCoord c = decode(p, t, nks, prank);
                 const int buf = lt & 1;
-                if (lt >= 2 && !mbar_wait(&acc_empty[buf], ((lt >> 1) & 1) ^ 1, s_abort, p.err, DEV_TIMEOUT_ACC)) break;
+                if (lt >= 2) {
+                    const uint32_t par = ((lt >> 1) & 1) ^ 1;
+                    if (!(PAIR ? mbar_wait_cluster(&acc_empty[buf], par, p.err, DEV_TIMEOUT_ACC)
+                                 : mbar_wait(&acc_empty[buf], par, s_abort, p.err, DEV_TIMEOUT_ACC)))
+                        break;
+                }
                 tc_fence_after();
                 const uint32_t dacc = tmem + buf * 256;
                 for (int kb = c.kb_begin; kb < c.kb_end; ++kb, ++it) {
@@ -696,17 +748,28 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     if (++s == nst) { s = 0; ph ^= 1; }
                     tc_fence_after();
                     const uint32_t sa = smem_u32(smem + cs * sbytes);
-                    const uint64_t adesc = make_sdesc_sw128(sa);
-                    const uint64_t bdesc = make_sdesc_sw128(sa + kABytes);
+                    for (int j = 0; j < kpb; ++j) {
+                        const uint64_t adesc = make_sdesc_sw128(sa + j * kABytes);
+                        const uint64_t bdesc = make_sdesc_sw128(sa + kpb * kABytes + j * b_bytes);
+                        const uint32_t acc0 = (kb > c.kb_begin || j > 0) ? 1u : 0u;
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        umma_f16_ss(dacc, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb > c.kb_begin || kk > 0) ? 1u : 0u);
-                    umma_commit(&empty[cs]);
+                        for (int kk = 0; kk < 4; ++kk) {
+                            if constexpr (PAIR) umma_f16_ss_pair(dacc, adesc + 2 * kk, bdesc + 2 * kk, idesc, (acc0 | kk) ? 1u : 0u);
+                            else umma_f16_ss(dacc, adesc + 2 * kk, bdesc + 2 * kk, idesc, (acc0 | kk) ? 1u : 0u);
+                        }
+                    }
+                    if constexpr (PAIR) umma_commit_pair(&empty[cs], pmask);
+                    else umma_commit(&empty[cs]);
                 }
-                umma_commit(&acc_full[buf]);
+                if constexpr (PAIR) umma_commit_pair(&acc_full[buf], pmask);
+                else umma_commit(&acc_full[buf]);
             }
         }
     } else if (warp >= 6) {
+        if (!p.a_q8 && lane == 0) {
+            if (warp == 6) produce(2, 0, 1);                    // activation tiles
+            else produce(1, 1, 2);                              // weight tiles of odd K steps
+        }
         // ---------------- Q8_0 converters (warps 6, 7) ----------------
         // Each stage's int8 tile (128 rows x 64, row-major) and its scales ([2 blocks][128 rows]
         // f16) become the bf16 A tile in the 128-byte-swizzled layout TMA would have written:
@@ -716,8 +779,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const int t64 = (warp - 6) * 32 + lane;
             int s = 0;
             uint32_t ph = 0;
-            for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-                const TileCoord c = decode(p, t, nkb);
+            for (int t = tile0; t < num_tiles; t += tstep) {
+                const TileCoord c = decode(p, t, nks, prank);    // kpb = 1 on this path
                 bool ok = true;
                 for (int kb = c.kb_begin; kb < c.kb_end; ++kb) {
                     if (!mbar_wait(&rfull[s], ph, s_abort, p.err, DEV_TIMEOUT_FULL)) { ok = false; break; }
@@ -769,8 +832,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         int nqk = 0;                                  // QKV: chunks that took the RMS exchange barrier
         int gl = 0;                                   // thread 64: residual / gate loads issued
         int lt = 0;
-        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++lt) {
-            const TileCoord c = decode(p, t, nkb);
+        // TMEM buffer `buf` is free again: on the pair leader's barrier for both CTAs
+        const auto release_acc = [&](int buf) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if (PAIR && prank) mbar_arrive_remote(mapa_shared(smem_u32(&acc_empty[buf]), lead));
+                else mbar_arrive(&acc_empty[buf]);
+            }
+        };
+        for (int t = tile0; t < num_tiles; t += tstep, ++lt) {
+            const TileCoord c = decode(p, t, nks, prank);
             const int buf = lt & 1;
             EpiCtx e;
             // output feature of this thread (SwiGLU: rows 2i / 2i + 1 are w1 / w3 of feature i)
@@ -887,23 +959,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         else emit_store<EK>(p, e, j0, v);
                     }
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                release_acc(buf);
                 if (failed) break;
             } else if (p.csplit) {
                 // Split-K inside the cluster (one tile per CTA; the operand stages are idle now):
                 // partial tile -> own shared memory; the row slices the other ranks finish are
                 // pushed into their receive slots by bulk copies that complete on their barrier;
                 // then this CTA's slice is summed over all ranks and finished.
-                const int rank = (int)cluster_ctarank();
+                // splits are ranks 0..splits-1 (pairs: cluster rank 2 * split + prank)
+                const int rank = srank;
+                const auto crk = [&](int d) { return (uint32_t)(PAIR ? 2 * d + prank : d); };
                 const int rows_max = slice_rows_max(p.BN, p.splits);
                 const int lo = slice_lo(rank, p.BN, p.splits), hi = slice_lo(rank + 1, p.BN, p.splits);
                 float * part = reinterpret_cast<float *>(smem);                  // [BN][128]
                 float * recv = part + (size_t)p.BN * 128;                         // [splits - 1][rows_max][128]
                 if (threadIdx.x == 64) {     // the MMAs are done: this CTA's stages may now be written by peers
                     for (int d = 0; d < p.splits; ++d)
-                        if (d != rank) mbar_arrive_remote(mapa_shared(smem_u32(&cbar[2]), (uint32_t)d));
+                        if (d != rank) mbar_arrive_remote(mapa_shared(smem_u32(&cbar[2]), crk(d)));
                 }
                 for (int j0 = 0; j0 < p.BN; j0 += 32) {
                     float v[32];
@@ -912,9 +984,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     for (int j = 0; j < 32; ++j)
                         if (j0 + j < p.BN) part[(j0 + j) * 128 + ml] = v[j];
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                release_acc(buf);
                 fence_proxy_async_smem();
                 epi_bar();
                 // push once every peer's stages are free (a timed-out wait sends nothing)
@@ -924,16 +994,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         const int dlo = slice_lo(d, p.BN, p.splits), dhi = slice_lo(d + 1, p.BN, p.splits);
                         if (dhi <= dlo) continue;
                         const int slot = rank < d ? rank : rank - 1;          // this rank's slot at d
-                        const uint32_t dst = mapa_shared(smem_u32(recv + (size_t)slot * rows_max * 128), (uint32_t)d);
+                        const uint32_t dst = mapa_shared(smem_u32(recv + (size_t)slot * rows_max * 128), crk(d));
                         bulk_copy_to_peer(dst, part + (size_t)dlo * 128, (uint32_t)(dhi - dlo) * 512u,
-                                          mapa_shared(smem_u32(&cbar[0]), (uint32_t)d));
+                                          mapa_shared(smem_u32(&cbar[0]), crk(d)));
                     }
                 }
                 // the other ranks' rows of this slice have landed (byte count on cbar[0])
                 if (__all_sync(0xffffffffu, mbar_wait_cluster(&cbar[0], 0, p.err, DEV_TIMEOUT_CLUSTER))) {
                     if (threadIdx.x == 64) {                                       // tell the senders
                         for (int d = 0; d < p.splits; ++d)
-                            if (d != rank) mbar_arrive_remote(mapa_shared(smem_u32(&cbar[1]), (uint32_t)d));
+                            if (d != rank) mbar_arrive_remote(mapa_shared(smem_u32(&cbar[1]), crk(d)));
                     }
                     finish_slice<EK>(p, &tmO, &tmG, c, e, part, recv, rows_max, rank, lo, hi, ml, lane, ebuf, ebar, gs, gl);
                 }
@@ -950,9 +1020,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     for (int j = 0; j < 32; ++j)
                         if (j0 + j < p.BN) __stcg(wsp + (size_t)(j0 + j) * 128, v[j]);
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                release_acc(buf);
                 __threadfence();
                 epi_bar();
                 if (threadIdx.x == 64) *s_last = (atomicAdd(&p.counters[c.otile], 1) == p.splits - 1);
@@ -975,10 +1043,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
     }
     tc_fence_before();
-    __syncthreads();
+    __syncwarp();
+    // a pair's CTAs signal each other's barriers and the leader's MMAs read the peer's shared
+    // memory and write its tensor memory: neither leaves before both are done
+    if (PAIR) cluster_sync_all();
+    else __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTmemCols);
+        if constexpr (PAIR) tmem_dealloc_pair(tmem, kTmemCols);
+        else tmem_dealloc(tmem, kTmemCols);
     }
 }
 
@@ -1047,7 +1120,7 @@ static int max_active_clusters(int cs) {
     if (dev < 0 || dev >= 64 || cs < 1 || cs > 8) return 0;
     if (!done[dev]) {
         done[dev] = true;
-        cudaFuncSetAttribute(gemm_tc_kernel<EK_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        cudaFuncSetAttribute(gemm_tc_kernel<EK_F32, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
         int sms = 148;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         for (int k = 1; k <= 8; ++k) {
@@ -1061,7 +1134,7 @@ static int max_active_clusters(int cs) {
             cfg.attrs = at;
             cfg.numAttrs = 1;
             int n = 0;
-            if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<EK_F32>, &cfg) != cudaSuccess) {
+            if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<EK_F32, false>, &cfg) != cudaSuccess) {
                 cudaGetLastError();
                 n = 0;
             }
@@ -1083,37 +1156,64 @@ static int max_active_clusters(int cs) {
 // arriving CTA was measured at ~40000 cycles.
 struct TileChoice {
     double cost;
-    int BN, splits;
+    int BN, splits, pair;
 };
-// Every feasible (BN, splits), cheapest first by the model.
+// CTA pairs (cta_group::2) halve the token bytes each SM draws: a pair computes 256 weight
+// rows x BN tokens, each CTA loading its 128 weight rows and BN / 2 tokens. They need an even
+// m-block count, a cluster of 2 (x the splits for a cluster split-K) and bf16 weights.
+static bool pairs_enabled() {       // read per plan: tests compare both forms in one process
+    const char * e = getenv("TSD_NO_PAIR");
+    return !(e && *e && *e != '0');
+}
+// Every feasible (BN, splits, pair), cheapest first by the model.
 static std::vector<TileChoice> tile_choices(int S, int nbatch, int mblocks, int nkb, int num_sms, int max_splits,
-                                            long long ws_floats, int n_counters, bool allow_cluster) {
+                                            long long ws_floats, int n_counters, bool allow_cluster, bool allow_pair,
+                                            bool k128, bool q8) {
     std::vector<TileChoice> out;
-    for (int bn = 16; bn <= 256; bn += 16) {
-        const int nt = (S + bn - 1) / bn;
-        if (nt > 1 && ((S + nt - 1) / nt + 15) / 16 * 16 < bn) continue;   // a smaller bn gives the same count
-        const long long otiles = (long long)mblocks * nbatch * nt;
-        for (int sp = 1; sp <= std::min(8, std::max(1, max_splits)); ++sp) {   // reducers sum <= 8 partials
-            if (sp > 1 && nkb / sp < 4) break;
-            const long long tiles = otiles * sp;
-            bool cluster = allow_cluster && sp > 1 && tiles <= num_sms;
-            if (cluster) {   // partial tile + receive slots fit the operand stages; clusters co-resident
-                const int rows_max = 16 * (((bn >> 4) + sp - 1) / sp);
-                const int mac = max_active_clusters(sp);
-                cluster = (long long)bn * 512 + (long long)(sp - 1) * rows_max * 512 <= (long long)kStageArea &&
-                          mac > 0 && otiles <= mac;
+    for (int pair = 0; pair <= 1; ++pair) {
+        if (pair && (!allow_pair || !allow_cluster || mblocks % 2 || !pairs_enabled() || max_active_clusters(2) < 1))
+            continue;
+        const int cpt = pair ? 2 : 1;                         // CTAs per tile
+        for (int bn = 16; bn <= 256; bn += 16) {
+            const int nt = (S + bn - 1) / bn;
+            if (nt > 1 && ((S + nt - 1) / nt + 15) / 16 * 16 < bn) continue;   // a smaller bn gives the same count
+            const long long otiles = (long long)(mblocks / cpt) * nbatch * nt;  // output tiles (pair tiles)
+            for (int sp = 1; sp <= std::min(8, std::max(1, max_splits)); ++sp) {   // reducers sum <= 8 partials
+                if (sp > 1 && nkb / sp < 4) break;
+                const long long ctas = otiles * sp * cpt;
+                bool cluster = allow_cluster && sp > 1 && ctas <= num_sms && cpt * sp <= 8;
+                if (cluster) {   // partial tile + receive slots fit the operand stages; clusters co-resident
+                    const int rows_max = 16 * (((bn >> 4) + sp - 1) / sp);
+                    const int mac = max_active_clusters(cpt * sp);
+                    cluster = (long long)bn * 512 + (long long)(sp - 1) * rows_max * 512 <= (long long)kStageArea &&
+                              mac > 0 && otiles <= mac;
+                }
+                if (sp > 1 && !cluster && (pair || otiles * cpt > n_counters || otiles * cpt * sp * bn * 128 > ws_floats))
+                    continue;                                  // pairs split K only inside the cluster
+                const long long slots = pair ? std::min<long long>(num_sms & ~1, 2ll * max_active_clusters(2)) : num_sms;
+                const long long waves = (ctas + slots - 1) / slots;
+                const double kb = (double)nkb / sp;                          // K blocks per tile
+                const double kb_bytes = 16384.0 + 128.0 * bn / cpt;          // per CTA and K block
+                const double tile_bytes = kb * kb_bytes;
+                const long long wave_ctas = std::min<long long>(ctas, slots);
+                // per stage of kpb K blocks: the MMAs (a K=16 MMA takes max(65, N / 2) cycles, N the
+                // instruction's N: BN, also for pairs), plus what the issuer loses at its barrier
+                // wait (~250 cycles, hidden only behind enough queued MMA work); at least one TMA
+                // instruction of the B issuer (~300 cycles each). Per SM intake <= ~110 B / cycle.
+                const int b_atom = (int)(128 * bn / cpt);
+                const int kpb = (k128 && !q8 && kStageArea / (2 * (kABytes + b_atom)) >= 3 && nkb % (2 * sp) == 0 &&
+                                 nkb / (2 * sp) >= 2) ? 2 : 1;
+                const double mi = std::max(65.0, bn / 2.0);
+                const double ex = 4.0 * kpb * mi;
+                const double idle = kpb == 1 ? std::max(250.0 - (mi >= 100.0 ? ex - 260.0 : 0.0), 0.0) : (mi < 100.0 ? 244.0 : 0.0);
+                const double t_stage = std::max(ex + idle, q8 ? 600.0 : 300.0);
+                const double t_sm = kb * std::max(t_stage / kpb, kb_bytes / 110.0);
+                const double t_l2 = (double)wave_ctas * tile_bytes / 12000.0;
+                const double epi = bn * 128.0 * 4.0 / 20.0;
+                const double reduce = sp == 1 ? 0.0 : cluster ? 2000.0 + bn * 512.0 * 2.0 / 100.0 : 40000.0;
+                const double cost = (double)waves * (std::max(t_sm, t_l2) + 3000.0) + epi + reduce;
+                out.push_back({cost, bn, sp, pair});
             }
-            if (sp > 1 && !cluster && (otiles > n_counters || otiles * sp * bn * 128 > ws_floats)) continue;
-            const long long waves = (tiles + num_sms - 1) / num_sms;
-            const double kb = (double)nkb / sp;                          // K blocks per tile
-            const double tile_bytes = kb * (16384.0 + 128.0 * bn);
-            const long long wave_tiles = std::min<long long>(tiles, num_sms);
-            const double t_sm = kb * 2.0 * bn + tile_bytes / 100.0;
-            const double t_l2 = (double)wave_tiles * tile_bytes / 5000.0;
-            const double epi = bn * 128.0 * 4.0 / 20.0;
-            const double reduce = sp == 1 ? 0.0 : cluster ? 2000.0 + bn * 512.0 * 2.0 / 100.0 : 40000.0;
-            const double cost = (double)waves * (std::max(t_sm, t_l2) + 3000.0) + epi + reduce;
-            out.push_back({cost, bn, sp});
         }
     }
     std::stable_sort(out.begin(), out.end(), [](const TileChoice & a, const TileChoice & b) { return a.cost < b.cost; });
@@ -1121,15 +1221,16 @@ static std::vector<TileChoice> tile_choices(int S, int nbatch, int mblocks, int 
 }
 
 int gemm_candidates(int M, int K_in, int taps, int nbatch, int S, int num_sms, int max_splits, long long ws_floats,
-                    int n_counters, bool allow_cluster, int max_out, int * bn, int * splits) {
+                    int n_counters, bool allow_cluster, int max_out, int * bn, int * splits, int * pair) {
     if (M % 128 || K_in % 64 || taps < 1 || S < 1 || nbatch < 1) return 0;
     const auto c = tile_choices(S, nbatch, M / 128, taps * (K_in / 64), num_sms, max_splits, ws_floats, n_counters,
-                                allow_cluster);
+                                allow_cluster, true, K_in % 128 == 0, false);
     int n = 0;
     for (const TileChoice & t : c) {
         if (n >= max_out) break;
         bn[n] = t.BN;
         splits[n] = t.splits;
+        if (pair) pair[n] = t.pair;
         ++n;
     }
     return n;
@@ -1140,10 +1241,13 @@ long long gemm_ws_floats(const GemmLaunch & L) {
     return p.splits > 1 && !p.csplit ? (long long)p.mblocks * p.nbatch * p.n_tiles * p.splits * p.BN * 128 : 0;
 }
 
+static bool make_tmap_4d(CUtensorMap * m, const void * ptr, CUtensorMapDataType dt, int esize, const uint64_t (&d)[4],
+                         const uint64_t (&stride_bytes)[3], const uint32_t (&box)[4], bool sw128);
+
 bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pad, int swiglu, const void * X,
                int nbatch, int S, long long x_row_stride, long long x_batch_stride, int num_sms, int max_splits,
                long long ws_floats, int n_counters, bool allow_cluster, int force_bn, int force_splits,
-               const void * q8_scales) {
+               const void * q8_scales, int force_pair) {
     if (M % 128 || K_in % 64 || taps < 1 || S < 1 || nbatch < 1) return false;
     if (q8_scales && taps != 1) return false;
     GemmParams & p = L.p;
@@ -1155,20 +1259,35 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
     const int nkb = taps * (K_in / 64);
     {
         // the model's best choice, or the requested one if it is among the feasible choices
-        const auto c = tile_choices(S, nbatch, p.mblocks, nkb, num_sms, max_splits, ws_floats, n_counters, allow_cluster);
+        // the same choice as for bf16 weights (the Q8_0 path must sum in the same order)
+        const auto c = tile_choices(S, nbatch, p.mblocks, nkb, num_sms, max_splits, ws_floats, n_counters, allow_cluster,
+                                    q8_scales == nullptr && force_pair != 0, K_in % 128 == 0, false);
         if (c.empty()) return false;
         TileChoice t = c[0];
+        if (force_pair < 0 && getenv("TSD_FORCE_PAIR")) force_pair = 1;   // tests: exercise the pair form
+        if (force_pair == 1)          // the model's best pair choice
+            for (const TileChoice & x : c)
+                if (x.pair) { t = x; break; }
         for (const TileChoice & x : c)
-            if (force_bn > 0 && x.BN == force_bn && x.splits == force_splits) t = x;
+            if (force_bn > 0 && x.BN == force_bn && x.splits == force_splits && (force_pair < 0 || x.pair == force_pair)) {
+                t = x;
+                break;
+            }
         p.BN = t.BN;
         p.n_tiles = (S + t.BN - 1) / t.BN;
         p.splits = t.splits;
+        p.pair = t.pair;
         p.a_q8 = q8_scales != nullptr;
-        p.stages = std::min(kMaxStages, kStageArea / (kABytes + p.BN * 128 + (p.a_q8 ? kQ8Bytes : 0)));
+        // two K blocks per stage when K allows (no stage straddles a conv tap), each split keeps
+        // whole stages, and at least 3 stages fit; else one
+        const int b_atom = (p.pair ? p.BN / 2 : p.BN) * 128;
+        const int st2 = kStageArea / (2 * (kABytes + b_atom));
+        p.kpb = (!p.a_q8 && K_in % 128 == 0 && st2 >= 3 && nkb % (2 * p.splits) == 0 && nkb / (2 * p.splits) >= 2) ? 2 : 1;
+        p.stages = std::min(kMaxStages, kStageArea / (p.kpb * (kABytes + b_atom) + (p.a_q8 ? kQ8Bytes : 0)));
     }
     if (getenv("TSD_DEBUG_PLAN")) {
-        fprintf(stderr, "tsd plan: M=%d K=%d taps=%d nbatch=%d S=%d -> BN=%d tiles/item=%d splits=%d | max active clusters",
-                M, K_in, taps, nbatch, S, p.BN, p.n_tiles, p.splits);
+        fprintf(stderr, "tsd plan: M=%d K=%d taps=%d nbatch=%d S=%d -> BN=%d tiles/item=%d splits=%d pair=%d kpb=%d stages=%d | max active clusters",
+                M, K_in, taps, nbatch, S, p.BN, p.n_tiles, p.splits, p.pair, p.kpb, p.stages);
         for (int k = 2; k <= 8; ++k) fprintf(stderr, " %d:%d", k, max_active_clusters(k));
         fprintf(stderr, "\n");
     }
@@ -1177,18 +1296,23 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
         const char * o = getenv("TSD_TILE_ORDER");
         p.order = (o && *o == '1') ? 1 : 0;
     }
-    const long long tiles = (long long)p.mblocks * nbatch * p.n_tiles * p.splits;
+    const long long tiles = (long long)p.mblocks * nbatch * p.n_tiles * p.splits;   // CTA tiles
+    const int cpt = p.pair ? 2 : 1;
     // one wave of split tiles: the splits of an output tile run as one cluster (rank = split,
-    // which m-block-major order makes consecutive)
+    // which m-block-major order makes consecutive; pairs: rank = 2 * split + half)
     {
         const int rows_max = 16 * (((p.BN >> 4) + p.splits - 1) / p.splits);
-        const int mac = p.splits > 1 ? max_active_clusters(p.splits) : 0;
+        const int mac = p.splits > 1 && cpt * p.splits <= 8 ? max_active_clusters(cpt * p.splits) : 0;
         p.csplit = allow_cluster && p.splits > 1 && tiles <= num_sms && mac > 0 &&
-                   (long long)p.mblocks * nbatch * p.n_tiles <= mac &&
+                   (long long)(p.mblocks / cpt) * nbatch * p.n_tiles <= mac &&
                    (long long)p.BN * 512 + (long long)(p.splits - 1) * rows_max * 512 <= (long long)kStageArea;
     }
-    if (p.csplit) p.order = 0;
-    L.grid = dim3((unsigned)std::min<long long>(tiles, num_sms), 1, 1);
+    if (p.csplit || p.pair) p.order = 0;
+    {
+        long long g = std::min<long long>(tiles, num_sms);
+        if (p.pair && !p.csplit) g = std::min<long long>(g, 2ll * max_active_clusters(2)) & ~1ll;   // whole pairs, co-resident
+        L.grid = dim3((unsigned)g, 1, 1);
+    }
     if (q8_scales) {
         // int8 plane: 64 x 128 boxes (64-byte rows, no swizzle); scales: 128 rows x 2 blocks
         if (!make_tmap_2d(&L.tmA, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K_in, (uint64_t)M, (uint64_t)K_in, 64,
@@ -1196,17 +1320,21 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
             !make_tmap_2d(&L.tmS, q8_scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)M, (uint64_t)K_in / 32,
                           (uint64_t)M * 2, 128, 2))
             return false;
-    } else if (!make_tmap_2d(&L.tmA, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)taps * K_in, (uint64_t)M,
-                             (uint64_t)taps * K_in * 2, 64, 128))
-        return false;
-    if (!make_tmap_3d(&L.tmB, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K_in, (uint64_t)S, (uint64_t)nbatch,
-                      (uint64_t)x_row_stride * 2, (uint64_t)x_batch_stride * 2, 64, p.BN, 1))
-        return false;
+    } else if (!make_tmap_3d(&L.tmA, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, (uint64_t)M, (uint64_t)nkb,
+                             (uint64_t)taps * K_in * 2, 128, 64, 128, (uint32_t)p.kpb))
+        return false;   // weights as [K atom][row][64]: one box = kpb atoms of 128 rows
+    {
+        // activations as [item][K atom][token][64]: one box = kpb atoms of the B tile's tokens
+        const uint64_t d[4] = {64, (uint64_t)S, (uint64_t)(K_in / 64), (uint64_t)nbatch};
+        const uint64_t st[3] = {(uint64_t)x_row_stride * 2, 128, (uint64_t)x_batch_stride * 2};
+        const uint32_t box[4] = {64, (uint32_t)(p.pair ? p.BN / 2 : p.BN), (uint32_t)p.kpb, 1};
+        if (!make_tmap_4d(&L.tmB, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d, st, box, true)) return false;
+    }
     return true;
 }
 
 static bool make_tmap_4d(CUtensorMap * m, const void * ptr, CUtensorMapDataType dt, int esize, const uint64_t (&d)[4],
-                         const uint64_t (&stride_bytes)[3], const uint32_t (&box)[4]) {
+                         const uint64_t (&stride_bytes)[3], const uint32_t (&box)[4], bool sw128) {
     auto fn = encode_fn();
     if (!fn || (reinterpret_cast<uintptr_t>(ptr) & 15) || (box[0] * esize) % 16) return false;
     for (int i = 0; i < 3; ++i)
@@ -1216,8 +1344,8 @@ static bool make_tmap_4d(CUtensorMap * m, const void * ptr, CUtensorMapDataType 
     cuuint32_t bx[4] = {box[0], box[1], box[2], box[3]};
     cuuint32_t es[4] = {1, 1, 1, 1};
     return fn(m, dt, 4, const_cast<void *>(ptr), dims, strides, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
-           CUDA_SUCCESS;
+              sw128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 void gemm_finalize(GemmLaunch & L) {
@@ -1241,9 +1369,9 @@ void gemm_finalize(GemmLaunch & L) {
         const uint32_t box[4] = {64, 16, 1, 1};
         const long long off = (long long)p.s_off * 64;
         p.epi_tma = p.nbatch * p.S == p.nbatch * p.s_item &&
-                    make_tmap_4d(&L.tmO, p.q_out + off, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, d, st, box) &&
-                    make_tmap_4d(&L.tmG, p.k_out + off, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, d, st, box) &&
-                    make_tmap_4d(&L.tmV, p.v_out + off, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, d, st, box);
+                    make_tmap_4d(&L.tmO, p.q_out + off, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, d, st, box, false) &&
+                    make_tmap_4d(&L.tmG, p.k_out + off, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, d, st, box, false) &&
+                    make_tmap_4d(&L.tmV, p.v_out + off, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, d, st, box, false);
     } else if (p.mode == EPI_GATE_RESID) {
         const bool gtile = p.gate_div == 1;
         {
@@ -1251,8 +1379,8 @@ void gemm_finalize(GemmLaunch & L) {
             const uint64_t sr[3] = {(uint64_t)p.ldr * 4, S * p.ldr * 4, S * nb * p.ldr * 4};
             const uint64_t sg[3] = {(uint64_t)p.ldg * 4, S * p.ldg * 4, S * nb * p.ldg * 4};
             const uint32_t box[4] = {128, 16, 1, 1};
-            p.epi_tma = make_tmap_4d(&L.tmO, p.resid, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d, sr, box) &&
-                        (!gtile || make_tmap_4d(&L.tmG, p.gate, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d, sg, box));
+            p.epi_tma = make_tmap_4d(&L.tmO, p.resid, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d, sr, box, false) &&
+                        (!gtile || make_tmap_4d(&L.tmG, p.gate, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d, sg, box, false));
         }
     } else {
         const int es = p.out_bf16 ? 2 : 4;
@@ -1262,11 +1390,11 @@ void gemm_finalize(GemmLaunch & L) {
         if (p.out_cblk == 0) {
             const uint64_t d[4] = {(uint64_t)p.m_valid, S, nb, 1};
             const uint64_t st[3] = {(uint64_t)p.ldo * es, S * p.ldo * es, S * nb * p.ldo * es};
-            p.epi_tma = make_tmap_4d(&L.tmO, p.out, dt, es, d, st, box);
+            p.epi_tma = make_tmap_4d(&L.tmO, p.out, dt, es, d, st, box, false);
         } else if (p.out_cblk % fw == 0 && p.m_valid % p.out_cblk == 0) {
             const uint64_t d[4] = {(uint64_t)p.out_cblk, S, nb, (uint64_t)(p.m_valid / p.out_cblk)};
             const uint64_t st[3] = {(uint64_t)p.ldo * es, S * p.ldo * es, (uint64_t)p.out_cstride * es};
-            p.epi_tma = make_tmap_4d(&L.tmO, p.out, dt, es, d, st, box);
+            p.epi_tma = make_tmap_4d(&L.tmO, p.out, dt, es, d, st, box, false);
         }
     }
     if (getenv("TSD_NO_TMA_EPILOGUE")) p.epi_tma = 0;
@@ -1274,14 +1402,18 @@ void gemm_finalize(GemmLaunch & L) {
 }
 
 namespace {
-template <int EK> cudaError_t launch_kind(cudaLaunchConfig_t & cfg, const GemmLaunch & L, const GemmParams & p) {
+template <int EK, bool PAIR> cudaError_t launch_form(cudaLaunchConfig_t & cfg, const GemmLaunch & L, const GemmParams & p) {
     static bool attr = false;   // per instance
     if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<EK>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        cudaError_t e =
+            cudaFuncSetAttribute(gemm_tc_kernel<EK, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<EK>, L.tmA, L.tmB, L.tmO, L.tmG, L.tmV, L.tmS, p);
+    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<EK, PAIR>, L.tmA, L.tmB, L.tmO, L.tmG, L.tmV, L.tmS, p);
+}
+template <int EK> cudaError_t launch_kind(cudaLaunchConfig_t & cfg, const GemmLaunch & L, const GemmParams & p) {
+    return p.pair ? launch_form<EK, true>(cfg, L, p) : launch_form<EK, false>(cfg, L, p);
 }
 }  // namespace
 
@@ -1302,9 +1434,9 @@ cudaError_t gemm_launch(const GemmLaunch & L0, cudaStream_t st) {
         at[na].val.programmaticStreamSerializationAllowed = 1;
         ++na;
     }
-    if (p.csplit) {
+    if (p.csplit || p.pair) {
         at[na].id = cudaLaunchAttributeClusterDimension;
-        at[na].val.clusterDim.x = (unsigned)p.splits;
+        at[na].val.clusterDim.x = (unsigned)((p.pair ? 2 : 1) * (p.csplit ? p.splits : 1));
         at[na].val.clusterDim.y = 1;
         at[na].val.clusterDim.z = 1;
         ++na;

@@ -35,6 +35,7 @@ struct GemmParams {
     int n_tiles;       // ceil(S / BN)
     int splits;        // split-K factor
     int stages;        // operand ring depth (set by gemm_plan from BN)
+    int kpb;           // K blocks of 64 per operand stage (1 or 2; 2 halves the TMA instructions per K)
     int a_q8;          // weights are planar Q8_0 (int8 [M][K] + f16 scales [K/32][M]), dequantised in smem
     int mode, act;
     int m_valid;       // features >= m_valid are not stored (zero-padded weight rows)
@@ -50,6 +51,8 @@ struct GemmParams {
     int vec;           // output buffers allow the split-K reducer's vector accesses
     int epi_tma;       // epilogue moves output (GATE_RESID: residual / gate) tiles with TMA
     int csplit;        // split-K through the cluster's shared memory (one wave; cluster = the splits of a tile)
+    int pair;          // CTA pairs (cta_group::2): 256 weight rows x BN tokens per pair, each CTA loading its
+                       // 128 rows and half the tokens; m-blocks even, no Q8_0 A, tile walk m-block-major
     // EPI_QKV: W rows are [Q | K | V] (H each, feature = head * 64 + d); out row = item * s_item + t
     __half * q_out, * k_out, * v_out;   // [item][nh][Sj][64], this stream's tokens at s_off
     const float * qg, * kg;             // RMSNorm gains [64]
@@ -88,11 +91,12 @@ bool make_tmap_3d(CUtensorMap * m, const void * ptr, CUtensorMapDataType dt, int
 bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pad, int swiglu,
                const void * X, int nbatch, int S, long long x_row_stride, long long x_batch_stride,
                int num_sms, int max_splits, long long ws_floats = 0, int n_counters = 0, bool allow_cluster = true,
-               int force_bn = 0, int force_splits = 0, const void * q8_scales = nullptr);
-// Up to max_out feasible (token tile, K splits) choices for a GEMM shape, best first by the cost
-// model; force_bn / force_splits in gemm_plan select one of them (plan-time autotuning).
+               int force_bn = 0, int force_splits = 0, const void * q8_scales = nullptr, int force_pair = -1);
+// Up to max_out feasible (token tile, K splits, CTA pair) choices for a GEMM shape, best first by
+// the cost model; force_bn / force_splits / force_pair in gemm_plan select one of them (plan-time
+// autotuning). force_pair: -1 the model's choice, 0 single CTAs only, 1 the best pair choice.
 int gemm_candidates(int M, int K_in, int taps, int nbatch, int S, int num_sms, int max_splits, long long ws_floats,
-                    int n_counters, bool allow_cluster, int max_out, int * bn, int * splits);
+                    int n_counters, bool allow_cluster, int max_out, int * bn, int * splits, int * pair = nullptr);
 // Workspace floats a planned launch needs (0 when it does not split K).
 long long gemm_ws_floats(const GemmLaunch & L);
 // After the epilogue fields of L.p are set: encode the epilogue tensor maps (TMA stores where the
