@@ -84,6 +84,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();   // launched with PDL: the Q / K / V writers have finished after this
 
     if (warp == 0) {
         if (lane == 0) {
@@ -265,7 +266,7 @@ cudaError_t attn_launch(const AttnLaunch & L, cudaStream_t st) {
     a.S = L.S; a.nh = L.nh; a.ldo = L.ldo; a.out = reinterpret_cast<__nv_bfloat16 *>(L.out); a.err = L.err;
     a.scale_log2 = L.scale * 1.4426950408889634f;
     dim3 grid((L.S + kQT - 1) / kQT, L.B * L.nh);
-    attn_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(L.tmQ, L.tmK, L.tmV, a);
+    launch_pdl(attn_tc_kernel, dim3(grid), dim3(kThreads), kSmemBytes, st, L.tmQ, L.tmK, L.tmV, a);
     return cudaGetLastError();
 }
 

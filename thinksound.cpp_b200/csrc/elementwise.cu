@@ -37,6 +37,7 @@ __global__ void ln_modulate_kernel(const float * __restrict__ x, int rows, int H
                                    const float * __restrict__ scale, long long ld_mod, int per_token, int rows_per_item,
                                    __nv_bfloat16 * __restrict__ y) {
     __shared__ float red[32];
+    pdl_wait();                // launched with PDL: the predecessor's writes are visible after this
     pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const int row = blockIdx.x;
     const int n4 = H >> 2;
@@ -85,6 +86,7 @@ __global__ void qk_norm_rope_kernel(const float * __restrict__ qkv, int B, int S
                                     const float * __restrict__ qg, const float * __restrict__ kg, int rope, float fscale,
                                     float theta, __half * __restrict__ Q, __half * __restrict__ K,
                                     __half * __restrict__ V, int Sj, int s_off) {
+    pdl_wait();                // launched with PDL: the predecessor's writes are visible after this
     pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -115,6 +117,7 @@ __global__ void qk_norm_rope_kernel(const float * __restrict__ qkv, int B, int S
 
 // The angle expression of qk_norm_rope_kernel, tabulated once per plan for the QKV GEMM epilogue.
 __global__ void rope_table_kernel(int S, float fscale, float theta, float2 * __restrict__ tab) {
+    pdl_wait();                // launched with PDL: earlier kernels are done with `tab`
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= S * 32) return;
     const int t = i >> 5, p = i & 31;
@@ -125,6 +128,7 @@ __global__ void rope_table_kernel(int S, float fscale, float theta, float2 * __r
 }
 
 __global__ void latent_to_tokens_kernel(const float * __restrict__ lat, int B, int C, int T, __nv_bfloat16 * __restrict__ y) {
+    pdl_wait();                // launched with PDL: the predecessor's writes are visible after this
     pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)B * C * T) return;
@@ -136,6 +140,7 @@ __global__ void latent_to_tokens_kernel(const float * __restrict__ lat, int B, i
 
 __global__ void sync_prep_kernel(const float * __restrict__ sync, int B, int S, int C, const float * __restrict__ pe,
                                  __nv_bfloat16 * __restrict__ y) {
+    pdl_wait();                // launched with PDL: the predecessor's writes are visible after this
     pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)B * S * C) return;
@@ -146,6 +151,7 @@ __global__ void sync_prep_kernel(const float * __restrict__ sync, int B, int S, 
 
 __global__ void text_prep_kernel(const float * __restrict__ text, int text_S, int text_dim, const float * __restrict__ t5,
                                  int t5_S, int t5_dim, int B, __nv_bfloat16 * __restrict__ y) {
+    pdl_wait();                // launched with PDL: the predecessor's writes are visible after this
     pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const int St = text_S + t5_S;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -160,6 +166,7 @@ __global__ void text_prep_kernel(const float * __restrict__ text, int text_S, in
 }
 
 __global__ void timestep_embed_kernel(const float * __restrict__ t, int B, int H, float max_period, float * __restrict__ y) {
+    pdl_wait();                // launched with PDL: the predecessor's writes are visible after this
     pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     const int half = H / 2;
@@ -173,6 +180,7 @@ __global__ void timestep_embed_kernel(const float * __restrict__ t, int B, int H
 }
 
 __global__ void seq_mean_kernel(const float * __restrict__ x, int B, int S, int H, float * __restrict__ y) {
+    pdl_wait();                // launched with PDL: the predecessor's writes are visible after this
     pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= B * H) return;
@@ -183,6 +191,7 @@ __global__ void seq_mean_kernel(const float * __restrict__ x, int B, int S, int 
 }
 
 __global__ void add_vec_kernel(const float * a, const float * b, int n, float * y) {
+    pdl_wait();                // launched with PDL: the predecessor's writes are visible after this
     pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) y[i] = a[i] + b[i];
@@ -190,6 +199,7 @@ __global__ void add_vec_kernel(const float * a, const float * b, int n, float * 
 
 __global__ void build_extended_kernel(const float * __restrict__ sync, int sync_S, const float * __restrict__ gc, int B,
                                       int T, int H, float * __restrict__ ext, __nv_bfloat16 * __restrict__ sext) {
+    pdl_wait();                // launched with PDL: the predecessor's writes are visible after this
     pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)B * T * H) return;
@@ -203,12 +213,14 @@ __global__ void build_extended_kernel(const float * __restrict__ sync, int sync_
 }
 
 __global__ void silu_vec_kernel(const float * __restrict__ x, int n, float * __restrict__ y) {
+    pdl_wait();                // launched with PDL: the predecessor's writes are visible after this
     pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) y[i] = silu_f(x[i]);
 }
 
 __global__ void cast_kernel(const float * __restrict__ x, long long n, __nv_bfloat16 * __restrict__ y) {
+    pdl_wait();                // launched with PDL: the predecessor's writes are visible after this
     pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) y[i] = __float2bfloat16_rn(x[i]);
@@ -216,6 +228,7 @@ __global__ void cast_kernel(const float * __restrict__ x, long long n, __nv_bflo
 
 __global__ void cfg_euler_kernel(const float * __restrict__ flow, int P, int T, int L, float cfg, float dt,
                                  float * __restrict__ x, float * __restrict__ flow0) {
+    pdl_wait();                // launched with PDL: the predecessor's writes are visible after this
     pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)P * L * T) return;
@@ -230,6 +243,7 @@ __global__ void cfg_euler_kernel(const float * __restrict__ flow, int P, int T, 
 }
 
 __global__ void dup_latent_kernel(const float * __restrict__ x, int P, int L, int T, float * __restrict__ lat2) {
+    pdl_wait();                // launched with PDL: the predecessor's writes are visible after this
     pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const long long per = (long long)L * T;
@@ -251,77 +265,77 @@ cudaError_t ln_modulate(const float * x, int rows, int H, const float * shift, c
     int threads = (n4 + kLnVec - 1) / kLnVec;
     threads = (threads + 31) / 32 * 32;
     if (threads > 1024 || (long long)threads * kLnVec < n4) return cudaErrorInvalidValue;
-    ln_modulate_kernel<<<rows, threads, 0, st>>>(x, rows, H, shift, scale, ld_mod, per_token, rows_per_item, y);
+    launch_pdl(ln_modulate_kernel, dim3(rows), dim3(threads), 0, st, x, rows, H, shift, scale, ld_mod, per_token, rows_per_item, y);
     return cudaGetLastError();
 }
 
 cudaError_t qk_norm_rope(const float * qkv, int B, int S, int H, int nh, const float * qg, const float * kg, int rope,
                          float fscale, float theta, __half * Q, __half * K, __half * V, int Sj, int s_off, cudaStream_t st) {
     if (H != nh * 64) return cudaErrorInvalidValue;
-    qk_norm_rope_kernel<<<nblk((long long)B * S * nh, 8), 256, 0, st>>>(qkv, B, S, H, nh, qg, kg, rope, fscale, theta, Q, K,
+    launch_pdl(qk_norm_rope_kernel, dim3(nblk((long long)B * S * nh, 8)), dim3(256), 0, st, qkv, B, S, H, nh, qg, kg, rope, fscale, theta, Q, K,
                                                                        V, Sj, s_off);
     return cudaGetLastError();
 }
 
 cudaError_t rope_table(int S, float fscale, float theta, float2 * tab, cudaStream_t st) {
-    rope_table_kernel<<<nblk((long long)S * 32, 256), 256, 0, st>>>(S, fscale, theta, tab);
+    launch_pdl(rope_table_kernel, dim3(nblk((long long)S * 32, 256)), dim3(256), 0, st, S, fscale, theta, tab);
     return cudaGetLastError();
 }
 
 cudaError_t latent_to_tokens(const float * lat, int B, int C, int T, __nv_bfloat16 * y, cudaStream_t st) {
-    latent_to_tokens_kernel<<<nblk((long long)B * C * T, 256), 256, 0, st>>>(lat, B, C, T, y);
+    launch_pdl(latent_to_tokens_kernel, dim3(nblk((long long)B * C * T, 256)), dim3(256), 0, st, lat, B, C, T, y);
     return cudaGetLastError();
 }
 
 cudaError_t sync_prep(const float * sync, int B, int S, int C, const float * pos_emb, __nv_bfloat16 * y, cudaStream_t st) {
-    sync_prep_kernel<<<nblk((long long)B * S * C, 256), 256, 0, st>>>(sync, B, S, C, pos_emb, y);
+    launch_pdl(sync_prep_kernel, dim3(nblk((long long)B * S * C, 256)), dim3(256), 0, st, sync, B, S, C, pos_emb, y);
     return cudaGetLastError();
 }
 
 cudaError_t text_prep(const float * text, int text_S, int text_dim, const float * t5, int t5_S, int t5_dim, int B,
                       __nv_bfloat16 * y, cudaStream_t st) {
-    text_prep_kernel<<<nblk((long long)B * (text_S + t5_S) * t5_dim, 256), 256, 0, st>>>(text, text_S, text_dim, t5, t5_S,
+    launch_pdl(text_prep_kernel, dim3(nblk((long long)B * (text_S + t5_S) * t5_dim, 256)), dim3(256), 0, st, text, text_S, text_dim, t5, t5_S,
                                                                                          t5_dim, B, y);
     return cudaGetLastError();
 }
 
 cudaError_t timestep_embed(const float * t, int B, int H, float max_period, float * y, cudaStream_t st) {
-    timestep_embed_kernel<<<nblk((long long)B * (H / 2), 256), 256, 0, st>>>(t, B, H, max_period, y);
+    launch_pdl(timestep_embed_kernel, dim3(nblk((long long)B * (H / 2), 256)), dim3(256), 0, st, t, B, H, max_period, y);
     return cudaGetLastError();
 }
 
 cudaError_t seq_mean(const float * x, int B, int S, int H, float * y, cudaStream_t st) {
-    seq_mean_kernel<<<nblk((long long)B * H, 256), 256, 0, st>>>(x, B, S, H, y);
+    launch_pdl(seq_mean_kernel, dim3(nblk((long long)B * H, 256)), dim3(256), 0, st, x, B, S, H, y);
     return cudaGetLastError();
 }
 
 cudaError_t add_vec(const float * a, const float * b, int n, float * y, cudaStream_t st) {
-    add_vec_kernel<<<nblk(n, 256), 256, 0, st>>>(a, b, n, y);
+    launch_pdl(add_vec_kernel, dim3(nblk(n, 256)), dim3(256), 0, st, a, b, n, y);
     return cudaGetLastError();
 }
 
 cudaError_t build_extended(const float * sync, int sync_S, const float * gc, int B, int T, int H, float * ext,
                            __nv_bfloat16 * sext, float * sgc, cudaStream_t st) {
-    build_extended_kernel<<<nblk((long long)B * T * H, 256), 256, 0, st>>>(sync, sync_S, gc, B, T, H, ext, sext);
+    launch_pdl(build_extended_kernel, dim3(nblk((long long)B * T * H, 256)), dim3(256), 0, st, sync, sync_S, gc, B, T, H, ext, sext);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    silu_vec_kernel<<<nblk((long long)B * H, 256), 256, 0, st>>>(gc, B * H, sgc);
+    launch_pdl(silu_vec_kernel, dim3(nblk((long long)B * H, 256)), dim3(256), 0, st, gc, B * H, sgc);
     return cudaGetLastError();
 }
 
 cudaError_t cast_f32_bf16(const float * x, long long n, __nv_bfloat16 * y, cudaStream_t st) {
-    cast_kernel<<<nblk(n, 256), 256, 0, st>>>(x, n, y);
+    launch_pdl(cast_kernel, dim3(nblk(n, 256)), dim3(256), 0, st, x, n, y);
     return cudaGetLastError();
 }
 
 cudaError_t cfg_euler(const float * flow, int P, int T, int L, float cfg, float dt, float * x, float * flow0,
                       cudaStream_t st) {
-    cfg_euler_kernel<<<nblk((long long)P * L * T, 256), 256, 0, st>>>(flow, P, T, L, cfg, dt, x, flow0);
+    launch_pdl(cfg_euler_kernel, dim3(nblk((long long)P * L * T, 256)), dim3(256), 0, st, flow, P, T, L, cfg, dt, x, flow0);
     return cudaGetLastError();
 }
 
 cudaError_t dup_latent(const float * x, int P, int L, int T, float * lat2, cudaStream_t st) {
-    dup_latent_kernel<<<nblk((long long)P * L * T, 256), 256, 0, st>>>(x, P, L, T, lat2);
+    launch_pdl(dup_latent_kernel, dim3(nblk((long long)P * L * T, 256)), dim3(256), 0, st, x, P, L, T, lat2);
     return cudaGetLastError();
 }
 

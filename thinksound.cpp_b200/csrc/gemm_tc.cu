@@ -8,14 +8,16 @@
 // epilogue, so no separate elementwise kernel touches HBM for them.
 //
 // Persistent CTAs (at most one per SM) walk output tiles of 128 weight rows x BN tokens (x a K
-// split), m-block-major so CTAs running at the same time share weight tiles through L2. Warp 0
-// issues TMA into a 4-stage ring, warp 1 owns TMEM and issues tcgen05.mma into one of two
-// 256-column accumulators, warps 2-5 drain the other accumulator (thread = output feature)
-// while the next tile accumulates. SwiGLU weight rows alternate w1 / w3 of one feature, so h1
-// and h3 of a feature sit in neighbouring TMEM lanes (= neighbouring threads) and the epilogue
-// pairs them with one register exchange. Launched with programmatic dependent launch:
-// weight tiles of the first stages are requested before the kernel waits for the activations
-// its predecessor writes.
+// split), m-block-major so CTAs running at the same time share weight tiles through L2. Warps 0
+// and 7 issue the weight tiles and warp 6 the token tiles into a ring of 3-8 stages (one TMA box
+// of one or two K blocks per operand per stage), warp 1 owns TMEM and issues tcgen05.mma into one
+// of two 256-column accumulators, warps 2-5 drain the other accumulator (thread = output
+// feature) while the next tile accumulates. A second instance of each kernel runs CTA pairs
+// (cta_group::2, 256 weight rows per pair, each CTA loading half of the token tile). SwiGLU
+// weight rows alternate w1 / w3 of one feature, so h1 and h3 of a feature sit in neighbouring
+// TMEM lanes (= neighbouring threads) and the epilogue pairs them with one register exchange.
+// Launched with programmatic dependent launch: weight tiles of the first stages are requested
+// before the kernel waits for the activations its predecessor writes.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -1144,16 +1146,15 @@ static int max_active_clusters(int cs) {
     return cache[dev][cs];
 }
 
-// Tile / split choice from a cost model of the kernel's time in SM cycles, fitted to per-CTA
-// phase timestamps taken on B200. Small-N GEMMs here are bound by L2 -> SM operand traffic:
-// every CTA streams its weight tile (16 KB per K block of 64) and its token tile (128 B per
-// token per K block), and all CTAs together draw ~5 KB / cycle (measured on the conv / long-K
-// shapes; short linear ones reach ~7); a single SM draws ~100 B /
-// cycle, and its MMA needs 2 * BN cycles per K block. The last tile's epilogue is exposed
-// (~20 B / cycle of output). Split-K trades a reduction for parallelism: within one wave the
-// splits of a tile form a cluster and reduce through distributed shared memory (~2000 cycles
-// + the slice rows); beyond one wave they reduce through the global workspace, whose last-
-// arriving CTA was measured at ~40000 cycles.
+// Tile / split / pair choice from a cost model of the kernel's time in SM cycles, built on
+// single-thread issue costs measured on B200: a TMA instruction costs its issuing thread ~300
+// cycles, a K=16 MMA at M=128 takes max(65, N / 2) cycles, and the MMA issuer loses ~250 cycles
+// at each stage's barrier wait unless enough MMA work is queued. A CTA's time is its K blocks
+// times the per-stage maximum of those, over the waves of CTAs, plus the exposed epilogue of
+// the last tile (~20 B / cycle of output). Split-K trades a reduction for parallelism: within
+// one wave the splits of a tile form a cluster and reduce through distributed shared memory
+// (~2000 cycles + the slice rows); beyond one wave they reduce through the global workspace,
+// whose last-arriving CTA was measured at ~40000 cycles.
 struct TileChoice {
     double cost;
     int BN, splits, pair;

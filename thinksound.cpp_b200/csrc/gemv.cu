@@ -49,6 +49,7 @@ __global__ void __launch_bounds__(256)
 gemv_kernel(const void * __restrict__ W, const void * __restrict__ W2, int M, int K, const float * __restrict__ x,
             long long ldx, int N, const float * __restrict__ bias, int act, int round_bf16, void * y, int y_bf16,
             long long ldy) {
+    pdl_wait();                // launched with PDL: the predecessor's writes are visible after this
     pdl_launch_dependents();   // let the next kernel in the stream start its prologue
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m = blockIdx.x * 8 + warp;
@@ -101,8 +102,8 @@ template <int WT>
 cudaError_t launch_wt(const void * W, const void * W2, int M, int K, const float * x, long long ldx, int N,
                       const float * bias, int act, int round_bf16, void * y, int y_bf16, long long ldy, cudaStream_t st) {
     dim3 grid((M + 7) / 8);
-    if (W2) gemv_kernel<WT, true><<<grid, 256, 0, st>>>(W, W2, M, K, x, ldx, N, bias, act, round_bf16, y, y_bf16, ldy);
-    else gemv_kernel<WT, false><<<grid, 256, 0, st>>>(W, W2, M, K, x, ldx, N, bias, act, round_bf16, y, y_bf16, ldy);
+    if (W2) launch_pdl(gemv_kernel<WT, true>, dim3(grid), dim3(256), 0, st, W, W2, M, K, x, ldx, N, bias, act, round_bf16, y, y_bf16, ldy);
+    else launch_pdl(gemv_kernel<WT, false>, dim3(grid), dim3(256), 0, st, W, W2, M, K, x, ldx, N, bias, act, round_bf16, y, y_bf16, ldy);
     return cudaGetLastError();
 }
 

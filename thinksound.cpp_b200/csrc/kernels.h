@@ -72,6 +72,22 @@ struct GemmLaunch {
 
 // Programmatic dependent launch on (default) unless TSD_NO_PDL is set to a non-zero value.
 bool pdl_enabled();
+// Launch with programmatic dependent launch (PDL) when enabled: the kernel may be scheduled while
+// its predecessor in the stream finishes; it calls pdl_wait() before it touches global memory.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args &&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
+}
 
 // Tensor-map helpers (driver entry point resolved at first use).
 bool make_tmap_2d(CUtensorMap * m, const void * ptr, CUtensorMapDataType dt, int esize,
