@@ -118,6 +118,17 @@ __device__ __forceinline__ void tma_load_4d_pair(void * dst, const CUtensorMap *
         ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
         : "memory");
 }
+// Element-wise f32 add of a shared-memory tile into the tensor-map box (in L2), tracked by the
+// calling thread's bulk groups like a store. Coordinates must not be negative.
+__device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap * map, const void * src, int c0, int c1, int c2, int c3) {
+    asm volatile("cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3) : "memory");
+}
+// Bring a tensor-map box into L2 only (no shared memory, no completion to wait for).
+__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap * map, int c0, int c1, int c2, int c3) {
+    asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3) : "memory");
+}
 __device__ __forceinline__ void tma_load_4d(void * dst, const CUtensorMap * map, uint64_t * bar, int c0, int c1, int c2,
                                             int c3) {
     asm volatile(

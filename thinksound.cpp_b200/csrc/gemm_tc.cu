@@ -192,12 +192,43 @@ __device__ __forceinline__ void tma_chunk(const GemmParams & p, const CUtensorMa
 
 // TMA epilogue, GATE_RESID: request the residual (and per-token gate) tile of 16 tokens into
 // staging buffer g & 1 (residual [16][128] f32, gate behind it). Thread 64 only.
-__device__ __forceinline__ void gate_issue(const CUtensorMap * tmO, const CUtensorMap * tmG, bool gtile, uint64_t * ebar,
-                                           uint8_t * ebuf, int g, int m0, int t, int b) {
-    uint8_t * bb = ebuf + (g & 1) * kEBufBytes;
-    mbar_arrive_expect_tx(&ebar[g & 1], gtile ? 16384u : 8192u);
-    tma_load_4d(bb, tmO, &ebar[g & 1], m0, t, b, 0);
-    if (gtile) tma_load_4d(bb + 8192, tmG, &ebar[g & 1], m0, t, b, 0);
+// Gate + residual epilogue, 16 tokens a step, through staging buffer g & 1 =
+// [increments 16 x 128 f32 | per-token gate 16 x 128 f32]. The residual is never loaded: the
+// increments gate * (acc + bias) go out by a TMA reduce-add into the residual (each element gets
+// exactly one f32 add, so the result equals x + increment computed in registers). Thread 64
+// loads the gate tiles (two steps ahead), thread 96 issues the reduce-adds: a TMA instruction
+// costs its issuing thread ~300 cycles, so the two streams run on threads of different warps.
+__device__ __forceinline__ void gate_issue(const CUtensorMap * tmG, uint64_t * ebar, uint8_t * ebuf, int g, int m0, int t,
+                                           int b) {
+    uint64_t * bar = &ebar[g & 1];
+    mbar_arrive_expect_tx(bar, 8192u);
+    tma_load_4d(ebuf + (g & 1) * kEBufBytes + 8192, tmG, bar, m0, t, b, 0);
+}
+// One step: this thread's feature of 16 tokens (v = accumulator sums, gv = per-item gate when the
+// gate is not per token). t = the step's first token; t2 = the token of the step two ahead, or
+// -1. Returns false if the gate tile did not arrive in time.
+__device__ __forceinline__ bool gate_step(const GemmParams & p, const EpiCtx & e, const CUtensorMap * tmO,
+                                          const CUtensorMap * tmG, bool gtile, uint64_t * ebar, uint8_t * ebuf, int gs,
+                                          int & gl, const float (&v)[16], const float (&gv)[16], int ml, int m0, int t,
+                                          int t2, int b) {
+    float * dbuf = reinterpret_cast<float *>(ebuf + (gs & 1) * kEBufBytes);
+    const float * gr = dbuf + 16 * 128;
+    if (gtile && !__all_sync(0xffffffffu, mbar_wait(&ebar[gs & 1], (gs >> 1) & 1, nullptr, p.err, DEV_TIMEOUT_ACC)))
+        return false;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) dbuf[j * 128 + ml] = (gtile ? gr[j * 128 + ml] : gv[j]) * (v[j] + e.bias);
+    fence_proxy_async_smem();
+    if (threadIdx.x == 96) bulk_wait_read<0>();     // the previous reduce has read the buffer written next step
+    epi_bar();
+    if (threadIdx.x == 96) {
+        tma_reduce_add_4d(tmO, dbuf, m0, t, b, 0);
+        bulk_commit();
+    }
+    if (threadIdx.x == 64 && gtile && t2 >= 0) {
+        gate_issue(tmG, ebar, ebuf, gl, m0, t2, b);
+        ++gl;
+    }
+    return true;
 }
 
 // QKV: RMSNorm over each head's 64 features (Q, K), RoPE on feature pairs (2i, 2i+1), fp16
@@ -452,18 +483,69 @@ __device__ __forceinline__ void finish_slice(const GemmParams & p, const CUtenso
     const int cb = p.out_cblk ? m0 / p.out_cblk : 0;
     const int c0o = m0 - cb * p.out_cblk;
     const int nsteps = (hi - lo) >> 4;
-    const bool gtile = p.gate_div == 1;
-    GateCursor gcur{nullptr, 0};
     if (Epi<EK>::gate) {
-        const long long r0 = e.row_base + lo;
-        const long long grow = r0 / p.gate_div;
+        GateCursor gcur{nullptr, 0};
+        const long long rr = e.row_base + lo;
+        const long long grow = rr / p.gate_div;
         gcur.g = p.gate + grow * p.ldg + e.m;
-        gcur.gpos = (int)(r0 - grow * p.gate_div);
-        if (tma && threadIdx.x == 64) {
-            bulk_wait_read<0>();
-            for (int k = 0; k < 2 && k < nsteps; ++k, ++gl)
-                gate_issue(tmO, tmG, gtile, ebar, ebuf, gl, m0, c.t0 + lo + 16 * k, c.b);
+        gcur.gpos = (int)(rr - grow * p.gate_div);
+        const bool gtile = p.gate_div == 1;
+        if (tma) {
+            // gate tiles by TMA two steps ahead, residual updates by TMA reduce-add (gate_step)
+            if (threadIdx.x == 64 && gtile)
+                for (int k = 0; k < 2 && k < nsteps; ++k, ++gl) gate_issue(tmG, ebar, ebuf, gl, m0, c.t0 + lo + 16 * k, c.b);
+            for (int k = 0; k < nsteps; ++k, ++gs) {
+                const int r0 = lo + 16 * k;
+                float gv[16];
+                if (!gtile) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        gv[j] = 0.f;
+                        if (e.m_ok && r0 + j < e.ncols) gv[j] = __ldg(gcur.g);
+                        if (++gcur.gpos == p.gate_div) { gcur.gpos = 0; gcur.g += p.ldg; }
+                    }
+                }
+                float acc[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+                for (int sp = 0; sp < p.splits; ++sp) {
+                    const float * src = sp == rank ? part + (size_t)r0 * 128
+                                                   : recv + ((size_t)(sp < rank ? sp : sp - 1) * rows_max + (r0 - lo)) * 128;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) acc[j] += src[j * 128 + ml];
+                }
+                if (!gate_step(p, e, tmO, tmG, gtile, ebar, ebuf, gs, gl, acc, gv, ml, m0, c.t0 + r0,
+                               k + 2 < nsteps ? c.t0 + r0 + 32 : -1, c.b))
+                    return;
+            }
+            return;
         }
+        // no tensor maps: residual and gate rows straight from global memory, the next step's
+        // loaded while this one is summed (each thread owns one feature: coalesced accesses)
+        float ga[16], xa[16], gb[16], xb[16];
+        gate_load16(p, e, lo, gcur, ga, xa);
+        for (int k = 0; k < nsteps; ++k) {
+            const int r0 = lo + 16 * k;
+            uint32_t v[16];
+            {
+                float acc[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+                for (int sp = 0; sp < p.splits; ++sp) {
+                    const float * src = sp == rank ? part + (size_t)r0 * 128
+                                                   : recv + ((size_t)(sp < rank ? sp : sp - 1) * rows_max + (r0 - lo)) * 128;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) acc[j] += src[j * 128 + ml];
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(acc[j]);
+            }
+            if (k + 1 < nsteps) gate_load16(p, e, r0 + 16, gcur, gb, xb);
+            gate_store16(p, e, r0, v, ga, xa);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) { ga[j] = gb[j]; xa[j] = xb[j]; }
+        }
+        return;
     }
     for (int k = 0; k < nsteps; ++k) {
         const int r0 = lo + 16 * k;                           // first tile row (token) of this step
@@ -475,42 +557,6 @@ __device__ __forceinline__ void finish_slice(const GemmParams & p, const CUtenso
                                           : recv + ((size_t)(s < rank ? s : s - 1) * rows_max + (r0 - lo)) * 128;
 #pragma unroll
             for (int j = 0; j < 16; ++j) acc[j] += src[j * 128 + ml];
-        }
-        if (Epi<EK>::gate) {
-            float gv[16];
-            if (!gtile || !tma) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    gv[j] = 0.f;
-                    if (e.m_ok && r0 + j < e.ncols) gv[j] = __ldg(gcur.g);
-                    if (++gcur.gpos == p.gate_div) { gcur.gpos = 0; gcur.g += p.ldg; }
-                }
-            }
-            if (tma) {
-                if (!__all_sync(0xffffffffu, mbar_wait(&ebar[gs & 1], (gs >> 1) & 1, nullptr, p.err, DEV_TIMEOUT_ACC))) return;
-                float * xr = reinterpret_cast<float *>(ebuf + (gs & 1) * kEBufBytes);
-                const float * gr = xr + 16 * 128;
-#pragma unroll
-                for (int j = 0; j < 16; ++j) xr[j * 128 + ml] += (gtile ? gr[j * 128 + ml] : gv[j]) * (acc[j] + e.bias);
-                fence_proxy_async_smem();
-                epi_bar();
-                if (threadIdx.x == 64) {
-                    tma_store_4d(tmO, xr, m0, c.t0 + r0, c.b, 0);
-                    bulk_commit();
-                    if (k + 2 < nsteps) {
-                        bulk_wait_read<0>();
-                        gate_issue(tmO, tmG, gtile, ebar, ebuf, gl, m0, c.t0 + r0 + 32, c.b);
-                        ++gl;
-                    }
-                }
-                ++gs;
-            } else if (e.m_ok) {
-                float * x = p.resid + (e.row_base + r0) * p.ldr + e.m;
-#pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    if (r0 + j < e.ncols) x[(long long)j * p.ldr] += gv[j] * (acc[j] + e.bias);
-            }
-            continue;
         }
         // STORE / SWIGLU: out row values of this thread's feature
         float o[16];
@@ -855,6 +901,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             e.row_base = (long long)c.b * p.S + c.t0;
             e.col = p.out_cblk ? (long long)(e.m / p.out_cblk) * p.out_cstride + e.m % p.out_cblk : e.m;
             const bool tma = p.epi_tma && p.splits == 1;
+            const bool tma_gate = p.epi_tma && (p.splits == 1 || p.csplit);     // residual / gate maps exist
             const int m0 = Epi<EK>::swiglu ? c.mb * 64 : c.mb * 128;    // first output feature of the tile
             const int cb = p.out_cblk ? m0 / p.out_cblk : 0;              // its column block (output map dim 3)
             const int c0o = m0 - cb * p.out_cblk;
@@ -863,6 +910,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // gate + residual of the first columns are fetched while the accumulator fills
             GateCursor gcur{nullptr, 0};
             float ga[16], xa[16], gb[16], xb[16];
+            if (Epi<EK>::gate && tma_gate && gtile && threadIdx.x == 64) {
+                // the gate rows this CTA will read, into L2 while the accumulator fills (the
+                // per-token gate planes are not L2-resident)
+                int lo = 0, hi = e.ncols;
+                if (p.csplit) { lo = slice_lo(srank, p.BN, p.splits); hi = min(slice_lo(srank + 1, p.BN, p.splits), e.ncols); }
+                for (int t = lo + 32; t < hi; t += 16) tma_prefetch_l2_4d(&tmG, m0, c.t0 + t, c.b, 0);
+            }
             if (Epi<EK>::gate && p.splits == 1) {
                 if (tma) {
                     if (!gtile) {                                         // gate rows walked by a cursor
@@ -870,10 +924,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         gcur.g = p.gate + grow * p.ldg + e.m;
                         gcur.gpos = (int)(e.row_base - grow * p.gate_div);
                     }
-                    if (threadIdx.x == 64) {
-                        bulk_wait_read<0>();
+                    if (threadIdx.x == 64 && gtile) {
                         for (int s2 = 0; s2 < 2 && s2 < nsteps; ++s2, ++gl)
-                            gate_issue(&tmO, &tmG, gtile, ebar, ebuf, gl, m0, c.t0 + 16 * s2, c.b);
+                            gate_issue(&tmG, ebar, ebuf, gl, m0, c.t0 + 16 * s2, c.b);
                     }
                 } else {
                     const long long grow = e.row_base / p.gate_div;
@@ -893,14 +946,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             if (p.splits == 1) {
                 bool failed = false;
                 if (Epi<EK>::gate && tma) {
-                    // residual (+ gate) tiles of 16 tokens arrive by TMA two steps ahead; the
-                    // updated residual goes back by TMA store from the same buffer
+                    // gate tiles of 16 tokens by TMA two steps ahead, residual updates by TMA
+                    // reduce-add (gate_step)
                     for (int s2 = 0; s2 < nsteps; ++s2, ++gs) {
-                        // no abort check: once issued, the load lands; all four warps agree
-                        if (!__all_sync(0xffffffffu, mbar_wait(&ebar[gs & 1], (gs >> 1) & 1, nullptr, p.err, DEV_TIMEOUT_ACC))) {
-                            failed = true;
-                            break;
-                        }
                         float v[16], gv[16];
                         if (!gtile) {
 #pragma unroll
@@ -911,23 +959,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                             }
                         }
                         tmem_ld16(trow + 16 * s2, v);
-                        float * xr = reinterpret_cast<float *>(ebuf + (gs & 1) * kEBufBytes);
-                        const float * gr = xr + 16 * 128;
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            const float g = gtile ? gr[j * 128 + ml] : gv[j];
-                            xr[j * 128 + ml] += g * (v[j] + e.bias);
-                        }
-                        fence_proxy_async_smem();
-                        epi_bar();
-                        if (threadIdx.x == 64) {
-                            tma_store_4d(&tmO, xr, m0, c.t0 + 16 * s2, c.b, 0);
-                            bulk_commit();
-                            if (s2 + 2 < nsteps) {
-                                bulk_wait_read<0>();
-                                gate_issue(&tmO, &tmG, gtile, ebar, ebuf, gl, m0, c.t0 + 16 * (s2 + 2), c.b);
-                                ++gl;
-                            }
+                        if (!gate_step(p, e, &tmO, &tmG, gtile, ebar, ebuf, gs, gl, v, gv, ml, m0, c.t0 + 16 * s2,
+                                       s2 + 2 < nsteps ? c.t0 + 16 * (s2 + 2) : -1, c.b)) {
+                            failed = true;
+                            break;
                         }
                     }
                 } else if (Epi<EK>::gate) {
@@ -1043,6 +1078,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             }
             bulk_wait<0>();                           // TMA stores complete before exit
         }
+        if (threadIdx.x == 96) bulk_wait<0>();      // gate epilogue: this thread's reduce-adds complete
     }
     tc_fence_before();
     __syncwarp();
