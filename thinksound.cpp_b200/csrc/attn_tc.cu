@@ -161,30 +161,36 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             if (!__all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, nullptr, a.err, DEV_TIMEOUT_ATTN))) { ok = false; break; }
             tc_fence_after();
             float sv[64];
+            {
+                // both 32-column loads in flight together
+                uint32_t u0[32], u1[32];
+                tmem_ld32_async(lane_base + (j & 1) * 128 + half * 64, u0);
+                tmem_ld32_async(lane_base + (j & 1) * 128 + half * 64 + 32, u1);
+                tmem_wait_ld(u0);
+                tmem_wait_ld(u1);
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                float tmp[32];
-                tmem_ld32(lane_base + (j & 1) * 128 + half * 64 + c * 32, tmp);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) sv[c * 32 + i] = tmp[i];
+                for (int i = 0; i < 32; ++i) { sv[i] = __uint_as_float(u0[i]); sv[32 + i] = __uint_as_float(u1[i]); }
             }
             tc_fence_before();
             mbar_arrive(&s_free[j & 1]);
             const int valid = S - j * kKV - half * 64;  // columns >= valid are padding keys
-            float mx = -INFINITY;
+            // four independent partial maxima / sums: the 64-long dependent chains dominated
+            float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
             for (int i = 0; i < 64; ++i) {
                 sv[i] = (i < valid) ? sv[i] * a.scale_log2 : -INFINITY;
-                mx = fmaxf(mx, sv[i]);
+                m4[i & 3] = fmaxf(m4[i & 3], sv[i]);
             }
+            float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
             float * rm = red + ((j & 1) * 2) * 128;     // this chunk's maxima [half][row]
             rm[half * 128 + r] = mx;
             soft_bar();
             mx = fmaxf(fmaxf(mx, rm[(half ^ 1) * 128 + r]), m_run);
             const float alpha = ex2_approx(m_run - mx);   // 0 on the first chunk
-            float rs = 0.f;
+            float r4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int i = 0; i < 64; ++i) { sv[i] = ex2_approx(sv[i] - mx); rs += sv[i]; }
+            for (int i = 0; i < 64; ++i) { sv[i] = ex2_approx(sv[i] - mx); r4[i & 3] += sv[i]; }
+            const float rs = (r4[0] + r4[1]) + (r4[2] + r4[3]);
             l_run = l_run * alpha + rs;
             m_run = mx;
             if (j > 0) {

@@ -1014,12 +1014,25 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     for (int d = 0; d < p.splits; ++d)
                         if (d != rank) mbar_arrive_remote(mapa_shared(smem_u32(&cbar[2]), crk(d)));
                 }
-                for (int j0 = 0; j0 < p.BN; j0 += 32) {
-                    float v[32];
-                    tmem_ld32(trow + j0, v);
+                // TMEM -> partial tile, 16 columns at a time with the next load in flight (BN % 16 == 0)
+                {
+                    uint32_t va[16], vb[16];
+                    tmem_ld16_async(trow, va);
+                    tmem_wait_ld(va);
+                    for (int j0 = 0; j0 < p.BN; j0 += 32) {
+                        const bool nb = j0 + 16 < p.BN;
+                        if (nb) tmem_ld16_async(trow + j0 + 16, vb);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (j0 + j < p.BN) part[(j0 + j) * 128 + ml] = v[j];
+                        for (int j = 0; j < 16; ++j) part[(j0 + j) * 128 + ml] = __uint_as_float(va[j]);
+                        if (!nb) break;
+                        tmem_wait_ld(vb);
+                        const bool na = j0 + 32 < p.BN;
+                        if (na) tmem_ld16_async(trow + j0 + 32, va);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) part[(j0 + 16 + j) * 128 + ml] = __uint_as_float(vb[j]);
+                        if (!na) break;
+                        tmem_wait_ld(va);
+                    }
                 }
                 release_acc(buf);
                 fence_proxy_async_smem();
