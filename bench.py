@@ -27,6 +27,7 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 CFG3 = dict(T=194, clip_S=72, sync_S=216, text_S=77, t5_S=128)
+CFG4 = dict(T=646, clip_S=240, sync_S=720, text_S=77, t5_S=512)
 HP3 = dict(hidden=1536, n_head=24, depth=21, fused_depth=14)
 METRIC = "DiT flow-steps/s at 9 s, CFG=2, BF16 (MM-DiT attn+proj TFLOP/s in roofline)"
 # ncu: dram__bytes_read.sum + dram__bytes_write.sum over the 36 GEMM launches of one forward of the
@@ -89,8 +90,9 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------------- weights
-def make_device_weights(hp, seed, device):
-    """Synthetic weights generated on the GPU in their BF16-file storage types."""
+def make_device_weights(hp, seed, device, wtype="bf16"):
+    """Synthetic weights generated on the GPU in the storage types of a BF16 or Q8_0 GGUF.
+    Q8_0 tensors are random blocks (int8 ~U[-127,127], fp16 scale ~U[1e-4,4e-3]: config 4)."""
     import torch
     import tsd_b200.synth as synth
     g = torch.Generator(device=device)
@@ -98,7 +100,17 @@ def make_device_weights(hp, seed, device):
     out = {}
     for name, ne, kind in synth.tensor_specs(hp):
         shp = tuple(reversed(ne))
-        t = synth.storage_type(name, ne, "bf16")
+        t = synth.storage_type(name, ne, wtype)
+        if t == synth.GGML_Q8_0 and kind not in ("zeros", "gain", "emb"):
+            nblk = 1
+            for v in shp:
+                nblk *= v
+            nblk //= 32
+            d = (1e-4 + (4e-3 - 1e-4) * torch.rand(nblk, 1, generator=g, device=device)).half()
+            q = torch.randint(-127, 128, (nblk, 32), generator=g, device=device, dtype=torch.int8)
+            blk = torch.cat([d.view(torch.uint8), q.view(torch.uint8)], dim=1)
+            out[name] = synth.WTensor(name, ne, t, blk.contiguous())
+            continue
         if kind == "zeros":
             a = torch.zeros(shp, device=device)
         elif kind == "gain":
@@ -107,7 +119,10 @@ def make_device_weights(hp, seed, device):
             a = torch.randn(shp, generator=g, device=device)
         else:
             a = 0.02 * torch.randn(shp, generator=g, device=device)
-        a = a.to(torch.bfloat16) if t == synth.GGML_BF16 else a.float()
+        if t == synth.GGML_Q8_0:   # quantise (zeros / gains / embeddings stored Q8_0 in the file)
+            a = torch.from_numpy(synth.quantize_q8_0(a.float().cpu().numpy())).to(device)
+        else:
+            a = a.to(torch.bfloat16) if t == synth.GGML_BF16 else a.float()
         out[name] = synth.WTensor(name, ne, t, a.contiguous())
     return out
 
@@ -284,8 +299,9 @@ def main():
     ap.add_argument("--pairs", type=int, default=1, help="CFG pairs per GPU (batch = 2 * pairs)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="cfg3", choices=["cfg3", "cfg5"],
-                    help="cfg3 (default): one flow step per CFG pair; cfg5: 64 prompts x 24 Euler steps, CFG 5, "
+    ap.add_argument("--workload", default="cfg3", choices=["cfg3", "cfg4", "cfg5"],
+                    help="cfg3 (default): one flow step per CFG pair; cfg4: the same at 30 s (T=646, clip 240, "
+                         "sync 720, T5 512) with Q8_0 weights; cfg5: 64 prompts x 24 Euler steps, CFG 5, "
                          "sharded over the ranks, latents gathered to rank 0")
     ap.add_argument("--runs", type=int, default=2, help="cfg5: timed sampling runs")
     ap.add_argument("--profile-case", choices=["bf16", "q8_0"],
@@ -321,15 +337,17 @@ def main():
     peaks = load_peaks()
     hp = synth.DitHParams(**HP3)
     B = 2 * args.pairs
-    W = make_device_weights(hp, seed=1234, device=dev)
+    cfg4 = args.workload == "cfg4"
+    SH = CFG4 if cfg4 else CFG3
+    W = make_device_weights(hp, seed=1234, device=dev, wtype="q8_0" if cfg4 else "bf16")
     model = tsd.DitModel.from_weights(hp, W, device=local)
     del W
     torch.cuda.empty_cache()
-    X = make_device_inputs(B, CFG3, seed=4242 + rank, device=dev)
+    X = make_device_inputs(B, SH, seed=4242 + rank, device=dev)
     ptrs = {k: v.data_ptr() for k, v in X.items()}
     stream = torch.cuda.Stream(device=dev)
     sh = stream.cuda_stream
-    args_fwd = (B, CFG3["T"], CFG3["clip_S"], CFG3["sync_S"], CFG3["text_S"], CFG3["t5_S"])
+    args_fwd = (B, SH["T"], SH["clip_S"], SH["sync_S"], SH["text_S"], SH["t5_S"])
 
     # per-op profile (events between ops, no graph): roofline of the dominant kernel class
     prof = None
@@ -400,11 +418,11 @@ def main():
     e2e_value = world * args.pairs * args.steps / (e2e_ms_max / 1000.0)
 
     if rank == 0:
-        fl = synth.step_flops(hp, B, **CFG3)
+        fl = synth.step_flops(hp, B, **SH)
         g_tf = g_fl / (g_ms / 1000.0) / 1e12 if g_ms > 0 else 0.0
         peak = peaks["bf16_sus"]
         cpu = None
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and not cfg4:
             try:
                 c = cpu_sample()
                 cpu = {k: c[k] for k in ("value", "unit", "cores", "kind", "sample")}
@@ -412,14 +430,20 @@ def main():
                 cpu = {"value": None, "unit": UNIT, "cores": None, "kind": "port", "sample": f"failed: {ex}"}
         # DRAM bytes per GEMM launch: the ratio measured by ncu over all GEMM launches of one
         # forward with the same shapes (profiles/gemm_tc_cfg3_b2.md), times an average launch's FLOPs
-        traffic = GEMM_DRAM_BYTES_PER_FLOP * (g_fl / max(1, g_n))
+        traffic = GEMM_DRAM_BYTES_PER_FLOP * (g_fl / max(1, g_n)) if not cfg4 else None
+        workload = ("cfg3 full flow step: 7 joint + 14 fused MM-DiT blocks + pre/final, H=1536, "
+                    "24x64 heads, T=194 clip=72 sync=216 text=77+128 (joint S=471)")
+        if cfg4:
+            workload = ("cfg4 full flow step at 30 s, Q8_0 weights (random blocks; conv weights F32 as in the "
+                        "reference's Q8_0 files): 7 joint + 14 fused, H=1536, 24x64 heads, T=646 clip=240 sync=720 "
+                        "text=77+512 (joint S=1475)")
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": METRIC if not cfg4 else "DiT flow-steps/s at 30 s, CFG=2, Q8_0 weights", "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded N(0,1) inputs, random-init N(0,0.02^2) weights, BF16 GGUF storage types)",
-            "config": {"workload": "cfg3 full flow step: 7 joint + 14 fused MM-DiT blocks + pre/final, H=1536, "
-                                   "24x64 heads, T=194 clip=72 sync=216 text=77+128 (joint S=471)",
+            "data": "synthetic (seeded N(0,1) inputs, random-init weights, " + ("Q8_0" if cfg4 else "BF16") +
+                    " GGUF storage types)",
+            "config": {"workload": workload,
                        "pairs_per_gpu": args.pairs, "batch_per_gpu": B, "parallelism": f"dp{world} (prompt x CFG pairs)",
                        "l2": "weights (5.6 GB bf16) streamed every step exceed the 126 MB L2; no extra flush",
                        "step_tflop": fl["total"] / 1e12, "attn_proj_tflop": fl["attn_proj"] / 1e12},

@@ -209,11 +209,8 @@ def test_gemm_strided_slice_of_joint_buffer():
     assert rel(out, ref) < 1e-5
 
 
-@pytest.mark.parametrize("wtype", [synth.GGML_BF16, synth.GGML_F32, synth.GGML_Q8_0])
-@pytest.mark.parametrize("N", [1, 2, 5])
-def test_gemv(wtype, N):
-    M, K = 300, 512
-    w = (0.02 * np.random.default_rng(1).standard_normal((M, K))).astype(np.float32)
+def gemv_weights(wtype, M, K, seed=1, scale=0.02):
+    w = (scale * np.random.default_rng(seed).standard_normal((M, K))).astype(np.float32)
     if wtype == synth.GGML_BF16:
         raw = synth.f32_to_bf16_bits(w)
     elif wtype == synth.GGML_Q8_0:
@@ -222,7 +219,17 @@ def test_gemv(wtype, N):
         raw = w
     wt = synth.WTensor("w", (K, M), wtype, raw)
     Wd = torch.from_numpy(np.ascontiguousarray(raw).view(np.uint8).copy()).to(DEV)
-    wf = torch.from_numpy(wt.dequant()).to(DEV)
+    return Wd, torch.from_numpy(wt.dequant()).to(DEV)
+
+
+# K % 256 == 0 takes the streaming form (a whole phase of the row in flight; 4096 = several
+# phases), K = 288 the per-chunk form.
+@pytest.mark.parametrize("K", [512, 4096, 288])
+@pytest.mark.parametrize("wtype", [synth.GGML_BF16, synth.GGML_F32, synth.GGML_Q8_0])
+@pytest.mark.parametrize("N", [1, 2, 5])
+def test_gemv(wtype, N, K):
+    M = 300
+    Wd, wf = gemv_weights(wtype, M, K)
     x = torch.randn(N, K, device=DEV)
     bias = torch.randn(M, device=DEV)
     y = torch.empty(N, M, device=DEV)
@@ -233,16 +240,43 @@ def test_gemv(wtype, N):
     assert rel(y, ref) < 1e-5
 
 
-def test_gemv_swiglu_pair():
-    M, K, N = 256, 256, 2
-    w1 = (0.05 * torch.randn(M, K, device=DEV)).to(torch.bfloat16)
-    w3 = (0.05 * torch.randn(M, K, device=DEV)).to(torch.bfloat16)
+def test_gemv_q8_streaming_equals_per_chunk_form():
+    """Q8_0 rows read as 16-byte words through shared memory must sum exactly like the
+    per-chunk form (taken for weights that are not 16-byte aligned): same chunks per lane in
+    the same order."""
+    M, K, N = 777, 1536, 2
+    Wd, _ = gemv_weights(synth.GGML_Q8_0, M, K, seed=5)
+    shifted = torch.zeros(Wd.numel() + 16, dtype=torch.uint8, device=DEV)
+    shifted[2:2 + Wd.numel()] = Wd.flatten()
+    x = torch.randn(N, K, device=DEV)
+    y1, y2 = torch.empty(N, M, device=DEV), torch.empty(N, M, device=DEV)
+    tsd.op_gemv(Wd, synth.GGML_Q8_0, None, M, K, x, K, N, None, 0, 0, y1, 0, M)
+    tsd.op_gemv(shifted[2:], synth.GGML_Q8_0, None, M, K, x, K, N, None, 0, 0, y2, 0, M)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+    # operands the kernels cannot read with their word sizes are rejected, not read
+    with pytest.raises(tsd.TsdError):
+        tsd.op_gemv(shifted[1:], synth.GGML_Q8_0, None, M, K, x, K, N, None, 0, 0, y2, 0, M)
+    wb = torch.zeros(M * K + 8, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(tsd.TsdError):
+        tsd.op_gemv(wb[1:], synth.GGML_BF16, None, M, K, x, K, N, None, 0, 1, y2, 0, M)
+    with pytest.raises(tsd.TsdError):
+        tsd.op_gemv(Wd, synth.GGML_Q8_0, None, M, K, x.flatten()[1:], K, N, None, 0, 0, y2, 0, M)
+
+
+@pytest.mark.parametrize("wtype,K", [(synth.GGML_BF16, 256), (synth.GGML_BF16, 4096), (synth.GGML_Q8_0, 1536),
+                                     (synth.GGML_F32, 2048), (synth.GGML_BF16, 96)])
+def test_gemv_swiglu_pair(wtype, K):
+    M, N = 256, 2
+    w1, f1 = gemv_weights(wtype, M, K, seed=2, scale=0.05)
+    w3, f3 = gemv_weights(wtype, M, K, seed=3, scale=0.05)
     x = torch.randn(N, K, device=DEV)
     y = torch.empty(N, M, device=DEV)
-    tsd.op_gemv(w1, synth.GGML_BF16, w3, M, K, x, K, N, None, 0, 1, y, 0, M)
+    rb = int(wtype == synth.GGML_BF16)
+    tsd.op_gemv(w1, wtype, w3, M, K, x, K, N, None, 0, rb, y, 0, M)
     torch.cuda.synchronize()
-    xr = x.to(torch.bfloat16).float()
-    ref = torch.nn.functional.silu(xr @ w1.float().T) * (xr @ w3.float().T)
+    xr = x.to(torch.bfloat16).float() if rb else x
+    ref = torch.nn.functional.silu(xr @ f1.T) * (xr @ f3.T)
     assert rel(y, ref) < 1e-5
 
 
@@ -279,6 +313,30 @@ def test_attention_row_stride_and_peaked_softmax():
     ref = ref_attention(Q, K, V, B, nh, S)
     assert rel(out[..., :128].float(), ref) < 4e-3
     assert float(out[..., 128:].abs().max()) == 0.0
+
+
+@pytest.mark.parametrize("growth", [0.5, 12.0, 60.0])
+def test_attention_running_max_grows_across_chunks(growth):
+    """Logits whose row maximum rises from KV chunk to chunk: by less than 2^8 per chunk (the
+    kernel keeps its stale running max and P exceeds 1) and by far more (O and the running sums
+    are rescaled in TMEM), over 6 chunks of 128 keys."""
+    B, nh, S = 1, 3, 700
+    Q = rnd(B * nh, S, 64, scale=1.0, dtype=torch.float32)
+    K = rnd(B * nh, S, 64, scale=1.0, dtype=torch.float32)
+    # key t gets an extra component aligned with every query's mean direction, growing with t
+    qdir = Q.mean(dim=1, keepdim=True)
+    ramp = torch.linspace(0.0, 1.0, S, device=DEV).view(1, S, 1)
+    K = K + growth * ramp * qdir / (qdir.norm(dim=-1, keepdim=True) + 1e-6) * 8.0
+    Q, K = Q.half(), K.half()
+    V = rnd(B * nh, S, 64, dtype=torch.float16)
+    out = torch.empty(B, S, nh * 64, device=DEV, dtype=torch.bfloat16)
+    err = torch.zeros(1, device=DEV, dtype=torch.int32)
+    tsd.op_attention(Q, K, V, B, nh, S, out, nh * 64, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = ref_attention(Q, K, V, B, nh, S)
+    assert torch.isfinite(out.float()).all()
+    assert rel(out.float(), ref) < 4e-3
 
 
 @pytest.mark.parametrize("per_token", [1, 0])

@@ -10,12 +10,14 @@
 // 3-stage ring). Warp 1: TMEM owner + MMA issuer: S_j = Q K_j^T into one of two 128-column
 // TMEM buffers, O += P_j V_j into a 64-column TMEM accumulator (V as an MN-major operand).
 // Warps 2-9: online softmax, two warps per TMEM lane quadrant: a query row (TMEM lane) is shared
-// by two threads, each taking 64 of a chunk's 128 key columns. Only the running max is
-// exchanged (once per chunk, through shared memory); each half keeps its own running sum under
-// the common max and the two are added at the end. P_j is written fp16 into a 128-B-swizzled
-// shared tile (one 64-key sub-tile per half), O is rescaled in TMEM (32 of its 64 columns per
-// half) when the max moves, and the final 1/l scale and bf16 token-major store
-// out[b][t][h*64 + d] are split the same way.
+// by two threads, each taking 64 of a chunk's 128 key columns. Only the chunk max is exchanged
+// (once per chunk, through shared memory); each half keeps its own running sum under the common
+// max and the two are added at the end. P_j is written fp16 into one of two 128-B-swizzled
+// shared tiles (one 64-key sub-tile per half), so the softmax of chunk j never waits for the
+// P V MMA of chunk j-1. The running max is updated lazily: while a chunk's max stays within
+// 2^8 of it, the stale max is kept (P <= 256, exact in the final O / l), so O is rescaled in
+// TMEM (32 of its 64 columns per half) only when the max jumps; the final 1/l scale and bf16
+// token-major store out[b][t][h*64 + d] are split the same way.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -28,13 +30,14 @@ constexpr int kTileBytes = 128 * 128;               // 128 rows x 64 fp16
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kTileBytes;
 constexpr int kOffV = kOffK + kStages * kTileBytes;
-constexpr int kOffP = kOffV + kStages * kTileBytes;  // 2 sub-tiles (kv 0-63, 64-127)
-constexpr int kOffRed = kOffP + 2 * kTileBytes;    // [3][2 halves][128 rows] f32: maxima (2 parities), sums
+constexpr int kOffP = kOffV + kStages * kTileBytes;  // 2 buffers x 2 sub-tiles (kv 0-63, 64-127)
+constexpr int kOffRed = kOffP + 4 * kTileBytes;    // [3][2 halves][128 rows] f32: maxima (2 parities), sums
 constexpr int kOffBar = kOffRed + 3 * 2 * 128 * 4;
 constexpr int kSmemBytes = kOffBar + 256 + 1024;
 constexpr int kThreads = 320;                        // warps: 0 TMA, 1 MMA, 2-9 softmax
 constexpr uint32_t kTmemCols = 512;                  // S0 @0, S1 @128, O @256
 constexpr uint32_t kColO = 256;
+constexpr float kLazyMax = 8.0f;                     // log2 of the largest P kept under a stale max
 
 struct AttnArgs {
     int S, nh;
@@ -58,9 +61,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     uint64_t * kv_empty = bars + 4;         // [3]
     uint64_t * s_full = bars + 7;           // [2]
     uint64_t * s_free = bars + 9;           // [2]
-    uint64_t * p_full = bars + 11;
-    uint64_t * pv_done = bars + 12;
-    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(bars + 13);
+    uint64_t * p_full = bars + 11;          // [2] per P buffer
+    uint64_t * pv_done = bars + 13;         // [2] per P buffer
+    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(bars + 15);
     volatile int * s_abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -73,8 +76,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         mbar_init(q_full, 1);
         for (int s = 0; s < kStages; ++s) { mbar_init(&kv_full[s], 1); mbar_init(&kv_empty[s], 1); }
         for (int s = 0; s < 2; ++s) { mbar_init(&s_full[s], 1); mbar_init(&s_free[s], 256); }
-        mbar_init(p_full, 256);
-        mbar_init(pv_done, 1);
+        for (int s = 0; s < 2; ++s) { mbar_init(&p_full[s], 256); mbar_init(&pv_done[s], 1); }
         *s_abort = 0;
         fence_mbar_init();
     }
@@ -129,11 +131,11 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             if (ok) ok = issue_s(0);
             for (int j = 0; ok && j < nchunks; ++j) {
                 if (j + 1 < nchunks && !issue_s(j + 1)) { ok = false; break; }
-                if (!mbar_wait(p_full, j & 1, s_abort, a.err, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+                if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, s_abort, a.err, DEV_TIMEOUT_ATTN)) { ok = false; break; }
                 tc_fence_after();
                 const int s = j % kStages;
                 const uint32_t vb = smem_u32(smem + kOffV + s * kTileBytes);
-                const uint32_t pb = smem_u32(smem + kOffP);
+                const uint32_t pb = smem_u32(smem + kOffP + (j & 1) * 2 * kTileBytes);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint64_t pd = make_sdesc_sw128(pb + (kk >> 2) * kTileBytes) + 2 * (kk & 3);
@@ -141,9 +143,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                     umma_f16_ss(tmem + kColO, pd, vd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
                 }
                 umma_commit(&kv_empty[s]);
-                umma_commit(pv_done);
+                umma_commit(&pv_done[j & 1]);
             }
-            if (!ok) umma_commit(pv_done);   // lets no waiter depend on MMAs that were never issued
+            if (!ok) { umma_commit(&pv_done[0]); umma_commit(&pv_done[1]); }   // no waiter depends on unissued MMAs
         }
     } else {
         // ---------------- softmax + epilogue (warps 2..9) ----------------
@@ -151,51 +153,60 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         const int half = (warp - 2) >> 2;             // key columns half * 64 .. + 63 of each chunk
         const int r = q * 32 + lane;                   // query row within the tile (TMEM lane)
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-        uint8_t * prow = smem + kOffP + half * kTileBytes + r * 128;
         float * red = reinterpret_cast<float *>(smem + kOffRed);
         float m_run = -INFINITY, l_run = 0.f;
+        // A failed (timed-out) wait leaves `ok` false for the whole warp; the warp still takes every
+        // named barrier below (one per chunk and one at the end), so the other seven never block.
+        // The waits carry no shared abort flag: each warp gives up only on its own deadline.
         bool ok = true;
         for (int j = 0; j < nchunks; ++j) {
-            // no shared abort flag in these waits: every warp gives up only on its own deadline,
-            // so all eight take the same branch around the named barrier below
-            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, nullptr, a.err, DEV_TIMEOUT_ATTN))) { ok = false; break; }
-            tc_fence_after();
             float sv[64];
-            {
-                // both 32-column loads in flight together
-                uint32_t u0[32], u1[32];
-                tmem_ld32_async(lane_base + (j & 1) * 128 + half * 64, u0);
-                tmem_ld32_async(lane_base + (j & 1) * 128 + half * 64 + 32, u1);
-                tmem_wait_ld(u0);
-                tmem_wait_ld(u1);
+            float mx = -INFINITY;
+            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, nullptr, a.err, DEV_TIMEOUT_ATTN));
+            if (ok) {
+                tc_fence_after();
+                {
+                    // both 32-column loads in flight together
+                    uint32_t u0[32], u1[32];
+                    tmem_ld32_async(lane_base + (j & 1) * 128 + half * 64, u0);
+                    tmem_ld32_async(lane_base + (j & 1) * 128 + half * 64 + 32, u1);
+                    tmem_wait_ld(u0);
+                    tmem_wait_ld(u1);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) { sv[i] = __uint_as_float(u0[i]); sv[32 + i] = __uint_as_float(u1[i]); }
-            }
-            tc_fence_before();
-            mbar_arrive(&s_free[j & 1]);
-            const int valid = S - j * kKV - half * 64;  // columns >= valid are padding keys
-            // four independent partial maxima / sums: the 64-long dependent chains dominated
-            float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                    for (int i = 0; i < 32; ++i) { sv[i] = __uint_as_float(u0[i]); sv[32 + i] = __uint_as_float(u1[i]); }
+                }
+                tc_fence_before();
+                mbar_arrive(&s_free[j & 1]);
+                const int valid = S - j * kKV - half * 64;  // columns >= valid are padding keys
+                // four independent partial maxima: the 64-long dependent chain dominated
+                float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
-                sv[i] = (i < valid) ? sv[i] * a.scale_log2 : -INFINITY;
-                m4[i & 3] = fmaxf(m4[i & 3], sv[i]);
+                for (int i = 0; i < 64; ++i) {
+                    sv[i] = (i < valid) ? sv[i] * a.scale_log2 : -INFINITY;
+                    m4[i & 3] = fmaxf(m4[i & 3], sv[i]);
+                }
+                mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
             }
-            float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
             float * rm = red + ((j & 1) * 2) * 128;     // this chunk's maxima [half][row]
             rm[half * 128 + r] = mx;
             soft_bar();
-            mx = fmaxf(fmaxf(mx, rm[(half ^ 1) * 128 + r]), m_run);
-            const float alpha = ex2_approx(m_run - mx);   // 0 on the first chunk
+            if (!ok) continue;
+            const float mc = fmaxf(mx, rm[(half ^ 1) * 128 + r]);   // chunk max of the row (both halves)
+            // both halves of a row hold the same m_run and mc, so they take the same branch
+            const bool grow = mc > m_run + kLazyMax;
+            const float m_new = grow ? mc : m_run;
+            const float alpha = grow ? ex2_approx(m_run - m_new) : 1.0f;   // 0 on the first chunk
             float r4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int i = 0; i < 64; ++i) { sv[i] = ex2_approx(sv[i] - mx); r4[i & 3] += sv[i]; }
+            for (int i = 0; i < 64; ++i) { sv[i] = ex2_approx(sv[i] - m_new); r4[i & 3] += sv[i]; }
             const float rs = (r4[0] + r4[1]) + (r4[2] + r4[3]);
             l_run = l_run * alpha + rs;
-            m_run = mx;
-            if (j > 0) {
-                // PV_{j-1} done: O is stable (rescale this half's 32 columns) and P is free.
-                if (!__all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, nullptr, a.err, DEV_TIMEOUT_ATTN))) { ok = false; break; }
+            m_run = m_new;
+            if (j > 0 && __any_sync(0xffffffffu, grow)) {
+                // O must hold PV_{j-1} before it is rescaled (rows that keep their max scale by 1)
+                ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, nullptr, a.err,
+                                                       DEV_TIMEOUT_ATTN));
+                if (!ok) continue;
                 tc_fence_after();
                 float o[32];
                 tmem_ld32(lane_base + kColO + half * 32, o);
@@ -203,7 +214,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 for (int i = 0; i < 32; ++i) o[i] *= alpha;
                 tmem_st32(lane_base + kColO + half * 32, o);
             }
+            if (j >= 2) {   // P buffer j & 1 was last read by PV_{j-2}
+                ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[j & 1], ((j - 2) >> 1) & 1, nullptr, a.err,
+                                                       DEV_TIMEOUT_ATTN));
+                if (!ok) continue;
+            }
             // P (fp16) into this half's 128-B swizzled K-major sub-tile: row r, 16-B chunk ch -> ch ^ (r & 7)
+            uint8_t * prow = smem + kOffP + ((j & 1) * 2 + half) * kTileBytes + r * 128;
 #pragma unroll
             for (int ch = 0; ch < 8; ++ch) {
                 uint4 u;
@@ -214,13 +231,16 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             }
             fence_proxy_async_smem();
             tc_fence_before();
-            mbar_arrive(p_full);
+            mbar_arrive(&p_full[j & 1]);
         }
-        if (ok && __all_sync(0xffffffffu, mbar_wait(pv_done, (nchunks - 1) & 1, nullptr, a.err, DEV_TIMEOUT_ATTN))) {
-            // both halves' sums under the common max
-            float * rl = red + 4 * 128;
-            rl[half * 128 + r] = l_run;
-            soft_bar();
+        const int jl = nchunks - 1;
+        const bool fin = ok && __all_sync(0xffffffffu, mbar_wait(&pv_done[jl & 1], (jl >> 1) & 1, nullptr, a.err,
+                                                                  DEV_TIMEOUT_ATTN));
+        // both halves' sums under the common max
+        float * rl = red + 4 * 128;
+        rl[half * 128 + r] = l_run;
+        soft_bar();
+        if (fin) {
             const float inv = 1.0f / (l_run + rl[(half ^ 1) * 128 + r]);
             tc_fence_after();
             const int t = q0 + r;
