@@ -304,6 +304,10 @@ def main():
                          "sync 720, T5 512) with Q8_0 weights; cfg5: 64 prompts x 24 Euler steps, CFG 5, "
                          "sharded over the ranks, latents gathered to rank 0")
     ap.add_argument("--runs", type=int, default=2, help="cfg5: timed sampling runs")
+    ap.add_argument("--head-parallel", action="store_true",
+                    help="with torchrun N>1: the ranks split the 24 heads of one CFG pair's forward (QKV rows and "
+                         "attention), exchanging attention rows over NVLink peer memory; all ranks compute the "
+                         "same pair (strong scaling)")
     ap.add_argument("--profile-case", choices=["bf16", "q8_0"],
                     help="instead of the bench: one op-by-op forward of a 2 joint + 1 fused block model at "
                          "the config-3 widths (the small case the ncu captures are taken on)")
@@ -343,7 +347,12 @@ def main():
     model = tsd.DitModel.from_weights(hp, W, device=local)
     del W
     torch.cuda.empty_cache()
-    X = make_device_inputs(B, SH, seed=4242 + rank, device=dev)
+    hpar = args.head_parallel and world > 1
+    if hpar:
+        from tsd_b200 import dp
+        dp.head_parallel(model, rank, world, arena_bytes=1 << 30)
+    # head-parallel ranks work on the same pair; data-parallel ranks each on their own
+    X = make_device_inputs(B, SH, seed=4242 + (0 if hpar else rank), device=dev)
     ptrs = {k: v.data_ptr() for k, v in X.items()}
     stream = torch.cuda.Stream(device=dev)
     sh = stream.cuda_stream
@@ -414,8 +423,9 @@ def main():
     if pg:
         pg.all_reduce(times, op=pg.ReduceOp.MAX)
     ms_max, e2e_ms_max = float(times[0]), float(times[1])
-    value = world * args.pairs * args.steps / (ms_max / 1000.0)
-    e2e_value = world * args.pairs * args.steps / (e2e_ms_max / 1000.0)
+    jobs = 1 if hpar else world          # distinct CFG-pair groups per step across the job
+    value = jobs * args.pairs * args.steps / (ms_max / 1000.0)
+    e2e_value = jobs * args.pairs * args.steps / (e2e_ms_max / 1000.0)
 
     if rank == 0:
         fl = synth.step_flops(hp, B, **SH)
@@ -439,12 +449,15 @@ def main():
                         "text=77+512 (joint S=1475)")
         line = {
             "metric": METRIC if not cfg4 else "DiT flow-steps/s at 30 s, CFG=2, Q8_0 weights", "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "strong" if hpar else "weak",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) inputs, random-init weights, " + ("Q8_0" if cfg4 else "BF16") +
                     " GGUF storage types)",
             "config": {"workload": workload,
-                       "pairs_per_gpu": args.pairs, "batch_per_gpu": B, "parallelism": f"dp{world} (prompt x CFG pairs)",
+                       "pairs_per_gpu": args.pairs, "batch_per_gpu": B,
+                       "parallelism": (f"head-parallel x{world} (24 heads split, attention rows exchanged over NVLink)"
+                                       if hpar else f"dp{world} (prompt x CFG pairs)"),
                        "l2": "weights (5.6 GB bf16) streamed every step exceed the 126 MB L2; no extra flush",
                        "step_tflop": fl["total"] / 1e12, "attn_proj_tflop": fl["attn_proj"] / 1e12},
             "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05 projections, all launches of a step)",
@@ -468,6 +481,8 @@ def main():
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+    if pg:
+        pg.barrier()     # head-parallel: no rank frees its exchange buffer while a peer maps it
     model.close()
     if pg:
         pg.barrier()

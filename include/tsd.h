@@ -110,6 +110,25 @@ TSD_API int tsd_sample_batched(tsd_model * m, int P, const float * noise, int64_
                        const float * t5, int64_t t5_S, const float * global_text, int steps, float cfg,
                        float * out, float * flow0);
 
+/* Head-parallel mode (optional; for long inputs such as 30 s). No counterpart API exists in the
+ * reference, which runs one GGML backend per process; this splits the attention heads of
+ * mmdit.cpp:85-94,219 across the GPUs of one node, one process per GPU, each with its own model
+ * loaded from the same weights. Rank r computes heads [h0, h0 + n_head / world) of every joint
+ * and fused block (QKV rows and attention) and writes their attention rows into every rank's
+ * exchange buffer over NVLink; all other work is replicated, so every rank returns the full
+ * result. Call tsd_hp_init on every rank, exchange the TSD_IPC_HANDLE_BYTES handles (rank
+ * order), then call tsd_hp_connect on every rank before the first forward. All ranks must then
+ * issue the same forwards (same shapes, same order); a forward completes only after its peers'
+ * rows of every layer arrived (bounded wait: a missing peer ends in TSD_ERR_DEVICE, after which
+ * the group must be set up again with new models). `arena_bytes` bounds the exchange buffers
+ * of all plans built in this mode (B * S * hidden * 2 bytes per layer and input shape; never
+ * reused). Needs bf16 QKV weights (not TSD_Q8_IN_KERNEL). Free the models only after every
+ * rank's last forward has returned. */
+#define TSD_IPC_HANDLE_BYTES 64
+TSD_API int tsd_hp_layout(int hidden, int n_head, int world, int rank, int32_t out[3]); /* h0, heads, rows per Q/K/V section */
+TSD_API int tsd_hp_init(tsd_model * m, int rank, int world, size_t arena_bytes, void * handle_out);
+TSD_API int tsd_hp_connect(tsd_model * m, const void * handles);
+
 /* Library / device information. */
 TSD_API const char * tsd_version(void);
 TSD_API int tsd_device_count(void);

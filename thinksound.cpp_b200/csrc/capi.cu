@@ -143,6 +143,24 @@ void tsd_model_free(tsd_model * h) {
     delete h;
 }
 
+int tsd_hp_layout(int hidden, int n_head, int world, int rank, int32_t out[3]) {
+    int h0, nl, sec;
+    if (!out || !hp_layout(hidden, n_head, world, rank, h0, nl, sec)) return TSD_ERR_ARG;
+    out[0] = h0; out[1] = nl; out[2] = sec;
+    return TSD_OK;
+}
+
+int tsd_hp_init(tsd_model * h, int rank, int world, size_t arena_bytes, void * handle_out) {
+    if (!h || !h->m) return TSD_ERR_ARG;
+    TSD_CUDA_TRY(cudaStreamSynchronize(h->stream));
+    return hp_init(*h->m, rank, world, arena_bytes, handle_out);
+}
+
+int tsd_hp_connect(tsd_model * h, const void * handles) {
+    if (!h || !h->m) return TSD_ERR_ARG;
+    return hp_connect(*h->m, handles);
+}
+
 int tsd_model_get_hparams(const tsd_model * h, tsd_hparams * out) {
     if (!h || !out) return TSD_ERR_ARG;
     *out = h->m->hp;

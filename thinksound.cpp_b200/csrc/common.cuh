@@ -22,6 +22,7 @@ enum DevErr : int {
     DEV_TIMEOUT_ATTN = 4,     // attention pipeline wait expired
     DEV_BAD_ARGS = 5,
     DEV_TIMEOUT_CLUSTER = 6,  // a split-K peer CTA of the cluster did not arrive in time
+    DEV_TIMEOUT_HP = 7,       // head-parallel: a peer rank's attention rows did not arrive in time
 };
 
 // 2 s: no healthy wait in these kernels comes anywhere near it.

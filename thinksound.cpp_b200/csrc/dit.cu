@@ -153,7 +153,7 @@ struct Builder {
         if (mode == EPI_QKV) {
             p.q_out = qspec.q; p.k_out = qspec.k; p.v_out = qspec.v;
             p.qg = qspec.qg; p.kg = qspec.kg; p.rope = qspec.rope;
-            p.hidden = m.H; p.nh = m.nh; p.Sj = qspec.Sj; p.s_off = qspec.s_off; p.s_item = qspec.s_item;
+            p.hidden = qspec.hidden; p.nh = qspec.nh; p.Sj = qspec.Sj; p.s_off = qspec.s_off; p.s_item = qspec.s_item;
         }
         gemm_finalize(L);
         if (autotune && hit == tuned.end()) {
@@ -203,14 +203,59 @@ struct Builder {
         const float * qg = nullptr, * kg = nullptr;
         const float2 * rope = nullptr;
         int Sj = 0, s_off = 0, s_item = 0;
+        int hidden = 0, nh = 0;      // rows per Q / K / V section, heads stored
     } qspec;
-    void gemm_qkv(const StreamW & w, const void * X, int nbatch, int S, const float2 * rope, __half * Q, __half * K,
-                  __half * V, int Sj, int s_off) {
+    // Head-parallel plans use this rank's slice of the QKV rows (sections of hpar.sec rows, nl
+    // heads each) in place of the full weight.
+    void gemm_qkv(const StreamW & w, const GW * slice, const void * X, int nbatch, int S, const float2 * rope,
+                  __half * Q, __half * K, __half * V, int Sj, int s_off) {
         qspec.q = Q; qspec.k = K; qspec.v = V; qspec.qg = w.qg; qspec.kg = w.kg; qspec.rope = rope;
         qspec.Sj = Sj; qspec.s_off = s_off; qspec.s_item = S;
-        gemm(w.qkv, X, nbatch, S, m.H, (long long)S * m.H, EPI_QKV, ACT_NONE, nullptr, 0, 0, nullptr, 0, nullptr, 0, 1, 0,
-             /*max_splits=*/1);
+        qspec.hidden = slice ? m.hpar.sec : m.H;
+        qspec.nh = slice ? m.hpar.nl : m.nh;
+        gemm(slice ? *slice : w.qkv, X, nbatch, S, m.H, (long long)S * m.H, EPI_QKV, ACT_NONE, nullptr, 0, 0, nullptr, 0,
+             nullptr, 0, 1, 0, /*max_splits=*/1);
     }
+    // Attention of one layer; returns the buffer the out-projection reads (the full [B][S][H]
+    // attention output). Head-parallel: this rank's heads, their rows stored into the layer's
+    // exchange buffer here and on every peer, then a wait for the peers' rows.
+    __nv_bfloat16 * attention(const __half * Q, const __half * K, const __half * V, int B, int S, __nv_bfloat16 * ao,
+                              int * err) {
+        const int H = m.H;
+        HeadParallel & hp = m.hpar;
+        AttnLaunch A;
+        if (!hp.connected) {
+            if (!attn_plan(A, Q, K, V, B, m.nh, S, ao, H, err)) { rc = TSD_ERR_ARG; return ao; }
+            op([A](cudaStream_t st) { return attn_launch(A, st); }, OP_ATTN, 4.0 * B * m.nh * 64.0 * S * S,
+               6.0 * B * m.nh * 64.0 * S + 2.0 * B * S * H);
+            return ao;
+        }
+        const long long off = hp_carve(m, (size_t)B * S * H * 2);
+        const int slot = hp_next_slot(m);
+        if (off < 0 || slot < 0) {
+            fprintf(stderr, "tsd: head-parallel exchange arena exhausted (give tsd_hp_init a larger arena)\n");
+            rc = TSD_ERR_ARG;
+            return ao;
+        }
+        auto * X = reinterpret_cast<__nv_bfloat16 *>(hp.arena + off);
+        const long long col = (long long)hp.h0 * 64;    // this rank's columns of the [B][S][H] rows
+        if (!attn_plan(A, Q, K, V, B, hp.nl, S, X + col, H, err)) { rc = TSD_ERR_ARG; return ao; }
+        for (int r = 0; r < hp.world; ++r) {
+            if (r == hp.rank) continue;
+            A.peer_out[A.n_peers] = reinterpret_cast<__nv_bfloat16 *>(hp.peer[r] + off) + col;
+            A.peer_flag[A.n_peers] = hp_counter(m, r, slot, hp.rank);
+            ++A.n_peers;
+        }
+        op([A](cudaStream_t st) { return attn_launch(A, st); }, OP_ATTN, 4.0 * B * hp.nl * 64.0 * S * S,
+           6.0 * B * hp.nl * 64.0 * S + 2.0 * B * S * H * hp.world);
+        const unsigned ctas = (unsigned)(((S + 127) / 128) * B * hp.nl);
+        const unsigned * counters = hp_counter(m, hp.rank, slot, 0);
+        const unsigned * epoch = epoch_ptr;
+        const int rank = hp.rank, world = hp.world;
+        op([=](cudaStream_t st) { return hp_wait_launch(counters, epoch, rank, world, ctas, err, st); });
+        return X;
+    }
+    unsigned * epoch_ptr = nullptr;
     // Few-token GEMV over B items (chunks of 8 tokens).
     void gemv(const VW & w, const float * x, long long ldx, int N, int act, float * y, long long ldy, int y_bf16 = 0) {
         if (rc) return;
@@ -280,9 +325,11 @@ struct Builder {
         float * mod_lat = alloc<float>((size_t)B * T * R);
         float * mod_c = alloc<float>((size_t)B * 6 * H);
         float * mod_t = alloc<float>((size_t)B * 6 * H);
-        auto * Qb = alloc<__half>((size_t)B * nh * Sj * 64);
-        auto * Kb = alloc<__half>((size_t)B * nh * Sj * 64);
-        auto * Vb = alloc<__half>((size_t)B * nh * Sj * 64);
+        const bool hpm = m.hpar.connected;
+        const int nhl = hpm ? m.hpar.nl : nh;             // heads this rank computes
+        auto * Qb = alloc<__half>((size_t)B * nhl * Sj * 64);
+        auto * Kb = alloc<__half>((size_t)B * nhl * Sj * 64);
+        auto * Vb = alloc<__half>((size_t)B * nhl * Sj * 64);
         auto * ao = alloc<__nv_bfloat16>((size_t)B * Sj * H);
         auto * rope_lat = alloc<float2>((size_t)T * 32);     // RoPE (cos, sin): latent positions, scale 1
         auto * rope_clip = alloc<float2>((size_t)cS * 32);   // clip positions, scale T / clip_S
@@ -318,6 +365,13 @@ struct Builder {
         }
 
         op([err](cudaStream_t st) { return cudaMemsetAsync(err, 0, sizeof(int), st); }, OP_COPY, 0, 0, 0);
+        if (hpm) {   // this plan's forward counter, read by its head-parallel waits
+            const int pi = hp_next_plan(m);
+            if (pi < 0) { rc = TSD_ERR_ARG; return; }
+            unsigned * const ep = hp_epoch(m, pi);
+            epoch_ptr = ep;
+            op([ep](cudaStream_t st) { return hp_epoch_launch(ep, st); });
+        }
 
         // The input projections are independent chains: audio, t-embed and sync on lane 0, clip
         // on lane 1, text on lane 2 (each lane with its own a1 / hbuf), joined before the
@@ -407,11 +461,6 @@ struct Builder {
         const int Ss[3] = {T, cS, St};
         const int soff[3] = {0, T, T + cS};
         float * modc[3] = {nullptr, mod_c, mod_t};
-        AttnLaunch AJ, AF;
-        if (!attn_plan(AJ, Qb, Kb, Vb, B, nh, Sj, ao, H, err) || !attn_plan(AF, Qb, Kb, Vb, B, nh, T, ao, H, err)) {
-            rc = TSD_ERR_ARG;
-            return;
-        }
         // The three streams of a joint block are independent except at the attention: stream s
         // runs on lane s (its own CUDA stream in the captured graph), joined before the
         // attention and forked after it.
@@ -437,19 +486,20 @@ struct Builder {
                 const long long ld = lds[s], cs = css[s];
                 op([=](cudaStream_t st) { return ln_modulate(xs[s], B * S, H, mod, mod + cs, ld, s == 0, S, xn, st); });
                 if (i == 0 && s == 2) snap("text_xn", xn, (long long)B * S * H, 1);
-                gemm_qkv(w, xn, B, S, s == 0 ? rope_lat : s == 1 ? rope_clip : nullptr, Qb, Kb, Vb, Sj, soff[s]);
+                gemm_qkv(w, hpm ? &m.hpar.joint_qkv[i][s] : nullptr, xn, B, S,
+                         s == 0 ? rope_lat : s == 1 ? rope_clip : nullptr, Qb, Kb, Vb, Sj, soff[s]);
             }
-            if (i == 0) {
-                snap("a0_q", Qb, (long long)B * Sj * H, 2, B, nh, Sj);
-                snap("a0_k", Kb, (long long)B * Sj * H, 2, B, nh, Sj);
-                snap("a0_v", Vb, (long long)B * Sj * H, 2, B, nh, Sj);
+            if (i == 0) {   // (head-parallel: this rank's heads)
+                snap("a0_q", Qb, (long long)B * Sj * nhl * 64, 2, B, nhl, Sj);
+                snap("a0_k", Kb, (long long)B * Sj * nhl * 64, 2, B, nhl, Sj);
+                snap("a0_v", Vb, (long long)B * Sj * nhl * 64, 2, B, nhl, Sj);
             }
             lane = 0;
             mark(2);
             tag = "j" + std::to_string(i);
-            op([AJ](cudaStream_t st) { return attn_launch(AJ, st); }, OP_ATTN, 4.0 * B * nh * 64.0 * Sj * Sj,
-               6.0 * B * nh * 64.0 * Sj + 2.0 * B * Sj * H);
-            if (i == 0) snap("a0_out", ao, (long long)B * Sj * H, 1);
+            __nv_bfloat16 * const aoj = attention(Qb, Kb, Vb, B, Sj, ao, err);
+            if (rc) return;
+            if (i == 0) snap("a0_out", aoj, (long long)B * Sj * H, 1);
             mark(1);
             for (int s = 0; s < 3; ++s) {
                 const StreamW & w = blk[s];
@@ -462,7 +512,7 @@ struct Builder {
                 const float * mod = mods[s];
                 const long long ld = lds[s], cs = css[s];
                 const int gdiv = (s == 0) ? 1 : S;
-                gemm(w.l1, ao + (long long)soff[s] * H, B, S, H, (long long)Sj * H, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0,
+                gemm(w.l1, aoj + (long long)soff[s] * H, B, S, H, (long long)Sj * H, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0,
                      xs[s], H, mod + 2 * cs, ld, gdiv);
                 op([=](cudaStream_t st) { return ln_modulate(xs[s], B * S, H, mod + 3 * cs, mod + 4 * cs, ld, s == 0, S, xn, st); });
                 gemm(w.w13, xn, B, S, H, (long long)S * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 1);
@@ -482,14 +532,15 @@ struct Builder {
         // ---- fused blocks (mmdit.cpp:274-282) ----
         int fi = 0;
         for (const StreamW & w : m.fused) {
+            const int fidx = fi;
             tag = "f" + std::to_string(fi++);
             const float * mod = mod_lat + (w.ada_off / H) * BTH;
             const long long ld = H, cs = BTH;
             op([=](cudaStream_t st) { return ln_modulate(x_lat, B * T, H, mod, mod + cs, ld, 1, T, xn, st); });
-            gemm_qkv(w, xn, B, T, rope_lat, Qb, Kb, Vb, T, 0);
-            op([AF](cudaStream_t st) { return attn_launch(AF, st); }, OP_ATTN, 4.0 * B * nh * 64.0 * T * T,
-               6.0 * B * nh * 64.0 * T + 2.0 * B * T * H);
-            gemm(w.l1, ao, B, T, H, (long long)T * H, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, x_lat, H, mod + 2 * cs, ld, 1);
+            gemm_qkv(w, hpm ? &m.hpar.fused_qkv[fidx] : nullptr, xn, B, T, rope_lat, Qb, Kb, Vb, T, 0);
+            __nv_bfloat16 * const aof = attention(Qb, Kb, Vb, B, T, ao, err);
+            if (rc) return;
+            gemm(w.l1, aof, B, T, H, (long long)T * H, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, x_lat, H, mod + 2 * cs, ld, 1);
             op([=](cudaStream_t st) { return ln_modulate(x_lat, B * T, H, mod + 3 * cs, mod + 4 * cs, ld, 1, T, xn, st); });
             gemm(w.w13, xn, B, T, H, (long long)T * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 1);
             gemm(w.w2, hbuf, B, T, F, (long long)T * F, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, x_lat, H, mod + 5 * cs, ld, 1);

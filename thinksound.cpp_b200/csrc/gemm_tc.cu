@@ -328,7 +328,8 @@ __device__ __forceinline__ void emit_qkv(const GemmParams & p, const EpiCtx & e,
     int b = (int)(row / p.s_item), t = (int)(row - (long long)b * p.s_item);
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-        if (j0 + j < e.ncols) dst[(((long long)b * p.nh + h) * p.Sj + p.s_off + t) * 64 + d] = __float2half_rn(v[j]);
+        // h >= nh: a padding head of a head-parallel slice (zero weight rows), not stored
+        if (j0 + j < e.ncols && h < p.nh) dst[(((long long)b * p.nh + h) * p.Sj + p.s_off + t) * 64 + d] = __float2half_rn(v[j]);
         if (++t == p.s_item) { t = 0; ++b; }
     }
 }

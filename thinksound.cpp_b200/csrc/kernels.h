@@ -134,6 +134,7 @@ cudaError_t gemv_launch(const void * W, int wtype, const void * W2, int M, int K
 // Attention (tcgen05): O = softmax(Q K^T * scale) V per (batch, head); Q, K, V fp16
 // [B*nh][S][64] (head-major). O written bf16 token-major: out[b][t][h*64 + d], row stride ldo.
 // ---------------------------------------------------------------------------------------------
+constexpr int kMaxHpRanks = 8;
 struct AttnLaunch {
     CUtensorMap tmQ, tmK, tmV;
     int S, nh, B;
@@ -141,6 +142,12 @@ struct AttnLaunch {
     void * out;
     int * err;
     float scale;
+    // Head-parallel exchange (n_peers > 0): every output row is also stored at peer_out[r] (the
+    // same offsets in rank r's exchange buffer, mapped into this process), and each CTA, once its
+    // rows are stored, adds 1 to peer_flag[r] (rank r's arrival counter for this layer and rank).
+    int n_peers = 0;
+    void * peer_out[kMaxHpRanks] = {};
+    unsigned * peer_flag[kMaxHpRanks] = {};
 };
 bool attn_plan(AttnLaunch & L, const void * Q, const void * K, const void * V, int B, int nh, int S,
                void * out, long long ldo, int * err);

@@ -94,6 +94,7 @@ __global__ void to_f32_kernel(const void * src, int type, long long n, float * d
 Model::~Model() {
     plan.reset();
     if (device >= 0) cudaSetDevice(device);
+    hp_release(*this);
     for (auto & kv : raw)
         if (kv.second.d) cudaFree(kv.second.d);
     for (void * p : allocs) cudaFree(p);

@@ -63,6 +63,20 @@ struct StreamW {
 
 struct Plan;
 
+// Head-parallel state (hp.cu): this rank's heads, its exchange arena and the peers' mappings.
+struct HeadParallel {
+    int rank = 0, world = 1;
+    int h0 = 0, nl = 0, sec = 0;          // heads [h0, h0 + nl); rows per sliced Q / K / V section
+    uint8_t * arena = nullptr;
+    size_t arena_bytes = 0, used = 0;
+    uint8_t * peer[kMaxHpRanks] = {};     // every rank's arena as mapped in this process
+    bool connected = false;
+    int next_plan = 0, next_slot = 0;
+    std::vector<std::array<GW, 3>> joint_qkv;   // QKV rows of this rank's heads
+    std::vector<GW> fused_qkv;
+    std::vector<void *> allocs;
+};
+
 struct Model {
     tsd_hparams hp{};
     int device = 0, num_sms = 148;
@@ -81,6 +95,7 @@ struct Model {
     std::vector<StreamW> fused;
     int * d_err = nullptr;
     std::unique_ptr<Plan> plan;
+    HeadParallel hpar;
 
     ~Model();
     void * dalloc(size_t bytes);
@@ -148,6 +163,20 @@ struct Plan {
 };
 
 int plan_build(Model & m, const Shape & sh, std::unique_ptr<Plan> & out);
+
+// Head-parallel mode (hp.cu).
+bool hp_layout(int H, int nh, int world, int rank, int & h0, int & nl, int & sec);
+int hp_init(Model & m, int rank, int world, size_t arena_bytes, void * handle_out);
+int hp_connect(Model & m, const void * handles);
+void hp_release(Model & m);
+int hp_next_plan(Model & m);
+int hp_next_slot(Model & m);
+long long hp_carve(Model & m, size_t bytes);            // arena offset, or -1 when exhausted
+unsigned * hp_counter(Model & m, int on_rank, int slot, int from_rank);
+unsigned * hp_epoch(Model & m, int plan);
+cudaError_t hp_epoch_launch(unsigned * epoch, cudaStream_t st);
+cudaError_t hp_wait_launch(const unsigned * counters, const unsigned * epoch, int rank, int world, unsigned ctas,
+                           int * err, cudaStream_t st);
 // Enqueue the forward (inputs already in the plan's buffers). reuse_cond: the conditioning
 // inputs (clip_in, sync_in, text_in, t5_in, gtext_in) are unchanged since the last full run of
 // this plan, whose conditioning-only results are reused instead of recomputed.

@@ -66,3 +66,31 @@ def sample_sharded(sample_fn: Callable[[Sequence, int, float], np.ndarray], item
         rlo, rhi = shard_range(len(items), r, world)
         parts.append(gathered[r][: rhi - rlo].cpu().numpy())
     return np.concatenate(parts, axis=0)
+
+
+def exchange_handles(handle: bytes, rank: int, world: int, group=None) -> List[bytes]:
+    """Every rank's IPC handle in rank order (one all_gather_object; any backend)."""
+    import torch.distributed as dist
+
+    if world == 1:
+        return [handle]
+    out: List[Optional[bytes]] = [None] * world
+    dist.all_gather_object(out, handle, group=group)
+    if any(not isinstance(h, (bytes, bytearray)) or len(h) != len(handle) for h in out):
+        raise RuntimeError("head-parallel set-up: a rank sent no handle")
+    return [bytes(h) for h in out]
+
+
+def head_parallel(model, rank: int, world: int, arena_bytes: int = 1 << 30, group=None) -> None:
+    """Put `model` (this rank's copy of the DiT) into head-parallel mode: rank r computes heads
+    [r * nh / world, (r + 1) * nh / world) of every block and exchanges its attention rows with
+    the other ranks over peer memory (tsd_hp_init / tsd_hp_connect). Collective: every rank of
+    the group calls it, then all ranks issue the same forwards. Before freeing the models, end
+    with a barrier so that no rank frees its exchange buffer while a peer still maps it."""
+    import torch.distributed as dist
+
+    handle = model.hp_init(rank, world, arena_bytes)
+    handles = exchange_handles(handle, rank, world, group)
+    model.hp_connect(handles)
+    if world > 1:
+        dist.barrier(group=group)   # every rank has mapped every peer before any forward stores to it

@@ -30,6 +30,7 @@ EXPORTS = [
     "tsd_forward_device", "tsd_sync_check", "tsd_sample", "tsd_sample_batched", "tsd_version",
     "tsd_device_count", "tsd_op_gemm", "tsd_op_gemv", "tsd_op_attention", "tsd_op_ln_modulate",
     "tsd_op_qk_norm_rope", "tsd_forward_profile", "tsd_plan_op_label", "tsd_op_gemm_static",
+    "tsd_hp_layout", "tsd_hp_init", "tsd_hp_connect",
 ]
 
 
@@ -81,6 +82,9 @@ def lib() -> ctypes.CDLL:
                                i64, vp, i64, i32, i32, vp, vp],
         "tsd_op_gemv": [vp, i32, vp, i32, i32, vp, i64, i32, vp, i32, i32, vp, i32, i64, vp],
         "tsd_op_attention": [vp, vp, vp, i32, i32, i32, vp, i64, vp, vp],
+        "tsd_hp_layout": [i32, i32, i32, i32, ctypes.POINTER(i32)],
+        "tsd_hp_init": [vp, i32, i32, ctypes.c_size_t, vp],
+        "tsd_hp_connect": [vp, vp],
         "tsd_op_ln_modulate": [vp, i32, i32, vp, vp, i64, i32, i32, vp, vp],
         "tsd_op_qk_norm_rope": [vp, i32, i32, i32, i32, vp, vp, i32, f32, f32, vp, vp, vp, i32, i32, vp],
         "tsd_forward_profile": [vp, i32, vp, i64, vp, vp, i64, vp, i64, vp, i64, vp, i64, vp, vp, vp, i32,
@@ -115,8 +119,30 @@ def _stack(items, attr) -> np.ndarray:
     return np.ascontiguousarray(np.stack([np.asarray(getattr(x, attr), np.float32) for x in items]))
 
 
+IPC_HANDLE_BYTES = 64
+
+
+def hp_layout(hidden: int, n_head: int, world: int, rank: int):
+    """(first head, heads, rows per Q/K/V section) of `rank` in a head-parallel group."""
+    out = (ctypes.c_int32 * 3)()
+    check("tsd_hp_layout", lib().tsd_hp_layout(hidden, n_head, world, rank, out))
+    return int(out[0]), int(out[1]), int(out[2])
+
+
 class DitModel:
     """A loaded DiT on one GPU (the reference's ts_dit)."""
+
+    def hp_init(self, rank: int, world: int, arena_bytes: int) -> bytes:
+        """Head-parallel set-up, step 1: returns this rank's exchange-buffer IPC handle."""
+        buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        check("tsd_hp_init", lib().tsd_hp_init(self.h, rank, world, arena_bytes, buf))
+        return buf.raw
+
+    def hp_connect(self, handles) -> None:
+        """Head-parallel set-up, step 2: every rank's handle, in rank order."""
+        blob = b"".join(handles)
+        assert len(blob) == IPC_HANDLE_BYTES * len(handles)
+        check("tsd_hp_connect", lib().tsd_hp_connect(self.h, ctypes.create_string_buffer(blob, len(blob))))
 
     def __init__(self, handle: int):
         self.h = ctypes.c_void_p(handle)
