@@ -221,6 +221,17 @@ class DitModel:
         check("tsd_forward_batched", rc)
         return (out, store) if dbg else out
 
+    def forward_host(self, B: int, T: int, clip_S: int, sync_S: int, text_S: int, t5_S: int,
+                     ptrs: Dict[str, int]) -> None:
+        """tsd_forward_batched on caller-owned host buffers given as raw addresses (e.g. pinned
+        memory, whose copies the GPU's copy engines run without staging); flow written to
+        ptrs["flow"] ([B][T][latent_dim]) before returning."""
+        fp = ctypes.POINTER(ctypes.c_float)
+        c = lambda k: ctypes.cast(ctypes.c_void_p(ptrs[k]), fp)
+        rc = lib().tsd_forward_batched(self.h, B, c("latent"), T, c("t"), c("clip_f"), clip_S, c("sync_f"), sync_S,
+                                       c("text_f"), text_S, c("t5"), t5_S, c("gtext"), c("flow"), DBG_FN(), None)
+        check("tsd_forward_batched", rc)
+
     def forward_device(self, B: int, T: int, clip_S: int, sync_S: int, text_S: int, t5_S: int, ptrs: Dict[str, int],
                        stream: int = 0) -> None:
         """Enqueue a forward on device-resident inputs (raw device pointers)."""
