@@ -324,6 +324,7 @@ struct Builder {
         auto * sext = alloc<__nv_bfloat16>((size_t)B * T * H);
         float * mod_lat = alloc<float>((size_t)B * T * R);
         float * mod_c = alloc<float>((size_t)B * 6 * H);
+        float * mod_ct = alloc<float>((size_t)B * std::max(1, m.ada_ct.M));
         float * mod_t = alloc<float>((size_t)B * 6 * H);
         const bool hpm = m.hpar.connected;
         const int nhl = hpm ? m.hpar.nl : nh;             // heads this rank computes
@@ -446,10 +447,19 @@ struct Builder {
         snap("global_c", gc, (long long)B * H);
         op([=](cudaStream_t st) { return build_extended(sync_out, yS, gc, B, T, H, ext, sext, sgc, st); });
         snap("extended_c", ext, (long long)B * T * H);
-        // ---- every per-token adaLN of the step in one GEMM (mmdit.cpp:209, 285) ----
+        // ---- every per-token adaLN of the step in one GEMM (mmdit.cpp:209, 285); on a side lane
+        // beside it, every clip / text adaLN of the step in one GEMV ----
         tag = "adaln";
+        const int R_ct = m.ada_ct.w ? m.ada_ct.M : 0;
+        if (R_ct) {
+            mark(1);
+            lane = 1;
+            gemv(m.ada_ct, sgc, H, B, ACT_NONE, mod_ct, R_ct);
+            lane = 0;
+        }
         gemm(m.ada_lat, sext, B, T, H, (long long)T * H, EPI_STORE, ACT_NONE, mod_lat, 0, H, nullptr, 0, nullptr, 0, 1, 0,
              8, H, BTH);
+        if (R_ct) mark(2);
         (void)R;
 
         // ---- joint blocks (mmdit.cpp:237-272) ----
@@ -476,7 +486,11 @@ struct Builder {
                 __nv_bfloat16 * const xn = xn_l[s];
                 tag = "j" + std::to_string(i) + (s == 0 ? ".lat" : s == 1 ? ".clip" : ".text");
                 if (s == 0) { mods[s] = mod_lat + (w.ada_off / H) * BTH; lds[s] = H; css[s] = BTH; }
-                else {
+                else if (R_ct) {   // this stream's rows of the stacked clip / text adaLN output
+                    lds[s] = R_ct;
+                    css[s] = H;
+                    mods[s] = mod_ct + w.ada_ct_off;
+                } else {
                     lds[s] = (long long)(w.pre_only ? 2 : 6) * H;
                     css[s] = H;
                     gemv(w.ada, sgc, H, B, ACT_NONE, modc[s], lds[s]);

@@ -387,6 +387,42 @@ struct Finalizer {
                 }
             }
         }
+        // The clip / text adaLN of every joint block reads the same [H] conditioning (global_c),
+        // so their weights are stacked row-wise, in their stored type, into one matrix that one
+        // GEMV launch per forward streams (mmdit.cpp:209 for the clip and text blocks).
+        if (!rc) {
+            long long ct_rows = 0;
+            int ct_type = -1;
+            bool ok = true;
+            for (auto & blk : M.joint)
+                for (int s = 1; s < 3; ++s) {
+                    const VW & v = blk[s].ada;
+                    if (!v.w || !v.bias || v.w2 || v.K != M.H || (ct_type >= 0 && v.type != ct_type)) ok = false;
+                    ct_type = v.type;
+                    ct_rows += v.M;
+                }
+            if (ok && ct_rows > 0) {
+                const size_t rowb = ggml_nbytes(ct_type, M.H);
+                auto * w = reinterpret_cast<uint8_t *>(M.dalloc((size_t)ct_rows * rowb));
+                auto * b = reinterpret_cast<float *>(M.dalloc((size_t)ct_rows * 4));
+                if (!w || !b) { rc = TSD_ERR_CUDA; return; }
+                long long off = 0;
+                for (int i = 0; i < (int)M.joint.size(); ++i)
+                    for (int s = 1; s < 3; ++s) {
+                        StreamW & st = M.joint[i][s];
+                        if (cudaMemcpy(w + off * rowb, st.ada.w, (size_t)st.ada.M * rowb, cudaMemcpyDeviceToDevice) != cudaSuccess ||
+                            cudaMemcpy(b + off, st.ada.bias, (size_t)st.ada.M * 4, cudaMemcpyDeviceToDevice) != cudaSuccess) {
+                            rc = TSD_ERR_CUDA;
+                            return;
+                        }
+                        st.ada_ct_off = off;
+                        off += st.ada.M;
+                        consumed.push_back("joint_blocks." + std::to_string(i) + (s == 1 ? ".clip_block" : ".text_block") +
+                                           ".adaLN_modulation.1.weight");
+                    }
+                M.ada_ct.w = w; M.ada_ct.type = ct_type; M.ada_ct.M = (int)ct_rows; M.ada_ct.K = M.H; M.ada_ct.bias = b;
+            }
+        }
         M.fused.resize(M.hp.fused_depth);
         for (int i = 0; i < M.hp.fused_depth; ++i) {
             StreamW & w = M.fused[i];

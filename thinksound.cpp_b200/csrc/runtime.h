@@ -59,6 +59,7 @@ struct StreamW {
     long long ada_off = 0;   // latent-style: first row in the batched adaLN weight
     int ada_rows = 0;
     VW ada;                  // global-conditioned (clip / text): GEMV weight
+    long long ada_ct_off = -1;   // clip / text: first row in the stacked clip / text adaLN (Model::ada_ct)
 };
 
 struct Plan;
@@ -90,6 +91,7 @@ struct Model {
     VW te0, te2, tcp, ccp, gc13, gc2;
     const float * sync_pe = nullptr;
     GW ada_lat;                // all latent-style adaLN weights stacked (joint latent, fused, final)
+    VW ada_ct;                 // every clip / text adaLN weight stacked in its stored type (one GEMV)
     long long final_ada_off = 0;
     std::vector<std::array<StreamW, 3>> joint;
     std::vector<StreamW> fused;
