@@ -376,6 +376,7 @@ def main():
     tot_ms = float(prof["ms"].sum())
     # attention + projection path (SURVEY's "attn+proj": qkv GEMMs, attention, out-projection GEMMs)
     labels = prof["labels"]
+    sa = [i for i, l in enumerate(labels) if kinds[i] == 1 and l.startswith("adaln")]
     # (QKV GEMMs carry mode=3: their epilogue applies the QK-RMSNorm + RoPE; linear1 = mode=2 with
     # K = 3H (conv) or H (text))
     ap = [i for i, l in enumerate(labels)
@@ -468,7 +469,11 @@ def main():
                 "gemm": {"launches": g_n, "ms": g_ms, "tflops": g_tf},
                 "attention": {"launches": a_n, "ms": a_ms, "tflops": a_fl / (a_ms / 1000.0) / 1e12 if a_ms else None},
                 "gemv": {"launches": int(prof["launches"][kinds == 1].sum()), "ms": v_ms,
-                         "gbs": v_by / (v_ms / 1000.0) / 1e9 if v_ms else None},
+                         "gbs": v_by / (v_ms / 1000.0) / 1e9 if v_ms else None,
+                         # the stacked clip / text adaLN of all joint blocks (one weight stream)
+                         "stacked_adaln": ({"ms": float(prof["ms"][sa].sum()), "mb": float(prof["bytes"][sa].sum()) / 1e6,
+                                            "gbs": float(prof["bytes"][sa].sum()) / float(prof["ms"][sa].sum()) / 1e6}
+                                           if sa else None)},
                 "attn_proj": {"launches": len(ap), "ms": ap_ms, "tflop": ap_fl / 1e12,
                               "tflops": ap_fl / (ap_ms / 1000.0) / 1e12 if ap_ms else None,
                               "frac_of_sustained_peak": ap_fl / (ap_ms / 1000.0) / 1e12 / peak if ap_ms else None},
