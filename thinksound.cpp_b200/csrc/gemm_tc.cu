@@ -302,22 +302,24 @@ __device__ __forceinline__ void emit_qkv(const GemmParams & p, const EpiCtx & e,
     }
     if (p.epi_tma) {
         // this warp pair's head: [32 tokens][64] fp16 in the staging buffer, then two 16-token
-        // TMA boxes (the second only inside the tile); tokens past the stream's length are clipped
+        // TMA boxes per head (the second only inside the tile); tokens past the stream's length
+        // are clipped. The four boxes are issued by lane 0 of the four epilogue warps (a TMA
+        // instruction costs its issuing thread ~300 cycles), each committing one group per chunk;
+        // each issuer waits for its own stores of two chunks ago before the buffer is rewritten.
         uint8_t * sbuf = ebuf + (gs & 1) * kEBufBytes;
-        if (gs >= 2 && threadIdx.x == 64) bulk_wait_read<1>();
+        if (gs >= 2 && lane == 0) bulk_wait_read<1>();
         epi_bar();
         __half * hb = reinterpret_cast<__half *>(sbuf + (ml >> 6) * 4096);
 #pragma unroll
         for (int j = 0; j < 32; ++j) hb[j * 64 + d] = __float2half_rn(v[j]);
         fence_proxy_async_smem();
         epi_bar();
-        if (threadIdx.x == 64) {
+        if (lane == 0) {
             const CUtensorMap * tm = which == 0 ? tmQ : which == 1 ? tmK : tmV;
             const int h0 = (f0 - which * p.hidden) >> 6;
-            for (int hh = 0; hh < 2; ++hh) {
-                tma_store_4d(tm, sbuf + hh * 4096, 0, c.t0 + j0, h0 + hh, c.b);
-                if (j0 + 16 < p.BN) tma_store_4d(tm, sbuf + hh * 4096 + 2048, 0, c.t0 + j0 + 16, h0 + hh, c.b);
-            }
+            const int hh = q >> 1, half = q & 1;       // this warp's box: head hh, tokens half * 16 ..
+            if (half == 0 || j0 + 16 < p.BN)
+                tma_store_4d(tm, sbuf + hh * 4096 + half * 2048, 0, c.t0 + j0 + half * 16, h0 + hh, c.b);
             bulk_commit();
         }
         ++gs;
@@ -1093,6 +1095,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             bulk_wait<0>();                           // TMA stores complete before exit
         }
         if (threadIdx.x == 96) bulk_wait<0>();      // gate epilogue: this thread's reduce-adds complete
+        if (Epi<EK>::qkv && lane == 0) bulk_wait<0>();   // QKV: every epilogue warp's stores complete
     }
     tc_fence_before();
     __syncwarp();
