@@ -45,9 +45,6 @@ struct AttnArgs {
     __nv_bfloat16 * out;
     int * err;
     float scale_log2;
-    int n_peers;
-    __nv_bfloat16 * peer_out[kMaxHpRanks];
-    unsigned * peer_flag[kMaxHpRanks];
 };
 
 __device__ __forceinline__ void soft_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
@@ -251,8 +248,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             float o[32];
             tmem_ld32(lane_base + kColO + half * 32, o);
             if (t < S) {
-                const long long off = ((long long)b * S + t) * a.ldo + h * kHD + half * 32;
-                __nv_bfloat16 * dst = a.out + off;
+                __nv_bfloat16 * dst = a.out + ((long long)b * S + t) * a.ldo + h * kHD + half * 32;
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     uint4 u;
@@ -260,21 +256,12 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 #pragma unroll
                     for (int i = 0; i < 4; ++i) p2[i] = __floats2bfloat162_rn(o[e * 8 + 2 * i] * inv, o[e * 8 + 2 * i + 1] * inv);
                     *reinterpret_cast<uint4 *>(dst + e * 8) = u;
-                    // head-parallel: the same 16 bytes into every other rank's exchange buffer
-                    // (peer memory over NVLink)
-                    for (int r = 0; r < a.n_peers; ++r) *reinterpret_cast<uint4 *>(a.peer_out[r] + off + e * 8) = u;
                 }
             }
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (a.n_peers > 0 && threadIdx.x == 0) {
-        // every thread's peer stores precede this (bar.sync above); the system-scope fence makes
-        // them visible to the peers before the arrival they count
-        __threadfence_system();
-        for (int r = 0; r < a.n_peers; ++r) atomicAdd_system(a.peer_flag[r], 1u);
-    }
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
@@ -304,11 +291,6 @@ cudaError_t attn_launch(const AttnLaunch & L, cudaStream_t st) {
     AttnArgs a;
     a.S = L.S; a.nh = L.nh; a.ldo = L.ldo; a.out = reinterpret_cast<__nv_bfloat16 *>(L.out); a.err = L.err;
     a.scale_log2 = L.scale * 1.4426950408889634f;
-    a.n_peers = L.n_peers;
-    for (int r = 0; r < kMaxHpRanks; ++r) {
-        a.peer_out[r] = reinterpret_cast<__nv_bfloat16 *>(L.peer_out[r]);
-        a.peer_flag[r] = L.peer_flag[r];
-    }
     dim3 grid((L.S + kQT - 1) / kQT, L.B * L.nh);
     launch_pdl(attn_tc_kernel, dim3(grid), dim3(kThreads), kSmemBytes, st, L.tmQ, L.tmK, L.tmV, a);
     return cudaGetLastError();

@@ -217,8 +217,9 @@ struct Builder {
              nullptr, 0, 1, 0, /*max_splits=*/1);
     }
     // Attention of one layer; returns the buffer the out-projection reads (the full [B][S][H]
-    // attention output). Head-parallel: this rank's heads, their rows stored into the layer's
-    // exchange buffer here and on every peer, then a wait for the peers' rows.
+    // attention output). Head-parallel: this rank's heads into the layer's exchange buffer, this
+    // rank's column block pushed into every peer's copy of that buffer, then a wait for the
+    // peers' blocks.
     __nv_bfloat16 * attention(const __half * Q, const __half * K, const __half * V, int B, int S, __nv_bfloat16 * ao,
                               int * err) {
         const int H = m.H;
@@ -240,15 +241,26 @@ struct Builder {
         auto * X = reinterpret_cast<__nv_bfloat16 *>(hp.arena + off);
         const long long col = (long long)hp.h0 * 64;    // this rank's columns of the [B][S][H] rows
         if (!attn_plan(A, Q, K, V, B, hp.nl, S, X + col, H, err)) { rc = TSD_ERR_ARG; return ao; }
+        __nv_bfloat16 * pdst[kMaxHpRanks] = {};
+        unsigned * pflag[kMaxHpRanks] = {};
+        int np = 0;
         for (int r = 0; r < hp.world; ++r) {
             if (r == hp.rank) continue;
-            A.peer_out[A.n_peers] = reinterpret_cast<__nv_bfloat16 *>(hp.peer[r] + off) + col;
-            A.peer_flag[A.n_peers] = hp_counter(m, r, slot, hp.rank);
-            ++A.n_peers;
+            pdst[np] = reinterpret_cast<__nv_bfloat16 *>(hp.peer[r] + off);
+            pflag[np] = hp_counter(m, r, slot, hp.rank);
+            ++np;
         }
         op([A](cudaStream_t st) { return attn_launch(A, st); }, OP_ATTN, 4.0 * B * hp.nl * 64.0 * S * S,
-           6.0 * B * hp.nl * 64.0 * S + 2.0 * B * S * H * hp.world);
-        const unsigned ctas = (unsigned)(((S + 127) / 128) * B * hp.nl);
+           6.0 * B * hp.nl * 64.0 * S + 2.0 * B * S * H);
+        // this rank's column block of every row, pushed into the peers' buffers over NVLink
+        const int rows = B * S, c0 = hp.h0 * 64, nc = hp.nl * 64;
+        std::array<__nv_bfloat16 *, kMaxHpRanks> d;
+        std::array<unsigned *, kMaxHpRanks> f;
+        for (int k = 0; k < kMaxHpRanks; ++k) { d[k] = pdst[k]; f[k] = pflag[k]; }
+        const __nv_bfloat16 * src = X;
+        op([=](cudaStream_t st) { return hp_push_launch(src, d.data(), f.data(), np, rows, H, c0, nc, st); },
+           OP_COPY, 0, 2.0 * rows * nc * np);
+        const unsigned ctas = (unsigned)hp_push_ctas(rows);
         const unsigned * counters = hp_counter(m, hp.rank, slot, 0);
         const unsigned * epoch = epoch_ptr;
         const int rank = hp.rank, world = hp.world;

@@ -3,13 +3,14 @@
 // The optional 30 s mode of the MM-DiT path: each of `world` ranks owns nh / world of the
 // attention heads of every joint and fused block. A rank computes the QKV projection rows of its
 // heads only (the reference's Wqkv, src/mmdit.cpp:219, sliced per head) and attention for those
-// heads (:85-94); the attention kernel stores each head's output rows both into this rank's
-// exchange buffer and, over NVLink, into the same place in every other rank's buffer, then
-// counts its arrival on each peer. Before the out-projection (:229-230) a one-warp kernel waits
-// until every peer's CTAs of that layer have arrived. Everything else (adaLN, LN-modulate,
-// out-projection, FFN, pre-processing, final layer) runs replicated on every rank, so every
-// rank ends with the full flow. There is no library collective: the exchange is the attention
-// epilogue's own peer stores.
+// heads (:85-94) into its exchange buffer; a copy kernel then pushes this rank's column block of
+// every row (nl * 128 contiguous bytes) into the same place in every other rank's buffer over
+// NVLink and counts its arrival on each peer. Before the out-projection (:229-230) a one-warp
+// kernel waits until every peer's push CTAs of that layer have arrived. Everything else (adaLN,
+// LN-modulate, out-projection, FFN, pre-processing, final layer) runs replicated on every rank,
+// so every rank ends with the full flow. There is no library collective: the exchange is plain
+// peer stores. (Storing the rows from the attention epilogue itself was measured slower: its
+// warp stores are 16-byte pieces of 32 different rows, which NVLink carries poorly.)
 //
 // Exchange arena (one cudaMalloc per rank, its IPC handle shared with the peers at set-up):
 //   [0, kFlagBytes)           arrival counters u32 [slot][rank], monotonic
@@ -66,7 +67,46 @@ __global__ void hp_wait_kernel(const unsigned * counters, const unsigned * epoch
     asm volatile("fence.proxy.async.global;" ::: "memory");   // the peers' rows are next read by TMA
 }
 
+// Copies this rank's column block [col0, col0 + ncols) of every row of X ([rows][H] bf16) to the
+// same place in every peer's buffer (a warp per row: the block is nl * 128 contiguous bytes, so a
+// warp instruction moves 512 contiguous bytes over NVLink), then counts this CTA's arrival on
+// every peer.
+struct HpPeers {
+    __nv_bfloat16 * dst[kMaxHpRanks];
+    unsigned * flag[kMaxHpRanks];
+};
+__global__ void __launch_bounds__(256) hp_push_kernel(const __nv_bfloat16 * __restrict__ X, const HpPeers peers,
+                                                      int n_peers, int rows, int H, int col0, int ncols) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nv = ncols >> 3;                       // 16-byte words of a row's block
+    for (int r = blockIdx.x * 8 + warp; r < rows; r += gridDim.x * 8) {
+        const long long base = (long long)r * H + col0;
+        const uint4 * s = reinterpret_cast<const uint4 *>(X + base);
+        for (int i = lane; i < nv; i += 32) {
+            const uint4 v = s[i];
+            for (int p = 0; p < n_peers; ++p) reinterpret_cast<uint4 *>(peers.dst[p] + base)[i] = v;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int p = 0; p < n_peers; ++p) atomicAdd_system(peers.flag[p], 1u);
+    }
+}
+
 }  // namespace
+
+int hp_push_ctas(int rows) { return rows < 1 ? 1 : (rows + 7) / 8 < 296 ? (rows + 7) / 8 : 296; }
+
+cudaError_t hp_push_launch(const __nv_bfloat16 * X, __nv_bfloat16 * const * dst, unsigned * const * flag, int n_peers,
+                           int rows, int H, int col0, int ncols, cudaStream_t st) {
+    HpPeers pe{};
+    for (int p = 0; p < n_peers && p < kMaxHpRanks; ++p) { pe.dst[p] = dst[p]; pe.flag[p] = flag[p]; }
+    launch_pdl(hp_push_kernel, dim3(hp_push_ctas(rows)), dim3(256), 0, st, X, pe, n_peers, rows, H, col0, ncols);
+    return cudaGetLastError();
+}
 
 bool hp_layout(int H, int nh, int world, int rank, int & h0, int & nl, int & sec) {
     if (world < 1 || world > kMaxHpRanks || rank < 0 || rank >= world || nh < 1 || nh % world || H != nh * 64)

@@ -142,12 +142,6 @@ struct AttnLaunch {
     void * out;
     int * err;
     float scale;
-    // Head-parallel exchange (n_peers > 0): every output row is also stored at peer_out[r] (the
-    // same offsets in rank r's exchange buffer, mapped into this process), and each CTA, once its
-    // rows are stored, adds 1 to peer_flag[r] (rank r's arrival counter for this layer and rank).
-    int n_peers = 0;
-    void * peer_out[kMaxHpRanks] = {};
-    unsigned * peer_flag[kMaxHpRanks] = {};
 };
 bool attn_plan(AttnLaunch & L, const void * Q, const void * K, const void * V, int B, int nh, int S,
                void * out, long long ldo, int * err);

@@ -177,6 +177,9 @@ long long hp_carve(Model & m, size_t bytes);            // arena offset, or -1 w
 unsigned * hp_counter(Model & m, int on_rank, int slot, int from_rank);
 unsigned * hp_epoch(Model & m, int plan);
 cudaError_t hp_epoch_launch(unsigned * epoch, cudaStream_t st);
+int hp_push_ctas(int rows);
+cudaError_t hp_push_launch(const __nv_bfloat16 * X, __nv_bfloat16 * const * dst, unsigned * const * flag, int n_peers,
+                           int rows, int H, int col0, int ncols, cudaStream_t st);
 cudaError_t hp_wait_launch(const unsigned * counters, const unsigned * epoch, int rank, int world, unsigned ctas,
                            int * err, cudaStream_t st);
 // Enqueue the forward (inputs already in the plan's buffers). reuse_cond: the conditioning
