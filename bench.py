@@ -6,12 +6,16 @@ T=194 (9 s), clip 72, sync 216, MetaCLIP-text 77 + T5 128 tokens. Weights random
 N(0, 0.02^2) in the BF16-GGUF storage types, inputs seeded N(0,1), all synthetic.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--pairs P] [--impl ours|reference]
+                  [--workload cfg3|cfg4|cfg5] [--head-parallel]
 
 N>1: launched by torchrun, one process per GPU; each rank runs its own P pairs (weak scaling,
 no collective on the data path). `value` = pair-steps/s of the whole job. `e2e` times the same
-steps through the public host-buffer C-ABI (tsd_forward_batched: H2D of inputs, D2H of the
-flow inside the timed region). `--impl reference` times the reference path's CPU restatement
-(oracle/, the GGML CPU backend is not buildable here) on the host cores.
+steps through the public host-buffer C-ABI (tsd_forward_batched on pinned host buffers: H2D of
+the inputs and D2H of the flow inside the timed region). `--impl reference` times the reference
+path's CPU restatement (oracle/, the GGML CPU backend is not buildable here) on the host cores.
+`--workload cfg4`: the same step at 30 s with Q8_0 weights; `--head-parallel` (N>1): the ranks
+split that step's heads (strong scaling of one pair); `--workload cfg5`: 64 prompts x 24 Euler
+steps sharded over the ranks.
 """
 from __future__ import annotations
 
