@@ -378,7 +378,8 @@ def main():
     a_ms, a_fl, a_by, a_n = agg(2)
     v_ms, v_fl, v_by, v_n = agg(1)
     tot_ms = float(prof["ms"].sum())
-    # attention + projection path (SURVEY's "attn+proj": qkv GEMMs, attention, out-projection GEMMs)
+    # attention + projection path of the headline metric ("MM-DiT attn TFLOP/s"): the QKV GEMMs,
+    # attention and the out-projection (linear1) GEMMs
     labels = prof["labels"]
     sa = [i for i, l in enumerate(labels) if kinds[i] == 1 and l.startswith("adaln")]
     # (QKV GEMMs carry mode=3: their epilogue applies the QK-RMSNorm + RoPE; linear1 = mode=2 with
