@@ -145,43 +145,53 @@ def make_device_inputs(B, shape, seed, device, clip_dim=1024, sync_dim=768, text
 
 
 # ----------------------------------------------------------------------------------- CPU legs
-def cpu_sample(seconds_hint=True):
-    """Time the CPU restatement on a bounded sample of the cfg-3 step: a truncated model
-    (2 joint + 1 fused blocks + pre/final) at the full cfg-3 widths and sequence lengths,
-    B=2 (one CFG pair), scaled to whole steps by the FLOP ratio."""
-    import numpy as np
-    sys.path.insert(0, os.path.join(REPO, "oracle"))
-    import oracle
-    import tsd_b200.synth as synth
-    hp_full = synth.DitHParams(**HP3)
-    hp_s = synth.DitHParams(hidden=1536, n_head=24, depth=3, fused_depth=1)
-    W = synth.make_weights(hp_s, seed=1234, wtype="bf16")
-    om = oracle.OracleModel(hp_s, W)
-    del W
-    items = synth.make_inputs(hp_s, seed=4242, batch=2, **CFG3)
-    om.forward(items[0], mode=oracle.MODE_EXACT)       # warm-up (page-in)
-    t0 = time.perf_counter()
-    for x in items:
-        om.forward(x, mode=oracle.MODE_EXACT)
-    dt = time.perf_counter() - t0
-    f_s = synth.step_flops(hp_s, 2, **CFG3)["total"]
-    f_full = synth.step_flops(hp_full, 2, **CFG3)["total"]
-    step_s = dt * f_full / f_s
-    return dict(value=1.0 / step_s, unit=UNIT, cores=oracle.num_threads(), kind="port",
-                sample=f"oracle (C++ restatement of src/mmdit.cpp, f32, OpenMP) on a truncated cfg-3 model "
-                       f"(2 joint + 1 fused blocks, H=1536, B=2): {dt:.2f} s for {f_s / 1e9:.0f} GFLOP, "
-                       f"scaled to the full step ({f_full / 1e9:.0f} GFLOP)",
-                seconds=dt)
+class CpuSampler:
+    """The CPU restatement on a bounded sample of the cfg-3 step: a truncated model (2 joint +
+    1 fused blocks + pre/final) at the full cfg-3 widths and sequence lengths, B=2 (one CFG pair),
+    scaled to whole steps by the FLOP ratio. The model is built (and paged in by one untimed
+    forward) once; each `sample()` times one forward of both items of the pair."""
+
+    def __init__(self):
+        sys.path.insert(0, os.path.join(REPO, "oracle"))
+        import oracle
+        import tsd_b200.synth as synth
+        self.oracle = oracle
+        hp_full = synth.DitHParams(**HP3)
+        hp_s = synth.DitHParams(hidden=1536, n_head=24, depth=3, fused_depth=1)
+        W = synth.make_weights(hp_s, seed=1234, wtype="bf16")
+        self.om = oracle.OracleModel(hp_s, W)
+        del W
+        self.items = synth.make_inputs(hp_s, seed=4242, batch=2, **CFG3)
+        self.om.forward(self.items[0], mode=oracle.MODE_EXACT)       # warm-up (page-in)
+        self.f_s = synth.step_flops(hp_s, 2, **CFG3)["total"]
+        self.f_full = synth.step_flops(hp_full, 2, **CFG3)["total"]
+
+    def sample(self):
+        t0 = time.perf_counter()
+        for x in self.items:
+            self.om.forward(x, mode=self.oracle.MODE_EXACT)
+        dt = time.perf_counter() - t0
+        step_s = dt * self.f_full / self.f_s
+        return dict(value=1.0 / step_s, unit=UNIT, cores=self.oracle.num_threads(), kind="port",
+                    sample=f"oracle (C++ restatement of src/mmdit.cpp, f32, OpenMP) on a truncated cfg-3 model "
+                           f"(2 joint + 1 fused blocks, H=1536, B=2): {dt:.2f} s for {self.f_s / 1e9:.0f} GFLOP, "
+                           f"scaled to the full step ({self.f_full / 1e9:.0f} GFLOP)",
+                    seconds=dt)
+
+
+def cpu_sample():
+    return CpuSampler().sample()
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    cb = cpu_sample()
-    steps = []
-    for _ in range(max(1, min(args.steps, 2))):
-        steps.append(cpu_sample()["value"])
-    v = statistics.median(steps)
+    import __graft_entry__
+    __graft_entry__.load_package()      # the synthetic-weight generator lives in the package
+    sampler = CpuSampler()
+    steps = [sampler.sample() for _ in range(max(1, min(args.steps, 2)))]
+    v = statistics.median(c["value"] for c in steps)
+    cb = dict(steps[0])
     cb["value"] = v
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": len(steps),
             "warmup": 1, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -222,19 +232,66 @@ def profile_case(wtype):
 CFG5 = dict(prompts=64, steps=24, cfg=5.0)
 
 
-def run_cfg5(args, rank, world, local):
-    """batched 24-step Euler CFG sampling of 64 prompts (cond + uncond each),
-    T=194, BF16, random-init weights, per-prompt seeded inputs with the config-3 shapes; prompts
-    sharded over the ranks (no collective while sampling), latents gathered to rank 0. Timed per
-    run around the whole job (each rank's synchronous tsd_sample_batched call, then the gather),
-    max over ranks; value = prompts x steps / seconds (pair-steps/s, the same unit as config 3)."""
-    import datetime
+def cfg5_measure(model, hp, rank, world, dev, pg, runs=2):
+    """BASELINE config 5 on an already loaded model: batched 24-step Euler CFG sampling of 64
+    prompts (cond + uncond each), T=194, per-prompt seeded inputs with the config-3 shapes;
+    prompts sharded over the ranks (no collective while sampling), latents gathered to rank 0.
+    Each run is timed around the whole job: a barrier and a device synchronise, each rank's
+    synchronous tsd_sample_batched call on its shard, the NCCL gather of the latents to rank 0,
+    a device synchronise; the max over ranks is taken. value = prompts x steps / seconds
+    (pair-steps/s, the unit of config 3). Returns the result dict on rank 0, None elsewhere."""
     import numpy as np
+    import torch
+    import tsd_b200.synth as synth
+    from tsd_b200 import dp
+
+    P, steps, cfg = CFG5["prompts"], CFG5["steps"], CFG5["cfg"]
+    lo, hi = dp.shard_range(P, rank, world)
+    items = [None] * P
+    for i in range(lo, hi):   # this rank's prompts only; prompt i always has seed 4242 + i
+        items[i] = synth.make_inputs(hp, **CFG3, seed=4242 + i)[0]
+
+    def sample_fn(it, n_steps, c):
+        return model.sample(it, n_steps, c)
+
+    if hi > lo:
+        sample_fn(items[lo:hi], 2, cfg)   # warm-up: builds the plan for this batch shape
+    times = []
+    out = None
+    for _ in range(max(1, runs)):
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        out = dp.sample_sharded(sample_fn, items, steps, cfg, rank, world, device=dev if pg else None)
+        torch.cuda.synchronize()
+        dt = torch.tensor([time.perf_counter() - t0], device=dev, dtype=torch.float64)
+        if pg:
+            pg.all_reduce(dt, op=pg.ReduceOp.MAX)
+        times.append(float(dt[0]))
+    if rank != 0:
+        return None
+    best = min(times)
+    assert out is not None and out.shape == (P, hp.latent_dim, CFG3["T"]) and np.isfinite(out).all()
+    fl = synth.step_flops(hp, 2, **CFG3)
+    return {"metric": "DiT CFG sampling pair-steps/s (cfg5: 64 prompts x 24 Euler steps, CFG 5, 9 s, BF16)",
+            "value": P * steps / best, "unit": UNIT, "n_gpus": world, "scaling": "strong",
+            "ms_per_step": best * 1000.0 / steps, "prompts": P, "prompts_per_gpu": hi - lo, "steps": steps,
+            "parallelism": f"dp{world} (prompts; latents gathered to rank 0 with NCCL inside the timed region)",
+            "runs_s": times, "tflop_per_run": P * steps * fl["total"] / 1e12,
+            "tflops": P * steps * fl["total"] / best / 1e12,
+            "timing": "barrier + device sync, each rank's synchronous sampling call + the gather, device sync; "
+                      "max over ranks; best of the runs"}
+
+
+def run_cfg5(args, rank, world, local):
+    """`--workload cfg5`: config 5 alone (see cfg5_measure), one JSON line from rank 0."""
+    import datetime
     import torch
     import __graft_entry__
     __graft_entry__.load_package()
     import tsd_b200.synth as synth
-    from tsd_b200 import dp, tsd
+    from tsd_b200 import tsd
 
     torch.cuda.set_device(local)
     dev = f"cuda:{local}"
@@ -249,44 +306,13 @@ def run_cfg5(args, rank, world, local):
     model = tsd.DitModel.from_weights(hp, W, device=local)
     del W
     torch.cuda.empty_cache()
-    P, steps, cfg = CFG5["prompts"], CFG5["steps"], CFG5["cfg"]
-    lo, hi = dp.shard_range(P, rank, world)
-    items = [None] * P
-    for i in range(lo, hi):   # this rank's prompts only; prompt i always has seed 4242 + i
-        items[i] = synth.make_inputs(hp, **CFG3, seed=4242 + i)[0]
-
-    def sample_fn(it, n_steps, c):
-        return model.sample(it, n_steps, c)
-
-    if hi > lo:
-        sample_fn(items[lo:hi], 2, cfg)   # warm-up: builds the plan for this batch shape
-    times = []
-    out = None
-    for _ in range(max(1, args.runs)):
-        if pg:
-            pg.barrier()
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        out = dp.sample_sharded(sample_fn, items, steps, cfg, rank, world, device=dev if pg else None)
-        torch.cuda.synchronize()
-        dt = torch.tensor([time.perf_counter() - t0], device=dev, dtype=torch.float64)
-        if pg:
-            pg.all_reduce(dt, op=pg.ReduceOp.MAX)
-        times.append(float(dt[0]))
-    best = min(times)
+    r = cfg5_measure(model, hp, rank, world, dev, pg, runs=args.runs)
     if rank == 0:
-        assert out is not None and out.shape == (P, hp.latent_dim, CFG3["T"]) and np.isfinite(out).all()
-        fl = synth.step_flops(hp, 2, **CFG3)
-        line = {
-            "metric": "DiT CFG sampling pair-steps/s (cfg5: 64 prompts x 24 Euler steps, CFG 5, 9 s, BF16)",
-            "value": P * steps / best, "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": 1,
-            "ms_per_step": best * 1000.0 / steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (per-prompt seeded inputs, random-init weights)",
-            "config": {"workload": "cfg5 batched sampling", "prompts": P, "prompts_per_gpu": hi - lo,
-                       "parallelism": f"dp{world} (prompts; latents gathered to rank 0)",
-                       "runs_s": times, "tflop_per_run": P * steps * fl["total"] / 1e12},
-            "timing": "host clock around each rank's synchronous sampling call + the gather, max over ranks",
-        }
+        line = dict(r)
+        line.update({"warmup": 1, "higher_is_better": True, "vs_baseline": None, "dtype": "bf16",
+                     "data": "synthetic (per-prompt seeded inputs, random-init weights)",
+                     "config": {"workload": "cfg5 batched sampling", "prompts": r["prompts"],
+                                "prompts_per_gpu": r["prompts_per_gpu"], "parallelism": r["parallelism"]}})
         print(json.dumps(line), flush=True)
     model.close()
     if pg:
@@ -308,6 +334,8 @@ def main():
                          "sync 720, T5 512) with Q8_0 weights; cfg5: 64 prompts x 24 Euler steps, CFG 5, "
                          "sharded over the ranks, latents gathered to rank 0")
     ap.add_argument("--runs", type=int, default=2, help="cfg5: timed sampling runs")
+    ap.add_argument("--no-cfg5", action="store_true",
+                    help="skip the config-5 sampling measurement that the default (cfg3) run adds as `cfg5`")
     ap.add_argument("--head-parallel", action="store_true",
                     help="with torchrun N>1: the ranks split the 24 heads of one CFG pair's forward (QKV rows and "
                          "attention), exchanging attention rows over NVLink peer memory; all ranks compute the "
@@ -343,7 +371,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device(dev))
         pg = dist
     peaks = load_peaks()
-    hp = synth.DitHParams(**HP3)
+    # learned empties as long as the config-3 text / T5 sequences (the config-5 sampler's uncond pass)
+    hp = synth.DitHParams(**HP3, text_seq=CFG3["text_S"], t5_seq=CFG3["t5_S"])
     B = 2 * args.pairs
     cfg4 = args.workload == "cfg4"
     SH = CFG4 if cfg4 else CFG3
@@ -433,10 +462,24 @@ def main():
     value = jobs * args.pairs * args.steps / (ms_max / 1000.0)
     e2e_value = jobs * args.pairs * args.steps / (e2e_ms_max / 1000.0)
 
+    # ---- config 5 (batched CFG sampling, prompts sharded over the ranks, latents gathered) ----
+    c5 = None
+    if not cfg4 and not hpar and not args.no_cfg5:
+        c5 = cfg5_measure(model, hp, rank, world, dev, pg, runs=max(1, args.runs))
+
     if rank == 0:
         fl = synth.step_flops(hp, B, **SH)
-        g_tf = g_fl / (g_ms / 1000.0) / 1e12 if g_ms > 0 else 0.0
-        peak = peaks["bf16_sus"]
+        ms_step = ms_max / args.steps
+        # The per-op pass runs the ops one at a time (CUDA events between them, no graph, no lane
+        # overlap), so its times are serialised. Each kernel class's time inside the timed
+        # graph-replayed step is estimated as its serialised share of the step times the timed
+        # step, which keeps the classes' sum equal to the step; the step time itself bounds the
+        # class time from above, which gives the lower bound on the class's rate.
+        share = (lambda x: x / tot_ms) if tot_ms else (lambda x: 0.0)
+        g_step_ms = ms_step * share(g_ms)
+        g_tf = g_fl / (g_step_ms / 1000.0) / 1e12 if g_step_ms > 0 else 0.0
+        g_tf_lb = g_fl / (ms_step / 1000.0) / 1e12
+        peak, peak_b = peaks["bf16_sus"], peaks["bf16"]
         cpu = None
         if world == 1 and not args.no_cpu_baseline and not cfg4:
             try:
@@ -444,8 +487,8 @@ def main():
                 cpu = {k: c[k] for k in ("value", "unit", "cores", "kind", "sample")}
             except Exception as ex:  # report, do not hide
                 cpu = {"value": None, "unit": UNIT, "cores": None, "kind": "port", "sample": f"failed: {ex}"}
-        # DRAM bytes per GEMM launch: the ratio measured by ncu over all GEMM launches of one
-        # forward with the same shapes (profiles/gemm_tc_cfg3_b2.md), times an average launch's FLOPs
+        # DRAM bytes per GEMM launch: the ratio ncu measured over all GEMM launches of one forward
+        # with the same shapes (GEMM_DRAM_BYTES_PER_FLOP), times an average launch's FLOPs
         traffic = GEMM_DRAM_BYTES_PER_FLOP * (g_fl / max(1, g_n)) if not cfg4 else None
         workload = ("cfg3 full flow step: 7 joint + 14 fused MM-DiT blocks + pre/final, H=1536, "
                     "24x64 heads, T=194 clip=72 sync=216 text=77+128 (joint S=471)")
@@ -453,9 +496,26 @@ def main():
             workload = ("cfg4 full flow step at 30 s, Q8_0 weights (random blocks; conv weights F32 as in the "
                         "reference's Q8_0 files): 7 joint + 14 fused, H=1536, 24x64 heads, T=646 clip=240 sync=720 "
                         "text=77+512 (joint S=1475)")
+        # config 1, the headline "MM-DiT attn TFLOP/s": one joint block's attention layer (the three
+        # streams' QKV projections with their fused QK-norm / RoPE, the joint attention, the three
+        # out-projections), averaged over the joint blocks whose clip / text streams are not pre_only
+        layers = []
+        for i in range(hp.depth - hp.fused_depth):
+            sel = [k for k in ap if labels[k].startswith(f"j{i}.") or labels[k].startswith(f"j{i} ")]
+            if sum(1 for k in sel if kinds[k] == 0) == 6:
+                layers.append((float(prof["ms"][sel].sum()), float(prof["flops"][sel].sum())))
+        cfg1 = None
+        if layers:
+            l_ms = statistics.mean(m for m, _ in layers)
+            l_fl = statistics.mean(f for _, f in layers)
+            l_step = ms_step * share(l_ms)
+            cfg1 = {"gflop": l_fl / 1e9, "serialised_ms": l_ms, "serialised_tflops": l_fl / l_ms / 1e9,
+                    "in_step_ms": l_step, "tflops": l_fl / l_step / 1e9,
+                    "frac_of_burst": l_fl / l_step / 1e9 / peak_b, "frac_of_sustained": l_fl / l_step / 1e9 / peak,
+                    "layers_averaged": len(layers)}
         line = {
             "metric": METRIC if not cfg4 else "DiT flow-steps/s at 30 s, CFG=2, Q8_0 weights", "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong" if hpar else "weak",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) inputs, random-init weights, " + ("Q8_0" if cfg4 else "BF16") +
@@ -468,27 +528,39 @@ def main():
                        "step_tflop": fl["total"] / 1e12, "attn_proj_tflop": fl["attn_proj"] / 1e12},
             "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05 projections, all launches of a step)",
                          "achieved": g_tf, "peak": peak, "unit": "TFLOP/s", "frac": g_tf / peak,
-                         "peak_kind": f"bf16 sustained ({peaks['src']})", "traffic": traffic,
-                         "share_of_step": g_ms / tot_ms if tot_ms else None},
+                         "peak_kind": f"bf16 sustained ({peaks['src']})",
+                         "frac_of_burst": g_tf / peak_b, "peak_burst": peak_b,
+                         "achieved_lower_bound": g_tf_lb, "frac_lower_bound": g_tf_lb / peak,
+                         "gemm_ms_in_step": g_step_ms, "share_of_step": share(g_ms),
+                         "method": "GEMM FLOPs per step / (timed graph step x the GEMMs' share of the serialised "
+                                   "per-op pass); lower bound: GEMM FLOPs per step / timed step",
+                         "traffic": traffic},
+            "attn_layer_cfg1": cfg1,
             "kernels": {
-                "gemm": {"launches": g_n, "ms": g_ms, "tflops": g_tf},
-                "attention": {"launches": a_n, "ms": a_ms, "tflops": a_fl / (a_ms / 1000.0) / 1e12 if a_ms else None},
+                "note": "ms: serialised per-op pass (CUDA events between ops, no graph); in_step_ms: share of the timed step",
+                "gemm": {"launches": g_n, "ms": g_ms, "in_step_ms": g_step_ms, "tflops": g_tf},
+                "attention": {"launches": a_n, "ms": a_ms, "in_step_ms": ms_step * share(a_ms),
+                              "tflops": a_fl / (ms_step * share(a_ms) / 1000.0) / 1e12 if a_ms else None},
                 "gemv": {"launches": int(prof["launches"][kinds == 1].sum()), "ms": v_ms,
-                         "gbs": v_by / (v_ms / 1000.0) / 1e9 if v_ms else None,
+                         "in_step_ms": ms_step * share(v_ms),
+                         "gbs": v_by / (ms_step * share(v_ms) / 1000.0) / 1e9 if v_ms else None,
                          # the stacked clip / text adaLN of all joint blocks (one weight stream)
                          "stacked_adaln": ({"ms": float(prof["ms"][sa].sum()), "mb": float(prof["bytes"][sa].sum()) / 1e6,
                                             "gbs": float(prof["bytes"][sa].sum()) / float(prof["ms"][sa].sum()) / 1e6}
                                            if sa else None)},
-                "attn_proj": {"launches": len(ap), "ms": ap_ms, "tflop": ap_fl / 1e12,
-                              "tflops": ap_fl / (ap_ms / 1000.0) / 1e12 if ap_ms else None,
-                              "frac_of_sustained_peak": ap_fl / (ap_ms / 1000.0) / 1e12 / peak if ap_ms else None},
+                "attn_proj": {"launches": len(ap), "ms": ap_ms, "in_step_ms": ms_step * share(ap_ms),
+                              "tflop": ap_fl / 1e12,
+                              "tflops": ap_fl / (ms_step * share(ap_ms) / 1000.0) / 1e12 if ap_ms else None,
+                              "frac_of_sustained_peak": ap_fl / (ms_step * share(ap_ms) / 1000.0) / 1e12 / peak if ap_ms else None,
+                              "frac_of_burst_peak": ap_fl / (ms_step * share(ap_ms) / 1000.0) / 1e12 / peak_b if ap_ms else None},
                 "other_ms": tot_ms - g_ms - a_ms - v_ms, "profiled_step_ms": tot_ms,
-                "step_tflops_device": fl["total"] / (ms_max / args.steps / 1000.0) / 1e12,
+                "step_tflops_device": fl["total"] / (ms_step / 1000.0) / 1e12,
             },
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": d2h},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
+            "cfg5": c5,
         }
         print(json.dumps(line), flush=True)
     if pg:

@@ -86,6 +86,22 @@ TSD_API int tsd_forward_batched(tsd_model * m, int B, const float * latent, int6
                         const float * text_f, int64_t text_S, const float * t5, int64_t t5_S,
                         const float * global_text, float * flow_out, tsd_dbg_fn dbg, void * ud);
 
+/* Stage capture with teacher forcing, for parity tests (the reference's dit_test compares the
+ * stages of one free-running forward, src/tools/dit_test.cpp:38-59; this also lets a test start
+ * every block from the same input as the reference). Like tsd_forward_batched with `dbg`, which
+ * additionally receives every block's output ("blk<i>_lat", "blk<i>_clip", "blk<i>_text"; i
+ * counts the joint blocks, then the fused blocks) and the residual stream after the attention
+ * half of each block ("blk<i>_attn_lat" ...). Before block i runs, inject(ud, name, data, n) is
+ * offered each residual stream the block reads ("blk<i>_in_lat", "blk<i>_in_clip",
+ * "blk<i>_in_text"; before the final layer "final_in_lat"), host f32 [B][S][hidden]; if it
+ * returns non-zero, its (modified) data replace the stream. Runs op by op, without a graph. */
+typedef int (*tsd_inject_fn)(void * ud, const char * name, float * data, int64_t n);
+TSD_API int tsd_forward_inject(tsd_model * m, int B, const float * latent, int64_t T, const float * t,
+                               const float * clip_f, int64_t clip_S, const float * sync_f, int64_t sync_S,
+                               const float * text_f, int64_t text_S, const float * t5, int64_t t5_S,
+                               const float * global_text, float * flow_out, tsd_dbg_fn dbg, tsd_inject_fn inject,
+                               void * ud);
+
 /* Device-resident forward: same layouts, all pointers in device memory of the model's GPU,
  * enqueued on `stream` (cudaStream_t; NULL = default stream) without host synchronisation.
  * Inputs are read and flow_out written in stream order. Call tsd_sync_check afterwards to
@@ -128,6 +144,14 @@ TSD_API int tsd_sample_batched(tsd_model * m, int P, const float * noise, int64_
 TSD_API int tsd_hp_layout(int hidden, int n_head, int world, int rank, int32_t out[3]); /* h0, heads, rows per Q/K/V section */
 TSD_API int tsd_hp_init(tsd_model * m, int rank, int world, size_t arena_bytes, void * handle_out);
 TSD_API int tsd_hp_connect(tsd_model * m, const void * handles);
+
+/* Deadline of every bounded device-side wait of the library's kernels on `device` (mbarrier
+ * waits of the GEMM and attention pipelines, the cluster split-K handshakes, the head-parallel
+ * arrival wait), in nanoseconds, 1 ms to 60 s; 2 s by default. A wait that runs out records an
+ * error in the model's device error word and its kernel returns; the call then reports
+ * TSD_ERR_DEVICE. No counterpart in the reference, whose GGML kernels have no device-side
+ * waits. Call it while no kernel of the library runs on the device. */
+TSD_API int tsd_set_wait_limit(int device, uint64_t ns);
 
 /* Library / device information. */
 TSD_API const char * tsd_version(void);

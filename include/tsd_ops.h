@@ -48,17 +48,36 @@ TSD_API int tsd_op_gemm(const void * W, int M, int K_in, int taps, int pad, cons
                 int * err, void * stream);
 
 /* tsd_op_gemm for callers that cannot allocate device memory (no counterpart in the
- * reference): same arguments and results, but the split-K scratch comes from fixed
- * file-scope device arrays in the library (8 MB of partial tiles + 32 KB of counters, held by
+ * reference): same arguments, and the same tiling and results as tsd_op_gemm given
+ * TSD_GEMM_STATIC_WS_FLOATS floats and TSD_GEMM_STATIC_COUNTERS counters of scratch, but that
+ * scratch is a pair of fixed file-scope device arrays in the library (8 MB + 32 KB, held by
  * every GPU that loads the library until exit), so the call performs no cudaMalloc/cudaFree.
- * Outputs are limited to m_valid * nbatch * S <= 1048576 values; larger requests return
- * TSD_ERR_ARG with a message. The first call on a device looks up the arrays' addresses
- * (make it before any stream capture). All calls on a device share the arrays: calls that
- * overlap on the GPU race. */
+ * Shapes whose best split-K plan would need more scratch run with fewer K splits (the planner
+ * keeps every plan within the arrays); a plan beyond them is rejected with TSD_ERR_ARG and a
+ * message. The first call on a device (and the first after its context is recreated) looks up
+ * the arrays' addresses: make it before any stream capture. All calls on a device share the
+ * arrays, which keep the last call's contents: calls that overlap on the GPU race. */
+#define TSD_GEMM_STATIC_WS_FLOATS 2097152
+#define TSD_GEMM_STATIC_COUNTERS 8192
 TSD_API int tsd_op_gemm_static(const void * W, int M, int K_in, int taps, int pad, const void * X, int nbatch, int S,
                                int64_t x_row_stride, int64_t x_batch_stride, int mode, int act, const float * bias,
                                int m_valid, void * out, int out_bf16, int64_t ldo, float * resid, int64_t ldr,
                                const float * gate, int64_t ldg, int gate_div, int max_splits, int * err, void * stream);
+
+/* The tiling tsd_op_gemm would choose for a GEMM shape given `ws_floats` / `n_counters` of
+ * scratch (no launch; for tests and tuning). out[0] token tile, out[1] K splits, out[2] 1 for
+ * CTA pairs, out[3] 1 if the splits reduce inside a thread-block cluster (no scratch), out[4]
+ * scratch floats the plan needs (non-zero only for split-K through global memory). Needs the
+ * GPU the GEMM would run on to be current (cluster occupancy is a property of the device). */
+TSD_API int tsd_op_gemm_plan(int M, int K_in, int taps, int nbatch, int S, int max_splits, int64_t ws_floats,
+                             int n_counters, int64_t out[5]);
+
+/* The head-parallel arrival wait (tsd_hp_* in tsd.h) as an operator: one warp waits until
+ * counters[r] >= *epoch * ctas for every rank r != rank of `world`, bounded by the wait limit
+ * (tsd_set_wait_limit); on expiry it sets *err (if non-NULL) to a non-zero code and returns.
+ * counters and epoch are device memory. Used to test the error path of the exchange. */
+TSD_API int tsd_op_peer_wait(const uint32_t * counters, const uint32_t * epoch, int rank, int world, uint32_t ctas,
+                             int * err, void * stream);
 
 /* Few-token GEMV with weights in their stored ggml type (0 F32, 30 BF16, 8 Q8_0), N <= 8
  * (the [H,1]-column mul_mats of mmdit.cpp:158-160,185-192,209). W2 != NULL: SwiGLU pair. */
@@ -69,6 +88,11 @@ TSD_API int tsd_op_gemv(const void * W, int ggml_type, const void * W2, int M, i
  * out bf16 token-major out[b][t][h*64+d] with row stride ldo (elements). */
 TSD_API int tsd_op_attention(const void * Q, const void * K, const void * V, int B, int nh, int S, void * out, int64_t ldo,
                      int * err, void * stream);
+
+/* tsd_op_attention with f32 output (same kernel and arithmetic; the output is not rounded to
+ * bf16), for parity checks of the attention itself. out[b][t][h*64+d], row stride ldo. */
+TSD_API int tsd_op_attention_f32(const void * Q, const void * K, const void * V, int B, int nh, int S, float * out,
+                                 int64_t ldo, int * err, void * stream);
 
 /* LayerNorm (eps 1e-5, no affine) + modulate x*(1+scale)+shift (mmdit.cpp:55-59,218,232):
  * x f32 [rows][H] -> y bf16; shift/scale row = row (per_token) or row / rows_per_item. */

@@ -302,14 +302,17 @@ struct Ctx {
         return P;
     }
     // post_attn (mmdit.cpp:226-235)
+    // `attn_name`: stage name of the residual stream after the attention half (gate_msa * out-proj
+    // added, :231), before the FFN half.
     void post_attn(const std::string & bp, std::vector<float> & x, int64_t N, const std::vector<float> & ao,
-                   const Pre & P, bool is_text) const {
+                   const Pre & P, bool is_text, const std::string & attn_name) const {
         const int64_t H = M.hidden;
         auto l1 = is_text ? lin(bp + ".linear1.weight", bp + ".linear1.bias", ao, N)
                           : conv(bp + ".linear1.weight", bp + ".linear1.bias", ao, N, 1);
         const float * gate_msa = P.mod.data() + 2 * H;
         for (int64_t n = 0; n < N; ++n)
             for (int64_t i = 0; i < H; ++i) x[(size_t)(n * H + i)] += l1[(size_t)(n * H + i)] * gate_msa[n * P.mod_stride + i];
+        dbg(attn_name.c_str(), x);
         auto r = ln_modulate(x, N, H, P.mod.data() + 3 * H, P.mod.data() + 4 * H, P.mod_stride);
         auto f = is_text ? mlp(bp + ".ffn", r, N) : convmlp(bp + ".ffn", r, N);
         const float * gate_mlp = P.mod.data() + 5 * H;
@@ -409,11 +412,14 @@ struct Ctx {
             std::vector<float> ao_l(ao.begin(), ao.begin() + T * H);
             std::vector<float> ao_c(ao.begin() + T * H, ao.begin() + (T + clip_S) * H);
             std::vector<float> ao_t(ao.begin() + (T + clip_S) * H, ao.end());
-            post_attn(jb + ".latent_block", lat, T, ao_l, pl, false);
+            // per-block stage names (the GPU library reports the same ones)
+            const std::string bi = "blk" + std::to_string(i);
+            post_attn(jb + ".latent_block", lat, T, ao_l, pl, false, bi + "_attn_lat");
             if (!pre_only) {
-                post_attn(jb + ".clip_block", clip, clip_S, ao_c, pc, false);
-                post_attn(jb + ".text_block", text, St, ao_t, pt, true);
+                post_attn(jb + ".clip_block", clip, clip_S, ao_c, pc, false, bi + "_attn_clip");
+                post_attn(jb + ".text_block", text, St, ao_t, pt, true, bi + "_attn_text");
             }
+            dbg((bi + "_lat").c_str(), lat); dbg((bi + "_clip").c_str(), clip); dbg((bi + "_text").c_str(), text);
             if (i == 0) { dbg("jb0_lat", lat); dbg("jb0_clip", clip); dbg("jb0_text", text); }
         }
         dbg("after_joint", lat);
@@ -422,7 +428,9 @@ struct Ctx {
             const std::string fb = "fused_blocks." + std::to_string(i);
             Pre p = pre_attn(fb, lat, T, ext, T, true, 1.0f, false);
             auto ao = attention(p.q, p.k, p.v, T, nh, hd);
-            post_attn(fb, lat, T, ao, p, false);
+            const std::string bi = "blk" + std::to_string(n_joint + i);
+            post_attn(fb, lat, T, ao, p, false, bi + "_attn_lat");
+            dbg((bi + "_lat").c_str(), lat);
         }
         dbg("after_fused", lat);
         // final layer (:284-290)

@@ -43,6 +43,32 @@ def test_load_gguf_rejects_missing_and_non_gguf_files(tmp_path):
     assert rc == -3
 
 
+def test_load_gguf_rejects_truncated_data_without_touching_the_gpu(tmp_path):
+    """A GGUF whose header and tensor table are intact but whose data section was cut short
+    (an interrupted download or copy) is rejected as TSD_ERR_IO before any device work."""
+    hp = synth.DitHParams(hidden=128, n_head=2, depth=2, fused_depth=1, ffn=256)
+    W = synth.make_weights(hp, seed=3, wtype="bf16")
+    path = tmp_path / "dit.gguf"
+    synth.write_gguf(str(path), hp, W)
+    data = path.read_bytes()
+    h = ctypes.c_void_p()
+    for keep in (len(data) - 1, len(data) - 4096, len(data) // 2):
+        cut = tmp_path / f"cut{keep}.gguf"
+        cut.write_bytes(data[:keep])
+        rc = tsd.lib().tsd_load_gguf(str(cut).encode(), 0, ctypes.byref(h))
+        assert rc == -3, (keep, rc)
+    # a header cut inside the tensor table is reported the same way
+    short = tmp_path / "short.gguf"
+    short.write_bytes(data[:200])
+    assert tsd.lib().tsd_load_gguf(str(short).encode(), 0, ctypes.byref(h)) == -3
+
+
+def test_wait_limit_range_is_checked_without_touching_the_gpu():
+    L = tsd.lib()
+    assert L.tsd_set_wait_limit(0, 10) == -1                 # below 1 ms
+    assert L.tsd_set_wait_limit(0, 120 * 10**9) == -1        # above 60 s
+
+
 def test_null_arguments_are_rejected_without_touching_the_gpu():
     L = tsd.lib()
     assert L.tsd_model_get_hparams(None, None) == -1

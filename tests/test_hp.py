@@ -7,6 +7,7 @@ results to the single-GPU path, for a width whose per-rank Q/K/V sections need p
 import os
 import socket
 import sys
+import time
 
 import numpy as np
 import pytest
@@ -140,3 +141,68 @@ def test_head_parallel_two_gpus_equals_single_gpu():
             assert np.array_equal(res[r][f"flow{k}b"], ref), (k, r)
     for r in range(world):
         assert np.array_equal(res[r]["latent"], res[0]["ref_latent"])
+
+
+def _hp_skip_worker(rank, world, port, q):
+    """Both ranks set up head-parallel mode; rank 1 then skips the forward (it stays alive with
+    nothing in flight). Rank 0's forward pushes its rows and waits for rank 1's, which never
+    come: its bounded wait runs out and the forward returns TSD_ERR_DEVICE."""
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    out = {}
+    try:
+        hp = synth.DitHParams(**HP)
+        W = synth.make_weights(hp, seed=1234, wtype="bf16")
+        m = tsd.DitModel.from_weights(hp, W, device=rank)
+        dp.head_parallel(m, rank, world, arena_bytes=256 << 20)
+        tsd.set_wait_limit(rank, 200_000_000)      # 200 ms
+        items = synth.make_inputs(hp, seed=4242, batch=2, **SHAPES[0])
+        if rank == 0:
+            t0 = time.perf_counter()
+            try:
+                m.forward(items)
+                out["rc"] = 0
+            except tsd.TsdError as e:
+                out["rc"] = e.rc
+            out["seconds"] = time.perf_counter() - t0
+        dist.barrier()                            # rank 0's forward has returned; nothing is in flight
+        tsd.set_wait_limit(rank, 2_000_000_000)
+        m.close()
+        if rank == 0:                             # the GPU still works: a plain single-GPU forward
+            ref = tsd.DitModel.from_weights(hp, W, device=0)
+            out["ok_after"] = bool(np.isfinite(ref.forward(items)).all())
+            ref.close()
+        q.put((rank, out, None))
+    except Exception as e:  # report to the parent instead of leaving it waiting
+        q.put((rank, None, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_head_parallel_missing_peer_ends_in_device_error():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs of one node")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_hp_skip_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, out, err = q.get(timeout=600)
+        assert err is None, f"rank {r}: {err}"
+        res[r] = out
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert res[0]["rc"] == -5                      # TSD_ERR_DEVICE
+    assert res[0]["seconds"] < 30
+    assert res[0]["ok_after"]

@@ -42,9 +42,10 @@ constexpr float kLazyMax = 8.0f;                     // log2 of the largest P ke
 struct AttnArgs {
     int S, nh;
     long long ldo;
-    __nv_bfloat16 * out;
+    void * out;            // bf16, or f32 when out_f32
     int * err;
     float scale_log2;
+    int out_f32;
 };
 
 __device__ __forceinline__ void soft_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
@@ -103,10 +104,10 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             }
             if (*s_abort) {
                 const unsigned long long t0 = globaltimer();
-                while (!mbar_try_wait(q_full, 0) && globaltimer() - t0 < kWaitNs) {}
+                while (!mbar_try_wait(q_full, 0) && globaltimer() - t0 < wait_ns()) {}
                 for (int i = (issued > kStages ? issued - kStages : 0); i < issued; ++i) {
                     const unsigned long long t1 = globaltimer();
-                    while (!mbar_try_wait(&kv_full[i % kStages], (i / kStages) & 1) && globaltimer() - t1 < kWaitNs) {}
+                    while (!mbar_try_wait(&kv_full[i % kStages], (i / kStages) & 1) && globaltimer() - t1 < wait_ns()) {}
                 }
             }
         }
@@ -247,8 +248,14 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             const int b = bh / a.nh, h = bh % a.nh;
             float o[32];
             tmem_ld32(lane_base + kColO + half * 32, o);
-            if (t < S) {
-                __nv_bfloat16 * dst = a.out + ((long long)b * S + t) * a.ldo + h * kHD + half * 32;
+            if (t < S && a.out_f32) {
+                float * dst = reinterpret_cast<float *>(a.out) + ((long long)b * S + t) * a.ldo + h * kHD + half * 32;
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    *reinterpret_cast<float4 *>(dst + e * 4) =
+                        make_float4(o[e * 4] * inv, o[e * 4 + 1] * inv, o[e * 4 + 2] * inv, o[e * 4 + 3] * inv);
+            } else if (t < S) {
+                __nv_bfloat16 * dst = reinterpret_cast<__nv_bfloat16 *>(a.out) + ((long long)b * S + t) * a.ldo + h * kHD + half * 32;
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     uint4 u;
@@ -271,8 +278,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 }  // namespace
 
 bool attn_plan(AttnLaunch & L, const void * Q, const void * K, const void * V, int B, int nh, int S, void * out,
-               long long ldo, int * err) {
-    if (S < 1 || B < 1 || nh < 1 || (ldo % 8)) return false;
+               long long ldo, int * err, bool out_f32) {
+    if (S < 1 || B < 1 || nh < 1 || (ldo % 8) || (reinterpret_cast<uintptr_t>(out) & 15)) return false;
+    L.out_f32 = out_f32;
     const uint64_t rows = S, heads = (uint64_t)B * nh;
     bool ok = make_tmap_3d(&L.tmQ, Q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, kHD, rows, heads, kHD * 2, rows * kHD * 2, kHD, kQT, 1) &&
               make_tmap_3d(&L.tmK, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, kHD, rows, heads, kHD * 2, rows * kHD * 2, kHD, kKV, 1) &&
@@ -289,7 +297,7 @@ cudaError_t attn_launch(const AttnLaunch & L, cudaStream_t st) {
         attr = true;
     }
     AttnArgs a;
-    a.S = L.S; a.nh = L.nh; a.ldo = L.ldo; a.out = reinterpret_cast<__nv_bfloat16 *>(L.out); a.err = L.err;
+    a.S = L.S; a.nh = L.nh; a.ldo = L.ldo; a.out = L.out; a.err = L.err; a.out_f32 = L.out_f32 ? 1 : 0;
     a.scale_log2 = L.scale * 1.4426950408889634f;
     dim3 grid((L.S + kQT - 1) / kQT, L.B * L.nh);
     launch_pdl(attn_tc_kernel, dim3(grid), dim3(kThreads), kSmemBytes, st, L.tmQ, L.tmK, L.tmV, a);

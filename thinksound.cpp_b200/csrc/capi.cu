@@ -7,6 +7,18 @@
 
 using namespace tsd;
 
+namespace tsd {
+// Setters of every translation unit's copy of the device wait limit (common.cuh).
+static std::vector<WaitLimitSetter> & wait_limit_setters() {
+    static std::vector<WaitLimitSetter> v;
+    return v;
+}
+int register_wait_limit_setter(WaitLimitSetter fn) {
+    wait_limit_setters().push_back(fn);
+    return 1;
+}
+}  // namespace tsd
+
 struct tsd_model {
     Model * m = nullptr;
     cudaStream_t stream = nullptr;
@@ -89,6 +101,19 @@ std::vector<float> host_f32(const RawTensor & t) {
 extern "C" {
 
 const char * tsd_version(void) { return "tsd_b200 0.1 (sm_100a)"; }
+
+int tsd_set_wait_limit(int device, uint64_t ns) {
+    if (ns < 1000000ull || ns > 60000000000ull) return TSD_ERR_ARG;
+    int prev = 0;
+    TSD_CUDA_TRY(cudaGetDevice(&prev));
+    TSD_CUDA_TRY(cudaSetDevice(device));
+    cudaError_t e = cudaSuccess;
+    for (WaitLimitSetter fn : wait_limit_setters())
+        if (e == cudaSuccess) e = fn((unsigned long long)ns);
+    cudaSetDevice(prev);
+    TSD_CUDA_TRY(e);
+    return TSD_OK;
+}
 
 int tsd_device_count(void) {
     int n = 0;
@@ -207,6 +232,27 @@ int tsd_forward_batched(tsd_model * h, int B, const float * latent, int64_t T, c
     rc = stage_inputs(m, *p, Inputs{latent, t, clip_f, sync_f, text_f, t5, global_text}, h->stream);
     if (rc) return rc;
     rc = plan_run(m, *p, h->stream, dbg, ud);
+    if (rc) return rc;
+    TSD_CUDA_TRY(cudaMemcpyAsync(flow_out, p->flow, (size_t)B * T * m.L * 4, cudaMemcpyDefault, h->stream));
+    return check_device(m, h->stream);
+}
+
+int tsd_forward_inject(tsd_model * h, int B, const float * latent, int64_t T, const float * t, const float * clip_f,
+                       int64_t clip_S, const float * sync_f, int64_t sync_S, const float * text_f, int64_t text_S,
+                       const float * t5, int64_t t5_S, const float * global_text, float * flow_out, tsd_dbg_fn dbg,
+                       tsd_inject_fn inject, void * ud) {
+    if (!h || !latent || !t || !clip_f || !sync_f || (text_S && !text_f) || (t5_S && !t5) || !global_text || !flow_out)
+        return TSD_ERR_ARG;
+    if (!shape_ok(B, T, clip_S, sync_S, text_S, t5_S)) return TSD_ERR_ARG;
+    if (h->m->hpar.connected) return TSD_ERR_UNSUPPORTED;   // head-parallel peers run graphs in lock step
+    Model & m = *h->m;
+    TSD_CUDA_TRY(cudaSetDevice(m.device));
+    Plan * p = nullptr;
+    int rc = get_plan(m, Shape{B, (int)T, (int)clip_S, (int)sync_S, (int)text_S, (int)t5_S}, &p);
+    if (rc) return rc;
+    rc = stage_inputs(m, *p, Inputs{latent, t, clip_f, sync_f, text_f, t5, global_text}, h->stream);
+    if (rc) return rc;
+    rc = plan_run(m, *p, h->stream, dbg, ud, false, inject);
     if (rc) return rc;
     TSD_CUDA_TRY(cudaMemcpyAsync(flow_out, p->flow, (size_t)B * T * m.L * 4, cudaMemcpyDefault, h->stream));
     return check_device(m, h->stream);
@@ -402,6 +448,29 @@ int tsd_op_gemm(const void * W, int M, int K_in, int taps, int pad, const void *
     return TSD_OK;
 }
 
+int tsd_op_gemm_plan(int M, int K_in, int taps, int nbatch, int S, int max_splits, int64_t ws_floats, int n_counters,
+                     int64_t out[5]) {
+    if (!out) return TSD_ERR_ARG;
+    int dev = 0, sms = 148;
+    TSD_CUDA_TRY(cudaGetDevice(&dev));
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // the tensor maps are encoded but never used: any 256-byte-aligned address serves
+    const void * dummy = reinterpret_cast<const void *>(uintptr_t(1) << 20);
+    GemmLaunch L;
+    if (!gemm_plan(L, dummy, M, K_in, taps, 0, 0, dummy, nbatch, S, K_in, (long long)S * K_in, sms, max_splits,
+                   ws_floats, n_counters, true))
+        return TSD_ERR_ARG;
+    out[0] = L.p.BN; out[1] = L.p.splits; out[2] = L.p.pair; out[3] = L.p.csplit; out[4] = gemm_ws_floats(L);
+    return TSD_OK;
+}
+
+int tsd_op_peer_wait(const uint32_t * counters, const uint32_t * epoch, int rank, int world, uint32_t ctas, int * err,
+                     void * stream) {
+    if (!counters || !epoch || world < 1 || world > kMaxHpRanks || rank < 0 || rank >= world) return TSD_ERR_ARG;
+    TSD_CUDA_TRY(hp_wait_launch(counters, epoch, rank, world, ctas, err, (cudaStream_t)stream));
+    return TSD_OK;
+}
+
 int tsd_op_gemv(const void * W, int ggml_type, const void * W2, int M, int K, const float * x, int64_t ldx, int N,
                 const float * bias, int act, int round_bf16, void * y, int y_bf16, int64_t ldy, void * stream) {
     if (!W || !x || !y) return TSD_ERR_ARG;
@@ -416,6 +485,15 @@ int tsd_op_attention(const void * Q, const void * K, const void * V, int B, int 
     if (!Q || !K || !V || !out) return TSD_ERR_ARG;
     AttnLaunch L;
     if (!attn_plan(L, Q, K, V, B, nh, S, out, ldo, err)) return TSD_ERR_ARG;
+    TSD_CUDA_TRY(attn_launch(L, (cudaStream_t)stream));
+    return TSD_OK;
+}
+
+int tsd_op_attention_f32(const void * Q, const void * K, const void * V, int B, int nh, int S, float * out, int64_t ldo,
+                         int * err, void * stream) {
+    if (!Q || !K || !V || !out) return TSD_ERR_ARG;
+    AttnLaunch L;
+    if (!attn_plan(L, Q, K, V, B, nh, S, out, ldo, err, true)) return TSD_ERR_ARG;
     TSD_CUDA_TRY(attn_launch(L, (cudaStream_t)stream));
     return TSD_OK;
 }

@@ -11,6 +11,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include "kernels.h"
+
 namespace tsd {
 
 // ---- error word written by device code ----
@@ -25,8 +27,16 @@ enum DevErr : int {
     DEV_TIMEOUT_HP = 7,       // head-parallel: a peer rank's attention rows did not arrive in time
 };
 
-// 2 s: no healthy wait in these kernels comes anywhere near it.
-constexpr unsigned long long kWaitNs = 2000000000ull;
+// Deadline of every bounded wait, in ns: 2 s by default (no healthy wait in these kernels comes
+// anywhere near it), changed per device at run time by tsd_set_wait_limit. The library is built
+// without relocatable device code, so every translation unit that includes this header holds its
+// own copy of the variable; each copy registers a host-side setter (capi.cu keeps the list).
+namespace {
+__device__ unsigned long long g_wait_ns = 2000000000ull;
+cudaError_t set_wait_limit_here(unsigned long long ns) { return cudaMemcpyToSymbol(g_wait_ns, &ns, sizeof(ns)); }
+[[maybe_unused]] const int g_wait_limit_registered = register_wait_limit_setter(&set_wait_limit_here);
+}  // namespace
+__device__ __forceinline__ unsigned long long wait_ns() { return g_wait_ns; }
 
 __device__ __forceinline__ unsigned long long globaltimer() {
     unsigned long long t;
@@ -72,7 +82,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity, volat
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 63) == 0) {
             if (abort && *abort) return false;
-            if (globaltimer() - t0 > kWaitNs) {
+            if (globaltimer() - t0 > wait_ns()) {
                 if (abort) *abort = 1;
                 if (err) atomicCAS(err, 0, code);
                 return false;
@@ -199,7 +209,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t * bar, uint32_t parit
             : "r"(smem_u32(bar)), "r"(parity)
             : "memory");
         if (ok) return true;
-        if ((it & 63) == 63 && globaltimer() - t0 > kWaitNs) {
+        if ((it & 63) == 63 && globaltimer() - t0 > wait_ns()) {
             if (err) atomicCAS(err, 0, code);
             return false;
         }

@@ -112,9 +112,12 @@ struct Builder {
         op([=](cudaStream_t st) { return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, st); }, OP_COPY, 0,
            2.0 * bytes);
     }
-    void snap(const char * name, const void * ptr, long long n, int kind = 0, int B = 0, int nh = 0, int S = 0) {
-        if (!P.ops.empty()) P.ops.back().snaps.push_back(Snap{name, ptr, n, kind, B, nh, S});
+    void snap(const std::string & name, const void * ptr, long long n, int kind = 0, int B = 0, int nh = 0, int S = 0,
+              bool inject = false) {
+        if (!P.ops.empty()) P.ops.back().snaps.push_back(Snap{name, ptr, n, kind, B, nh, S, inject});
     }
+    // A residual stream at a block boundary: reported, and offered for teacher forcing.
+    void inject_point(const std::string & name, float * ptr, long long n) { snap(name, ptr, n, 0, 0, 0, 0, true); }
 
     // GEMM over activations X [nbatch][S][K_in] (row stride xrs, batch stride xbs, elements).
     void gemm(const GW & w, const void * X, int nbatch, int S, long long xrs, long long xbs, int mode, int act,
@@ -487,8 +490,11 @@ struct Builder {
         // runs on lane s (its own CUDA stream in the captured graph), joined before the
         // attention and forked after it.
         mark(1);
+        const char * const sname[3] = {"lat", "clip", "text"};
         for (int i = 0; i < n_joint; ++i) {
             const auto & blk = m.joint[i];
+            for (int s = 0; s < 3; ++s)
+                inject_point("blk" + std::to_string(i) + "_in_" + sname[s], xs[s], (long long)B * Ss[s] * H);
             const float * mods[3];
             long long lds[3], css[3];
             for (int s = 0; s < 3; ++s) {
@@ -540,12 +546,14 @@ struct Builder {
                 const int gdiv = (s == 0) ? 1 : S;
                 gemm(w.l1, aoj + (long long)soff[s] * H, B, S, H, (long long)Sj * H, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0,
                      xs[s], H, mod + 2 * cs, ld, gdiv);
+                snap("blk" + std::to_string(i) + "_attn_" + sname[s], xs[s], (long long)B * S * H);
                 op([=](cudaStream_t st) { return ln_modulate(xs[s], B * S, H, mod + 3 * cs, mod + 4 * cs, ld, s == 0, S, xn, st); });
                 gemm(w.w13, xn, B, S, H, (long long)S * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 1);
                 gemm(w.w2, hbuf, B, S, F, (long long)S * F, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, xs[s], H, mod + 5 * cs,
                      ld, gdiv);
             }
             lane = 0;
+            for (int s = 0; s < 3; ++s) snap("blk" + std::to_string(i) + "_" + sname[s], xs[s], (long long)B * Ss[s] * H);
             if (i == 0) {
                 snap("jb0_lat", x_lat, (long long)B * T * H);
                 snap("jb0_clip", x_clip, (long long)B * cS * H);
@@ -562,18 +570,23 @@ struct Builder {
             tag = "f" + std::to_string(fi++);
             const float * mod = mod_lat + (w.ada_off / H) * BTH;
             const long long ld = H, cs = BTH;
+            const std::string bi = "blk" + std::to_string(n_joint + fidx);
+            inject_point(bi + "_in_lat", x_lat, (long long)B * T * H);
             op([=](cudaStream_t st) { return ln_modulate(x_lat, B * T, H, mod, mod + cs, ld, 1, T, xn, st); });
             gemm_qkv(w, hpm ? &m.hpar.fused_qkv[fidx] : nullptr, xn, B, T, rope_lat, Qb, Kb, Vb, T, 0);
             __nv_bfloat16 * const aof = attention(Qb, Kb, Vb, B, T, ao, err);
             if (rc) return;
             gemm(w.l1, aof, B, T, H, (long long)T * H, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, x_lat, H, mod + 2 * cs, ld, 1);
+            snap(bi + "_attn_lat", x_lat, (long long)B * T * H);
             op([=](cudaStream_t st) { return ln_modulate(x_lat, B * T, H, mod + 3 * cs, mod + 4 * cs, ld, 1, T, xn, st); });
             gemm(w.w13, xn, B, T, H, (long long)T * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 1);
             gemm(w.w2, hbuf, B, T, F, (long long)T * F, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, x_lat, H, mod + 5 * cs, ld, 1);
+            snap(bi + "_lat", x_lat, (long long)B * T * H);
         }
         snap("after_fused", x_lat, (long long)B * T * H);
         // ---- final layer (mmdit.cpp:284-290) ----
         tag = "final";
+        inject_point("final_in_lat", x_lat, (long long)B * T * H);
         const float * fmod = mod_lat + (m.final_ada_off / H) * BTH;
         op([=](cudaStream_t st) { return ln_modulate(x_lat, B * T, H, fmod, fmod + BTH, H, 1, T, xn, st); });
         gemm(m.fconv, xn, B, T, H, (long long)T * H, EPI_STORE, ACT_NONE, P.flow, 0, L);
@@ -640,17 +653,20 @@ int plan_profile(Model & m, Plan & p, cudaStream_t st, std::vector<float> & ms) 
     return rc;
 }
 
-int plan_run(Model & m, Plan & p, cudaStream_t st, tsd_dbg_fn dbg, void * ud, bool reuse_cond) {
+int plan_run(Model & m, Plan & p, cudaStream_t st, tsd_dbg_fn dbg, void * ud, bool reuse_cond, tsd_inject_fn inject) {
     (void)m;
-    if (dbg) {
+    if (dbg || inject) {
         std::vector<float> h;
         for (const Op & o : p.ops) {
             if (o.fn) TSD_CUDA_TRY(o.fn(st));
             if (!o.snaps.empty()) {
                 TSD_CUDA_TRY(cudaStreamSynchronize(st));
                 for (const Snap & s : o.snaps) {
+                    if (!dbg && !s.inject) continue;
                     to_host_f32(s, h);
-                    dbg(ud, s.name.c_str(), h.data(), (int64_t)h.size());
+                    if (dbg) dbg(ud, s.name.c_str(), h.data(), (int64_t)h.size());
+                    if (s.inject && inject && s.kind == 0 && inject(ud, s.name.c_str(), h.data(), (int64_t)h.size()))
+                        TSD_CUDA_TRY(cudaMemcpy(const_cast<void *>(s.ptr), h.data(), (size_t)s.n * 4, cudaMemcpyHostToDevice));
                 }
             }
         }

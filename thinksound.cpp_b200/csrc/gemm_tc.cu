@@ -766,7 +766,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const unsigned long long t_start = globaltimer();
             for (int i = (issued > nst ? issued - nst : 0); i < issued; ++i) {
                 uint64_t * bar = (p.a_q8 && do_a) ? &rfull[i % nst] : &full[i % nst];
-                while (!mbar_try_wait(bar, (i / nst) & 1) && globaltimer() - t_start < kWaitNs) {}
+                while (!mbar_try_wait(bar, (i / nst) & 1) && globaltimer() - t_start < wait_ns()) {}
             }
         }
     };
@@ -1090,7 +1090,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // loads issued but not consumed (a wait gave up): let them land before the CTA exits
             for (int g = gs; g < gl; ++g) {
                 const unsigned long long t_start = globaltimer();
-                while (!mbar_try_wait(&ebar[g & 1], (g >> 1) & 1) && globaltimer() - t_start < kWaitNs) {}
+                while (!mbar_try_wait(&ebar[g & 1], (g >> 1) & 1) && globaltimer() - t_start < wait_ns()) {}
             }
             bulk_wait<0>();                           // TMA stores complete before exit
         }
@@ -1219,6 +1219,12 @@ static bool pairs_enabled() {       // read per plan: tests compare both forms i
     const char * e = getenv("TSD_NO_PAIR");
     return !(e && *e && *e != '0');
 }
+// Split-K inside a thread-block cluster (no scratch) unless TSD_NO_CLUSTER_SPLIT is set to a
+// non-zero value (tests: exercises the split-K that reduces through caller scratch). Read per plan.
+static bool cluster_split_enabled() {
+    const char * e = getenv("TSD_NO_CLUSTER_SPLIT");
+    return !(e && *e && *e != '0');
+}
 // Every feasible (BN, splits, pair), cheapest first by the model.
 static std::vector<TileChoice> tile_choices(int S, int nbatch, int mblocks, int nkb, int num_sms, int max_splits,
                                             long long ws_floats, int n_counters, bool allow_cluster, bool allow_pair,
@@ -1235,7 +1241,7 @@ static std::vector<TileChoice> tile_choices(int S, int nbatch, int mblocks, int 
             for (int sp = 1; sp <= std::min(8, std::max(1, max_splits)); ++sp) {   // reducers sum <= 8 partials
                 if (sp > 1 && nkb / sp < 4) break;
                 const long long ctas = otiles * sp * cpt;
-                bool cluster = allow_cluster && sp > 1 && ctas <= num_sms && cpt * sp <= 8;
+                bool cluster = allow_cluster && cluster_split_enabled() && sp > 1 && ctas <= num_sms && cpt * sp <= 8;
                 if (cluster) {   // partial tile + receive slots fit the operand stages; clusters co-resident
                     const int rows_max = 16 * (((bn >> 4) + sp - 1) / sp);
                     const int mac = max_active_clusters(cpt * sp);
@@ -1357,7 +1363,7 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
     {
         const int rows_max = 16 * (((p.BN >> 4) + p.splits - 1) / p.splits);
         const int mac = p.splits > 1 && cpt * p.splits <= 8 ? max_active_clusters(cpt * p.splits) : 0;
-        p.csplit = allow_cluster && p.splits > 1 && tiles <= num_sms && mac > 0 &&
+        p.csplit = allow_cluster && cluster_split_enabled() && p.splits > 1 && tiles <= num_sms && mac > 0 &&
                    (long long)(p.mblocks / cpt) * nbatch * p.n_tiles <= mac &&
                    (long long)p.BN * 512 + (long long)(p.splits - 1) * rows_max * 512 <= (long long)kStageArea;
     }

@@ -56,7 +56,7 @@ __global__ void hp_wait_kernel(const unsigned * counters, const unsigned * epoch
         for (;;) {
             asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(counters + r) : "memory");
             if ((int)(v - want) >= 0) break;
-            if (globaltimer() - t0 > kWaitNs) {
+            if (globaltimer() - t0 > wait_ns()) {
                 if (err) atomicExch(err, DEV_TIMEOUT_HP);
                 break;
             }

@@ -8,6 +8,11 @@
 
 namespace tsd {
 
+// Host-side setter of one translation unit's copy of the device wait limit (common.cuh);
+// every copy registers itself at load time (list kept in capi.cu, used by tsd_set_wait_limit).
+using WaitLimitSetter = cudaError_t (*)(unsigned long long);
+int register_wait_limit_setter(WaitLimitSetter fn);
+
 // ---------------------------------------------------------------------------------------------
 // tcgen05 GEMM:  out[b][t][m] = epi( sum_tap sum_k  X[b][t + tap - pad][k] * W[m][tap*K_in + k] )
 //   W: bf16, [M rows][taps*K_in] (tap-major columns), via a 2-D tensor map (box 64 x 128*numA).
@@ -142,9 +147,10 @@ struct AttnLaunch {
     void * out;
     int * err;
     float scale;
+    bool out_f32 = false;   // f32 output (parity tests) instead of bf16
 };
 bool attn_plan(AttnLaunch & L, const void * Q, const void * K, const void * V, int B, int nh, int S,
-               void * out, long long ldo, int * err);
+               void * out, long long ldo, int * err, bool out_f32 = false);
 cudaError_t attn_launch(const AttnLaunch & L, cudaStream_t st);
 
 // ---------------------------------------------------------------------------------------------

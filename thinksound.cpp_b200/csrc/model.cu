@@ -625,6 +625,27 @@ int model_load_gguf(const char * path, int device, Model ** out) {
     hp.rope_theta = getf("dit.rope_theta", 10000.f);
     hp.t_max_period = getf("dit.t_embed_max_period", 1.f);
 
+    // every tensor's type and byte range are checked against the file before any device work,
+    // so a truncated or inconsistent file fails as TSD_ERR_IO without touching the GPU (the
+    // reference's loader fails on its first short read, ts_model.cpp:33-35)
+    r.f.clear();
+    r.f.seekg(0, std::ios::end);
+    const uint64_t file_size = (uint64_t)r.f.tellg();
+    for (const TI & ti : tis) {
+        for (int d = 0; d < 4; ++d)
+            if (ti.ne[d] < 1 || ti.ne[d] > (int64_t(1) << 40)) {
+                fprintf(stderr, "tsd: tensor '%s' has a bad shape in '%s'\n", ti.name.c_str(), path);
+                return TSD_ERR_IO;
+            }
+        const size_t nb = ggml_nbytes(ti.type, ti.ne[0] * ti.ne[1] * ti.ne[2] * ti.ne[3]);
+        if (!nb) { fprintf(stderr, "tsd: tensor '%s' has unsupported type %d\n", ti.name.c_str(), ti.type); return TSD_ERR_UNSUPPORTED; }
+        if (ti.off > file_size || data_off + ti.off + nb > file_size) {
+            fprintf(stderr, "tsd: truncated GGUF '%s': tensor '%s' needs bytes up to %llu of a %llu-byte file\n", path,
+                    ti.name.c_str(), (unsigned long long)(data_off + ti.off + nb), (unsigned long long)file_size);
+            return TSD_ERR_IO;
+        }
+    }
+
     std::unique_ptr<Model> m(new Model());
     m->hp = hp;
     m->device = device;

@@ -118,6 +118,7 @@ struct Snap {
     long long n;
     int kind;          // 0 f32, 1 bf16, 2 fp16 head-major [B][nh][S][64] (S = rows) -> [B][S][H]
     int B, nh, S;
+    bool inject = false;   // teacher forcing: offered to the inject callback, which may replace it (f32 only)
 };
 enum OpKind : int { OP_GEMM = 0, OP_GEMV = 1, OP_ATTN = 2, OP_ELEM = 3, OP_COPY = 4 };
 struct Op {
@@ -185,7 +186,10 @@ cudaError_t hp_wait_launch(const unsigned * counters, const unsigned * epoch, in
 // Enqueue the forward (inputs already in the plan's buffers). reuse_cond: the conditioning
 // inputs (clip_in, sync_in, text_in, t5_in, gtext_in) are unchanged since the last full run of
 // this plan, whose conditioning-only results are reused instead of recomputed.
-int plan_run(Model & m, Plan & p, cudaStream_t st, tsd_dbg_fn dbg, void * ud, bool reuse_cond = false);
+// inject (op-by-op runs only): offered the residual streams at block boundaries (Snap::inject);
+// a non-zero return writes the callback's data back before the next op.
+int plan_run(Model & m, Plan & p, cudaStream_t st, tsd_dbg_fn dbg, void * ud, bool reuse_cond = false,
+             tsd_inject_fn inject = nullptr);
 // Run the forward op by op with CUDA events around each op; per-op milliseconds.
 int plan_profile(Model & m, Plan & p, cudaStream_t st, std::vector<float> & ms);
 

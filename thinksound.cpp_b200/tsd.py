@@ -30,7 +30,8 @@ EXPORTS = [
     "tsd_forward_device", "tsd_sync_check", "tsd_sample", "tsd_sample_batched", "tsd_version",
     "tsd_device_count", "tsd_op_gemm", "tsd_op_gemv", "tsd_op_attention", "tsd_op_ln_modulate",
     "tsd_op_qk_norm_rope", "tsd_forward_profile", "tsd_plan_op_label", "tsd_op_gemm_static",
-    "tsd_hp_layout", "tsd_hp_init", "tsd_hp_connect",
+    "tsd_hp_layout", "tsd_hp_init", "tsd_hp_connect", "tsd_op_gemm_plan",
+    "tsd_set_wait_limit", "tsd_op_peer_wait", "tsd_op_attention_f32", "tsd_forward_inject",
 ]
 
 
@@ -47,6 +48,8 @@ class HParams(ctypes.Structure):
 
 
 DBG_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_float), ctypes.c_int64)
+INJECT_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_float),
+                             ctypes.c_int64)
 
 _lib = None
 
@@ -81,7 +84,12 @@ def lib() -> ctypes.CDLL:
         "tsd_op_gemm_static": [vp, i32, i32, i32, i32, vp, i32, i32, i64, i64, i32, i32, vp, i32, vp, i32, i64, vp,
                                i64, vp, i64, i32, i32, vp, vp],
         "tsd_op_gemv": [vp, i32, vp, i32, i32, vp, i64, i32, vp, i32, i32, vp, i32, i64, vp],
+        "tsd_op_gemm_plan": [i32, i32, i32, i32, i32, i32, i64, i32, ctypes.POINTER(i64)],
+        "tsd_set_wait_limit": [i32, ctypes.c_uint64],
+        "tsd_op_peer_wait": [vp, vp, i32, i32, ctypes.c_uint32, vp, vp],
         "tsd_op_attention": [vp, vp, vp, i32, i32, i32, vp, i64, vp, vp],
+        "tsd_op_attention_f32": [vp, vp, vp, i32, i32, i32, vp, i64, vp, vp],
+        "tsd_forward_inject": [vp, i32, fp, i64, fp, fp, i64, fp, i64, fp, i64, fp, i64, fp, fp, DBG_FN, INJECT_FN, vp],
         "tsd_hp_layout": [i32, i32, i32, i32, ctypes.POINTER(i32)],
         "tsd_hp_init": [vp, i32, i32, ctypes.c_size_t, vp],
         "tsd_hp_connect": [vp, vp],
@@ -221,6 +229,36 @@ class DitModel:
         check("tsd_forward_batched", rc)
         return (out, store) if dbg else out
 
+    def forward_inject(self, items: Sequence, inject: Dict[str, np.ndarray]):
+        """Teacher-forced forward (tsd_forward_inject): `inject` maps boundary names
+        ("blk<i>_in_lat", ..., "final_in_lat") to [B][S][hidden] f32 arrays that replace the
+        residual stream before that block. Returns (flow, stages) like forward(dbg=True)."""
+        lat = _stack(items, "latent")
+        B, _, T = lat.shape
+        t = np.asarray([x.t for x in items], np.float32)
+        clip, sync, text, t5, gt = (_stack(items, a) for a in ("clip_f", "sync_f", "text_f", "t5", "gtext"))
+        out = np.zeros((B, T, self.latent_dim), np.float32)
+        store: Dict[str, np.ndarray] = {}
+
+        def cb(_ud, name, ptr, n):
+            store[name.decode()] = np.ctypeslib.as_array(ptr, shape=(n,)).copy()
+
+        def inj(_ud, name, ptr, n):
+            v = inject.get(name.decode())
+            if v is None:
+                return 0
+            v = np.ascontiguousarray(v, np.float32).reshape(-1)
+            assert v.size == n, (name, v.size, n)
+            np.ctypeslib.as_array(ptr, shape=(n,))[:] = v
+            return 1
+
+        cbf, injf = DBG_FN(cb), INJECT_FN(inj)
+        rc = lib().tsd_forward_inject(self.h, B, _fp(lat), T, _fp(t), _fp(clip), clip.shape[1], _fp(sync),
+                                      sync.shape[1], _fp(text), text.shape[1], _fp(t5), t5.shape[1], _fp(gt),
+                                      _fp(out), cbf, injf, None)
+        check("tsd_forward_inject", rc)
+        return out, store
+
     def forward_host(self, B: int, T: int, clip_S: int, sync_S: int, text_S: int, t5_S: int,
                      ptrs: Dict[str, int]) -> None:
         """tsd_forward_batched on caller-owned host buffers given as raw addresses (e.g. pinned
@@ -301,6 +339,25 @@ def op_gemm_static(W, M, K_in, taps, pad, X, nbatch, S, x_row_stride, x_batch_st
     check("tsd_op_gemm_static", rc)
 
 
+def set_wait_limit(device: int, ns: int) -> None:
+    """Deadline of every bounded device-side wait on `device` (default 2 s)."""
+    check("tsd_set_wait_limit", lib().tsd_set_wait_limit(device, ns))
+
+
+def op_peer_wait(counters, epoch, rank, world, ctas, err=None, stream=0):
+    check("tsd_op_peer_wait", lib().tsd_op_peer_wait(_ptr(counters), _ptr(epoch), rank, world, ctas, _ptr(err), stream))
+
+
+GEMM_STATIC_WS_FLOATS, GEMM_STATIC_COUNTERS = 2097152, 8192   # include/tsd_ops.h
+
+
+def op_gemm_plan(M, K_in, taps, nbatch, S, max_splits=8, ws_floats=0, n_counters=0):
+    """The tiling tsd_op_gemm chooses for a shape: dict(BN, splits, pair, csplit, ws_floats)."""
+    out = (ctypes.c_int64 * 5)()
+    check("tsd_op_gemm_plan", lib().tsd_op_gemm_plan(M, K_in, taps, nbatch, S, max_splits, ws_floats, n_counters, out))
+    return dict(BN=int(out[0]), splits=int(out[1]), pair=int(out[2]), csplit=int(out[3]), ws_floats=int(out[4]))
+
+
 def op_gemv(W, ggml_type, W2, M, K, x, ldx, N, bias, act, round_bf16, y, y_bf16, ldy, stream=0):
     rc = lib().tsd_op_gemv(_ptr(W), ggml_type, _ptr(W2), M, K, _ptr(x), ldx, N, _ptr(bias), act, round_bf16, _ptr(y),
                            y_bf16, ldy, stream)
@@ -309,6 +366,11 @@ def op_gemv(W, ggml_type, W2, M, K, x, ldx, N, bias, act, round_bf16, y, y_bf16,
 
 def op_attention(Q, K, V, B, nh, S, out, ldo, err=None, stream=0):
     check("tsd_op_attention", lib().tsd_op_attention(_ptr(Q), _ptr(K), _ptr(V), B, nh, S, _ptr(out), ldo, _ptr(err), stream))
+
+
+def op_attention_f32(Q, K, V, B, nh, S, out, ldo, err=None, stream=0):
+    check("tsd_op_attention_f32",
+          lib().tsd_op_attention_f32(_ptr(Q), _ptr(K), _ptr(V), B, nh, S, _ptr(out), ldo, _ptr(err), stream))
 
 
 def op_ln_modulate(x, rows, H, shift, scale, ld_mod, per_token, rows_per_item, y, stream=0):
