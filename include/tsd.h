@@ -94,7 +94,10 @@ TSD_API int tsd_forward_batched(tsd_model * m, int B, const float * latent, int6
  * half of each block ("blk<i>_attn_lat" ...). Before block i runs, inject(ud, name, data, n) is
  * offered each residual stream the block reads ("blk<i>_in_lat", "blk<i>_in_clip",
  * "blk<i>_in_text"; before the final layer "final_in_lat"), host f32 [B][S][hidden]; if it
- * returns non-zero, its (modified) data replace the stream. Runs op by op, without a graph. */
+ * returns non-zero, its (modified) data replace the stream; "blk<i>_mid_<stream>" is offered
+ * between a block's attention half and its FFN half. The conditioning the blocks'
+ * adaLN projections read is offered the same way ("global_c" [B][hidden], "extended_c"
+ * [B][T][hidden]). Runs op by op, without a graph. */
 typedef int (*tsd_inject_fn)(void * ud, const char * name, float * data, int64_t n);
 TSD_API int tsd_forward_inject(tsd_model * m, int B, const float * latent, int64_t T, const float * t,
                                const float * clip_f, int64_t clip_S, const float * sync_f, int64_t sync_S,

@@ -55,10 +55,11 @@ def run_pair(mode, M, K, taps, nb, S, seed=0):
 
 @pytest.mark.parametrize("mode", [tsd.EPI_STORE, tsd.EPI_GATE_RESID])
 def test_static_scratch_gemm_matches_caller_scratch_gemm(mode, monkeypatch):
-    # Long K, few tokens: the planner splits K. With the in-cluster reduction switched off the
-    # splits reduce through global scratch, which for the static entry point is its device arrays.
+    # Very long K, few tokens: the planner splits K. With the in-cluster reduction switched off
+    # the splits reduce through global scratch, which for the static entry point is its device
+    # arrays.
     monkeypatch.setenv("TSD_NO_CLUSTER_SPLIT", "1")
-    M, K, taps, nb, S = 512, 1536, 3, 2, 40
+    M, K, taps, nb, S = 512, 8192, 3, 2, 40
     plan = tsd.op_gemm_plan(M, K, taps, nb, S, 8, tsd.GEMM_STATIC_WS_FLOATS, tsd.GEMM_STATIC_COUNTERS)
     assert plan["splits"] > 1 and not plan["csplit"] and 0 < plan["ws_floats"] <= tsd.GEMM_STATIC_WS_FLOATS, plan
     ref, got = run_pair(mode, M, K, taps, nb, S)

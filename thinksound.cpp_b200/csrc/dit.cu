@@ -117,7 +117,11 @@ struct Builder {
         if (!P.ops.empty()) P.ops.back().snaps.push_back(Snap{name, ptr, n, kind, B, nh, S, inject});
     }
     // A residual stream at a block boundary: reported, and offered for teacher forcing.
-    void inject_point(const std::string & name, float * ptr, long long n) { snap(name, ptr, n, 0, 0, 0, 0, true); }
+    void inject_point(const std::string & name, float * ptr, long long n,
+                      std::function<cudaError_t(cudaStream_t)> after_inject = {}) {
+        snap(name, ptr, n, 0, 0, 0, 0, true);
+        if (!P.ops.empty()) P.ops.back().snaps.back().after_inject = std::move(after_inject);
+    }
 
     // GEMM over activations X [nbatch][S][K_in] (row stride xrs, batch stride xbs, elements).
     void gemm(const GW & w, const void * X, int nbatch, int S, long long xrs, long long xbs, int mode, int act,
@@ -459,9 +463,11 @@ struct Builder {
         snap("gcmlp", gcm, (long long)B * H);
         inv = false;
         op([=](cudaStream_t st) { return add_vec(gcm, te, B * H, gc, st); });
-        snap("global_c", gc, (long long)B * H);
+        inject_point("global_c", gc, (long long)B * H);
         op([=](cudaStream_t st) { return build_extended(sync_out, yS, gc, B, T, H, ext, sext, sgc, st); });
-        snap("extended_c", ext, (long long)B * T * H);
+        // a teacher-forced ext also replaces the adaLN GEMM's operand bf16(silu(ext)) derived from it
+        inject_point("extended_c", ext, (long long)B * T * H,
+                     [=](cudaStream_t st) { return silu_cast_bf16(ext, (long long)B * T * H, sext, st); });
         // ---- every per-token adaLN of the step in one GEMM (mmdit.cpp:209, 285); on a side lane
         // beside it, every clip / text adaLN of the step in one GEMV ----
         tag = "adaln";
@@ -547,6 +553,7 @@ struct Builder {
                 gemm(w.l1, aoj + (long long)soff[s] * H, B, S, H, (long long)Sj * H, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0,
                      xs[s], H, mod + 2 * cs, ld, gdiv);
                 snap("blk" + std::to_string(i) + "_attn_" + sname[s], xs[s], (long long)B * S * H);
+                inject_point("blk" + std::to_string(i) + "_mid_" + sname[s], xs[s], (long long)B * S * H);
                 op([=](cudaStream_t st) { return ln_modulate(xs[s], B * S, H, mod + 3 * cs, mod + 4 * cs, ld, s == 0, S, xn, st); });
                 gemm(w.w13, xn, B, S, H, (long long)S * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 1);
                 gemm(w.w2, hbuf, B, S, F, (long long)S * F, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, xs[s], H, mod + 5 * cs,
@@ -578,6 +585,7 @@ struct Builder {
             if (rc) return;
             gemm(w.l1, aof, B, T, H, (long long)T * H, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, x_lat, H, mod + 2 * cs, ld, 1);
             snap(bi + "_attn_lat", x_lat, (long long)B * T * H);
+            inject_point(bi + "_mid_lat", x_lat, (long long)B * T * H);
             op([=](cudaStream_t st) { return ln_modulate(x_lat, B * T, H, mod + 3 * cs, mod + 4 * cs, ld, 1, T, xn, st); });
             gemm(w.w13, xn, B, T, H, (long long)T * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 1);
             gemm(w.w2, hbuf, B, T, F, (long long)T * F, EPI_GATE_RESID, ACT_NONE, nullptr, 0, 0, x_lat, H, mod + 5 * cs, ld, 1);
@@ -665,8 +673,14 @@ int plan_run(Model & m, Plan & p, cudaStream_t st, tsd_dbg_fn dbg, void * ud, bo
                     if (!dbg && !s.inject) continue;
                     to_host_f32(s, h);
                     if (dbg) dbg(ud, s.name.c_str(), h.data(), (int64_t)h.size());
-                    if (s.inject && inject && s.kind == 0 && inject(ud, s.name.c_str(), h.data(), (int64_t)h.size()))
-                        TSD_CUDA_TRY(cudaMemcpy(const_cast<void *>(s.ptr), h.data(), (size_t)s.n * 4, cudaMemcpyHostToDevice));
+                    if (s.inject && inject && s.kind == 0 && inject(ud, s.name.c_str(), h.data(), (int64_t)h.size())) {
+                        // on the plan's stream and waited for: a synchronous copy from pageable memory may
+                        // return before its DMA lands and is not ordered against a non-blocking stream
+                        TSD_CUDA_TRY(cudaMemcpyAsync(const_cast<void *>(s.ptr), h.data(), (size_t)s.n * 4,
+                                                     cudaMemcpyHostToDevice, st));
+                        if (s.after_inject) TSD_CUDA_TRY(s.after_inject(st));
+                        TSD_CUDA_TRY(cudaStreamSynchronize(st));
+                    }
                 }
             }
         }

@@ -323,6 +323,18 @@ cudaError_t build_extended(const float * sync, int sync_S, const float * gc, int
     return cudaGetLastError();
 }
 
+__global__ void silu_cast_kernel(const float * __restrict__ x, long long n, __nv_bfloat16 * __restrict__ y) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = __float2bfloat16_rn(silu_f(x[i]));
+}
+
+cudaError_t silu_cast_bf16(const float * x, long long n, __nv_bfloat16 * y, cudaStream_t st) {
+    launch_pdl(silu_cast_kernel, dim3(nblk(n, 256)), dim3(256), 0, st, x, n, y);
+    return cudaGetLastError();
+}
+
 cudaError_t cast_f32_bf16(const float * x, long long n, __nv_bfloat16 * y, cudaStream_t st) {
     launch_pdl(cast_kernel, dim3(nblk(n, 256)), dim3(256), 0, st, x, n, y);
     return cudaGetLastError();

@@ -178,6 +178,8 @@ cudaError_t add_vec(const float * a, const float * b, int n, float * y, cudaStre
 cudaError_t build_extended(const float * sync, int sync_S, const float * gc, int B, int T, int H,
                            float * ext, __nv_bfloat16 * sext, float * sgc, cudaStream_t st);
 cudaError_t cast_f32_bf16(const float * x, long long n, __nv_bfloat16 * y, cudaStream_t st);
+// y = bf16(silu(x)) (the adaLN GEMM operand build_extended writes; rebuilt after a teacher-forced ext)
+cudaError_t silu_cast_bf16(const float * x, long long n, __nv_bfloat16 * y, cudaStream_t st);
 // CFG combine + Euler update on [B2][T][L] flows: pairs (cond = item 2p, uncond = 2p+1);
 // x [P][L][T] (t fastest) += dt * (u + (c - u) * cfg); optionally also store v into flow0.
 cudaError_t cfg_euler(const float * flow, int P, int T, int L, float cfg, float dt, float * x, float * flow0,

@@ -119,6 +119,7 @@ struct Snap {
     int kind;          // 0 f32, 1 bf16, 2 fp16 head-major [B][nh][S][64] (S = rows) -> [B][S][H]
     int B, nh, S;
     bool inject = false;   // teacher forcing: offered to the inject callback, which may replace it (f32 only)
+    std::function<cudaError_t(cudaStream_t)> after_inject;   // rebuilds what the op derived from it, if replaced
 };
 enum OpKind : int { OP_GEMM = 0, OP_GEMV = 1, OP_ATTN = 2, OP_ELEM = 3, OP_COPY = 4 };
 struct Op {
