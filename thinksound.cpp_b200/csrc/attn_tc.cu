@@ -6,18 +6,21 @@
 // [B*nh][S][64]; for the joint blocks S is the [latent | clip | text] concatenation
 // (:251-254), which the QKV producers write in place, so no concat/split copies exist.
 //
-// One CTA per (128-query tile, batch*head). Warp 0: TMA (Q once, K/V 128-row chunks through a
-// 3-stage ring). Warp 1: TMEM owner + MMA issuer: S_j = Q K_j^T into one of two 128-column
-// TMEM buffers, O += P_j V_j into a 64-column TMEM accumulator (V as an MN-major operand).
-// Warps 2-9: online softmax, two warps per TMEM lane quadrant: a query row (TMEM lane) is shared
-// by two threads, each taking 64 of a chunk's 128 key columns. Only the chunk max is exchanged
-// (once per chunk, through shared memory); each half keeps its own running sum under the common
-// max and the two are added at the end. P_j is written fp16 into one of two 128-B-swizzled
-// shared tiles (one 64-key sub-tile per half), so the softmax of chunk j never waits for the
-// P V MMA of chunk j-1. The running max is updated lazily: while a chunk's max stays within
-// 2^8 of it, the stale max is kept (P <= 256, exact in the final O / l), so O is rescaled in
-// TMEM (32 of its 64 columns per half) only when the max jumps; the final 1/l scale and bf16
-// token-major store out[b][t][h*64 + d] are split the same way.
+// One CTA per (128-query tile, batch*head), two CTAs per SM: each takes 256 TMEM columns (S
+// 0-127, O 128-191, P 192-255) and ~84 KB of shared memory (Q, a 2-stage K / V ring), so one
+// CTA's softmax overlaps the other's MMAs and a joint layer's 192 CTAs run as one wave.
+// Warp 0: TMA (Q once, 128-row K and V chunks). Warp 1: TMEM owner + MMA issuer: S_j = Q K_j^T
+// (M=128, N=128) into the S columns, then, once the softmax has read S_j, S_{j+1} while the
+// softmax of chunk j runs, and O += P_j V_j with P_j taken from tensor memory as the MMA's A
+// operand (V an MN-major shared-memory operand). Warps 2-9: online softmax, two warps per TMEM
+// lane quadrant: a query row (TMEM lane) is shared by two threads, each taking 64 of a chunk's
+// 128 key columns. Only the chunk max is exchanged (once per chunk, through shared memory); each
+// half keeps its own running sum under the common max and the two are added at the end. P_j
+// goes to tensor memory as fp16 pairs (tcgen05.st), never through shared memory. The running max
+// is updated lazily: while a chunk's max stays within 2^8 of it, the stale max is kept (P <= 256,
+// exact in the final O / l), so O is rescaled in TMEM (32 of its 64 columns per half) only when
+// the max jumps; the final 1/l scale and the token-major store out[b][t][h*64 + d] are split the
+// same way.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -25,18 +28,17 @@ namespace tsd {
 
 namespace {
 
-constexpr int kQT = 128, kKV = 128, kHD = 64, kStages = 3;
+constexpr int kQT = 128, kKV = 128, kHD = 64, kStages = 2;
 constexpr int kTileBytes = 128 * 128;               // 128 rows x 64 fp16
 constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kTileBytes;
-constexpr int kOffV = kOffK + kStages * kTileBytes;
-constexpr int kOffP = kOffV + kStages * kTileBytes;  // 2 buffers x 2 sub-tiles (kv 0-63, 64-127)
-constexpr int kOffRed = kOffP + 4 * kTileBytes;    // [3][2 halves][128 rows] f32: maxima (2 parities), sums
+constexpr int kOffK = kOffQ + kTileBytes;            // [kStages]
+constexpr int kOffV = kOffK + kStages * kTileBytes;  // [kStages]
+constexpr int kOffRed = kOffV + kStages * kTileBytes;   // [3][2 halves][128 rows] f32: maxima (2 parities), sums
 constexpr int kOffBar = kOffRed + 3 * 2 * 128 * 4;
 constexpr int kSmemBytes = kOffBar + 256 + 1024;
 constexpr int kThreads = 320;                        // warps: 0 TMA, 1 MMA, 2-9 softmax
-constexpr uint32_t kTmemCols = 512;                  // S0 @0, S1 @128, O @256
-constexpr uint32_t kColO = 256;
+constexpr uint32_t kTmemCols = 256;                  // two CTAs per SM share the 512 columns
+constexpr uint32_t kColO = 128, kColP = 192;
 constexpr float kLazyMax = 8.0f;                     // log2 of the largest P kept under a stale max
 
 struct AttnArgs {
@@ -50,7 +52,7 @@ struct AttnArgs {
 
 __device__ __forceinline__ void soft_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
     pdl_launch_dependents();   // let the next kernel in the stream start its prologue
@@ -58,13 +60,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t * bars = reinterpret_cast<uint64_t *>(smem + kOffBar);
     uint64_t * q_full = bars + 0;
-    uint64_t * kv_full = bars + 1;          // [3]
-    uint64_t * kv_empty = bars + 4;         // [3]
-    uint64_t * s_full = bars + 7;           // [2]
-    uint64_t * s_free = bars + 9;           // [2]
-    uint64_t * p_full = bars + 11;          // [2] per P buffer
-    uint64_t * pv_done = bars + 13;         // [2] per P buffer
-    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(bars + 15);
+    uint64_t * kv_full = bars + 1;          // [2]
+    uint64_t * kv_empty = bars + 3;         // [2]
+    uint64_t * s_full = bars + 5;           // S_j in TMEM
+    uint64_t * s_free = bars + 6;           // the softmax has read S_j (256 arrivals)
+    uint64_t * p_full = bars + 7;           // P_j in TMEM (256 arrivals)
+    uint64_t * pv_done = bars + 8;          // O += P_j V_j complete (P and O may be touched again)
+    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(bars + 9);
     volatile int * s_abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -76,8 +78,10 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
         for (int s = 0; s < kStages; ++s) { mbar_init(&kv_full[s], 1); mbar_init(&kv_empty[s], 1); }
-        for (int s = 0; s < 2; ++s) { mbar_init(&s_full[s], 1); mbar_init(&s_free[s], 256); }
-        for (int s = 0; s < 2; ++s) { mbar_init(&p_full[s], 256); mbar_init(&pv_done[s], 1); }
+        mbar_init(s_full, 1);
+        mbar_init(s_free, 256);
+        mbar_init(p_full, 256);
+        mbar_init(pv_done, 1);
         *s_abort = 0;
         fence_mbar_init();
     }
@@ -102,7 +106,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 tma_load_3d(smem + kOffK + s * kTileBytes, &tmK, &kv_full[s], 0, j * kKV, bh);
                 tma_load_3d(smem + kOffV + s * kTileBytes, &tmV, &kv_full[s], 0, j * kKV, bh);
             }
-            if (*s_abort) {
+            if (*s_abort) {   // let the copies still in flight land before the CTA exits
                 const unsigned long long t0 = globaltimer();
                 while (!mbar_try_wait(q_full, 0) && globaltimer() - t0 < wait_ns()) {}
                 for (int i = (issued > kStages ? issued - kStages : 0); i < issued; ++i) {
@@ -115,38 +119,35 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         if (lane == 0) {
             const uint32_t idesc_s = make_idesc_f16(128, kKV, false, false);
             const uint32_t idesc_o = make_idesc_f16(128, kHD, false, true);
-            const uint32_t sq = smem_u32(smem + kOffQ);
+            const uint64_t qd = make_sdesc_sw128(smem_u32(smem + kOffQ));
             bool ok = mbar_wait(q_full, 0, s_abort, a.err, DEV_TIMEOUT_ATTN);
-            auto issue_s = [&](int j) -> bool {
+            const auto issue_s = [&](int j) -> bool {
                 const int s = j % kStages;
                 if (!mbar_wait(&kv_full[s], (j / kStages) & 1, s_abort, a.err, DEV_TIMEOUT_ATTN)) return false;
-                if (j >= 2 && !mbar_wait(&s_free[j & 1], ((j >> 1) - 1) & 1, s_abort, a.err, DEV_TIMEOUT_ATTN)) return false;
                 tc_fence_after();
-                const uint64_t qd = make_sdesc_sw128(sq);
                 const uint64_t kd = make_sdesc_sw128(smem_u32(smem + kOffK + s * kTileBytes));
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk) umma_f16_ss(tmem + (j & 1) * 128, qd + 2 * kk, kd + 2 * kk, idesc_s, kk > 0);
-                umma_commit(&s_full[j & 1]);
+                for (int kk = 0; kk < 4; ++kk) umma_f16_ss(tmem, qd + 2 * kk, kd + 2 * kk, idesc_s, kk > 0);
+                umma_commit(s_full);
                 return true;
             };
             if (ok) ok = issue_s(0);
             for (int j = 0; ok && j < nchunks; ++j) {
-                if (j + 1 < nchunks && !issue_s(j + 1)) { ok = false; break; }
-                if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, s_abort, a.err, DEV_TIMEOUT_ATTN)) { ok = false; break; }
-                tc_fence_after();
-                const int s = j % kStages;
-                const uint32_t vb = smem_u32(smem + kOffV + s * kTileBytes);
-                const uint32_t pb = smem_u32(smem + kOffP + (j & 1) * 2 * kTileBytes);
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint64_t pd = make_sdesc_sw128(pb + (kk >> 2) * kTileBytes) + 2 * (kk & 3);
-                    const uint64_t vd = make_sdesc_sw128(vb + kk * 2048);
-                    umma_f16_ss(tmem + kColO, pd, vd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+                // S_{j+1} once the softmax has read S_j (it then overlaps the softmax of chunk j)
+                if (j + 1 < nchunks) {
+                    if (!mbar_wait(s_free, j & 1, s_abort, a.err, DEV_TIMEOUT_ATTN) || !issue_s(j + 1)) { ok = false; break; }
                 }
-                umma_commit(&kv_empty[s]);
-                umma_commit(&pv_done[j & 1]);
+                if (!mbar_wait(p_full, j & 1, s_abort, a.err, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t vb = smem_u32(smem + kOffV + (j % kStages) * kTileBytes);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    umma_f16_ts(tmem + kColO, tmem + kColP + 8 * kk, make_sdesc_sw128(vb + kk * 2048), idesc_o,
+                                (j > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(&kv_empty[j % kStages]);
+                umma_commit(pv_done);
             }
-            if (!ok) { umma_commit(&pv_done[0]); umma_commit(&pv_done[1]); }   // no waiter depends on unissued MMAs
+            if (!ok) { umma_commit(s_full); umma_commit(pv_done); }   // no waiter depends on unissued MMAs
         }
     } else {
         // ---------------- softmax + epilogue (warps 2..9) ----------------
@@ -161,32 +162,33 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         // The waits carry no shared abort flag: each warp gives up only on its own deadline.
         bool ok = true;
         for (int j = 0; j < nchunks; ++j) {
-            float sv[64];
+            const int valid = S - j * kKV - half * 64;   // columns >= valid are padding keys
             float mx = -INFINITY;
-            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, nullptr, a.err, DEV_TIMEOUT_ATTN));
+            uint32_t w[32];                            // columns 32-63 of this half, kept from pass 1
+            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, nullptr, a.err, DEV_TIMEOUT_ATTN));
             if (ok) {
                 tc_fence_after();
-                {
-                    // both 32-column loads in flight together
-                    uint32_t u0[32], u1[32];
-                    tmem_ld32_async(lane_base + (j & 1) * 128 + half * 64, u0);
-                    tmem_ld32_async(lane_base + (j & 1) * 128 + half * 64 + 32, u1);
-                    tmem_wait_ld(u0);
-                    tmem_wait_ld(u1);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) { sv[i] = __uint_as_float(u0[i]); sv[32 + i] = __uint_as_float(u1[i]); }
-                }
-                tc_fence_before();
-                mbar_arrive(&s_free[j & 1]);
-                const int valid = S - j * kKV - half * 64;  // columns >= valid are padding keys
-                // four independent partial maxima: the 64-long dependent chain dominated
+                // pass 1: the row max of this half's 64 scores (masking only in the ragged last chunk)
                 float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                uint32_t u[32];
+                tmem_ld32_async(lane_base + half * 64, u);
+                tmem_ld32_async(lane_base + half * 64 + 32, w);
+                tmem_wait_ld(u);
+                tmem_wait_ld(w);
+                if (valid >= 64) {
 #pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    sv[i] = (i < valid) ? sv[i] * a.scale_log2 : -INFINITY;
-                    m4[i & 3] = fmaxf(m4[i & 3], sv[i]);
+                    for (int i = 0; i < 32; ++i) {
+                        m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(u[i]));
+                        m4[(i + 2) & 3] = fmaxf(m4[(i + 2) & 3], __uint_as_float(w[i]));
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        if (i < valid) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(u[i]));
+                        if (32 + i < valid) m4[(i + 2) & 3] = fmaxf(m4[(i + 2) & 3], __uint_as_float(w[i]));
+                    }
                 }
-                mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+                mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * a.scale_log2;
             }
             float * rm = red + ((j & 1) * 2) * 128;     // this chunk's maxima [half][row]
             rm[half * 128 + r] = mx;
@@ -197,46 +199,69 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             const bool grow = mc > m_run + kLazyMax;
             const float m_new = grow ? mc : m_run;
             const float alpha = grow ? ex2_approx(m_run - m_new) : 1.0f;   // 0 on the first chunk
-            float r4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int i = 0; i < 64; ++i) { sv[i] = ex2_approx(sv[i] - m_new); r4[i & 3] += sv[i]; }
-            const float rs = (r4[0] + r4[1]) + (r4[2] + r4[3]);
-            l_run = l_run * alpha + rs;
-            m_run = m_new;
-            if (j > 0 && __any_sync(0xffffffffu, grow)) {
-                // O must hold PV_{j-1} before it is rescaled (rows that keep their max scale by 1)
-                ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, nullptr, a.err,
-                                                       DEV_TIMEOUT_ATTN));
+            if (j > 0) {
+                // PV_{j-1} must be done with P (rewritten below) and O (rescaled here)
+                ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, nullptr, a.err, DEV_TIMEOUT_ATTN));
                 if (!ok) continue;
                 tc_fence_after();
-                float o[32];
-                tmem_ld32(lane_base + kColO + half * 32, o);
+                if (__any_sync(0xffffffffu, grow)) {   // rows that keep their max scale by 1
 #pragma unroll
-                for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                tmem_st32(lane_base + kColO + half * 32, o);
-            }
-            if (j >= 2) {   // P buffer j & 1 was last read by PV_{j-2}
-                ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[j & 1], ((j - 2) >> 1) & 1, nullptr, a.err,
-                                                       DEV_TIMEOUT_ATTN));
-                if (!ok) continue;
-            }
-            // P (fp16) into this half's 128-B swizzled K-major sub-tile: row r, 16-B chunk ch -> ch ^ (r & 7)
-            uint8_t * prow = smem + kOffP + ((j & 1) * 2 + half) * kTileBytes + r * 128;
+                    for (int c0 = 0; c0 < 32; c0 += 16) {  // 16 columns at a time: few live registers
+                        float o[16];
+                        tmem_ld16(lane_base + kColO + half * 32 + c0, o);
 #pragma unroll
-            for (int ch = 0; ch < 8; ++ch) {
-                uint4 u;
-                __half2 * h2 = reinterpret_cast<__half2 *>(&u);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) h2[e] = __floats2half2_rn(sv[ch * 8 + 2 * e], sv[ch * 8 + 2 * e + 1]);
-                *reinterpret_cast<uint4 *>(prow + ((ch ^ (r & 7)) << 4)) = u;
+                        for (int i = 0; i < 16; ++i) o[i] *= alpha;
+                        tmem_st16(lane_base + kColO + half * 32 + c0, o);
+                    }
+                }
             }
-            fence_proxy_async_smem();
+            // pass 2: P = 2^(s * scale - m), fp16 pairs (key 2c in the low half) into the P columns;
+            // one exponential in four on the FMA pipes (exp2_poly), the rest on the SFU
+            float r4[4] = {0.f, 0.f, 0.f, 0.f};
+            const float nm = -m_new;
+            {
+                // columns 0-31 are read again (the last read of S_j: S_{j+1} may then overwrite it,
+                // and runs while the exponentials below are computed); columns 32-63 are in w
+                uint32_t u[32];
+                tmem_ld32_async(lane_base + half * 64, u);
+                tmem_wait_ld(u);
+                tc_fence_before();
+                mbar_arrive(s_free);
+                const auto piece = [&](const uint32_t (&v)[32], int c0) {
+                    const int vlim = valid - c0;       // columns >= vlim of this piece are padding keys
+#pragma unroll
+                    for (int c1 = 0; c1 < 32; c1 += 16) {
+                        uint32_t pk[8];
+#pragma unroll
+                        for (int c = 0; c < 8; ++c) {
+                            const int i0 = c1 + 2 * c;
+                            float x0 = fmaf(__uint_as_float(v[i0]), a.scale_log2, nm);
+                            float x1 = fmaf(__uint_as_float(v[i0 + 1]), a.scale_log2, nm);
+                            if (vlim < 32) {           // only in the ragged last chunk
+                                if (i0 >= vlim) x0 = -INFINITY;
+                                if (i0 + 1 >= vlim) x1 = -INFINITY;
+                            }
+                            const float p0 = ex2_approx(x0);
+                            const float p1 = (i0 & 2) ? exp2_poly(x1) : ex2_approx(x1);
+                            r4[(2 * c) & 3] += p0;
+                            r4[(2 * c + 1) & 3] += p1;
+                            const __half2 h2 = __floats2half2_rn(p0, p1);
+                            pk[c] = *reinterpret_cast<const uint32_t *>(&h2);
+                        }
+                        tmem_st8_u(lane_base + kColP + half * 32 + (c0 + c1) / 2, pk);
+                    }
+                };
+                piece(u, 0);
+                piece(w, 32);
+            }
+            l_run = l_run * alpha + ((r4[0] + r4[1]) + (r4[2] + r4[3]));
+            m_run = m_new;
+            tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&p_full[j & 1]);
+            mbar_arrive(p_full);
         }
         const int jl = nchunks - 1;
-        const bool fin = ok && __all_sync(0xffffffffu, mbar_wait(&pv_done[jl & 1], (jl >> 1) & 1, nullptr, a.err,
-                                                                  DEV_TIMEOUT_ATTN));
+        const bool fin = ok && __all_sync(0xffffffffu, mbar_wait(pv_done, jl & 1, nullptr, a.err, DEV_TIMEOUT_ATTN));
         // both halves' sums under the common max
         float * rl = red + 4 * 128;
         rl[half * 128 + r] = l_run;
@@ -258,11 +283,11 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 __nv_bfloat16 * dst = reinterpret_cast<__nv_bfloat16 *>(a.out) + ((long long)b * S + t) * a.ldo + h * kHD + half * 32;
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    uint4 u;
-                    __nv_bfloat162 * p2 = reinterpret_cast<__nv_bfloat162 *>(&u);
+                    uint4 u4;
+                    __nv_bfloat162 * p2 = reinterpret_cast<__nv_bfloat162 *>(&u4);
 #pragma unroll
                     for (int i = 0; i < 4; ++i) p2[i] = __floats2bfloat162_rn(o[e * 8 + 2 * i] * inv, o[e * 8 + 2 * i + 1] * inv);
-                    *reinterpret_cast<uint4 *>(dst + e * 8) = u;
+                    *reinterpret_cast<uint4 *>(dst + e * 8) = u4;
                 }
             }
         }
@@ -294,6 +319,8 @@ cudaError_t attn_launch(const AttnLaunch & L, cudaStream_t st) {
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        // all of the SM's unified L1 / shared storage as shared memory: two CTAs per SM
+        cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         attr = true;
     }
     AttnArgs a;
