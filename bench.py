@@ -22,6 +22,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -513,6 +514,17 @@ def main():
                     "in_step_ms": l_step, "tflops": l_fl / l_step / 1e9,
                     "frac_of_burst": l_fl / l_step / 1e9 / peak_b, "frac_of_sustained": l_fl / l_step / 1e9 / peak,
                     "layers_averaged": len(layers)}
+        # config 2: the stack of 14 fused (single-stream) blocks (LN-modulate, QKV with QK-norm /
+        # RoPE, attention, out-projection, LN-modulate, SwiGLU FFN) of this step, same B and T
+        fsel = [k for k, l in enumerate(labels) if re.match(r"f\d+ ", l)]
+        cfg2 = None
+        if fsel:
+            f_ms = float(prof["ms"][fsel].sum())
+            f_fl = float(prof["flops"][fsel].sum())
+            f_step = ms_step * share(f_ms)
+            cfg2 = {"blocks": hp.fused_depth, "tflop": f_fl / 1e12, "serialised_ms": f_ms, "in_step_ms": f_step,
+                    "tflops": f_fl / f_step / 1e9, "frac_of_sustained": f_fl / f_step / 1e9 / peak,
+                    "frac_of_burst": f_fl / f_step / 1e9 / peak_b}
         line = {
             "metric": METRIC if not cfg4 else "DiT flow-steps/s at 30 s, CFG=2, Q8_0 weights", "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
@@ -536,6 +548,7 @@ def main():
                                    "per-op pass); lower bound: GEMM FLOPs per step / timed step",
                          "traffic": traffic},
             "attn_layer_cfg1": cfg1,
+            "fused_stack_cfg2": cfg2,
             "kernels": {
                 "note": "ms: serialised per-op pass (CUDA events between ops, no graph); in_step_ms: share of the timed step",
                 "gemm": {"launches": g_n, "ms": g_ms, "in_step_ms": g_step_ms, "tflops": g_tf},

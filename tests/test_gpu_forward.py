@@ -276,3 +276,18 @@ def test_cfg4_q8_30s_shapes_h1536():
     fe1 = om.forward(items[1], mode=oracle.MODE_EXACT)
     fo1 = om.forward(items[1], mode=oracle.MODE_GGML)
     assert oracle.rel_l2(flow[1], fe1) <= 1.2 * oracle.rel_l2(fo1, fe1) + 2e-3
+
+
+def test_many_item_batch_conditioning_gemms(small_bf16):
+    """With more than 8 items the few-token projections (timestep MLP, conditioning projections,
+    the stacked clip / text adaLN) run on the tensor-core GEMM instead of the GEMV; every item
+    must still match its single-item forward and the oracle."""
+    hp, W, m, om = small_bf16
+    items = synth.make_inputs(hp, seed=91, batch=10, **SHAPE)
+    fb = m.forward(items)
+    for b in (0, 9):
+        assert oracle.rel_l2(fb[b], m.forward([items[b]])[0]) < 3e-3
+    fo = om.forward(items[9], mode=oracle.MODE_GGML)
+    fe = om.forward(items[9], mode=oracle.MODE_EXACT)
+    assert oracle.rel_l2(fb[9], fo) < 5e-3
+    assert oracle.rel_l2(fb[9], fe) <= 1.2 * oracle.rel_l2(fo, fe) + 1e-3

@@ -275,9 +275,23 @@ struct Builder {
         return X;
     }
     unsigned * epoch_ptr = nullptr;
-    // Few-token GEMV over B items (chunks of 8 tokens).
+    // Few-token GEMV over B items (chunks of 8 tokens). With more than 8 tokens a GEMV would
+    // stream the weight once per chunk of 8, so a single BF16 weight (the GEMV also rounds x to
+    // bf16 for it) runs on the tensor-core GEMM instead, after a cast of x to bf16.
     void gemv(const VW & w, const float * x, long long ldx, int N, int act, float * y, long long ldy, int y_bf16 = 0) {
         if (rc) return;
+        if (N > 8 && w.type == GT_BF16 && !w.w2 && w.M % 128 == 0 && w.K % 64 == 0 && ldx == w.K) {
+            auto * xb = alloc<__nv_bfloat16>((size_t)N * w.K);
+            if (rc) return;
+            const long long n = (long long)N * w.K;
+            op([=](cudaStream_t st) { return cast_f32_bf16(x, n, xb, st); });
+            GW g;
+            g.w = const_cast<__nv_bfloat16 *>(static_cast<const __nv_bfloat16 *>(w.w));
+            g.M = w.M; g.K_in = w.K; g.taps = 1; g.pad = 0; g.m_valid = w.M;
+            g.bias = const_cast<float *>(w.bias);
+            gemm(g, xb, 1, N, w.K, (long long)N * w.K, EPI_STORE, act, y, y_bf16, ldy);
+            return;
+        }
         const VW wc = w;
         int * const err = m.d_err;
         op([wc, x, ldx, N, act, y, ldy, y_bf16, err](cudaStream_t st) {
