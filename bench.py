@@ -205,10 +205,11 @@ def run_reference(args, rank, world):
 
 
 # ----------------------------------------------------------------------------------- ours
-def profile_case(wtype):
-    """One forward (B=2, config-3 token counts) of a depth-3 model (2 joint + 1 fused blocks) with
-    the full model's GEMM / attention / GEMV shapes, op by op through tsd_forward_profile; prints
-    each op's time. Small enough (~1.3 GB of weights) for a full ncu capture of single launches."""
+def profile_case(wtype, workload="cfg3"):
+    """One forward (B=2, config-3 token counts, or config 4's with workload "cfg4") of a depth-3
+    model (2 joint + 1 fused blocks) with the full model's GEMM / attention / GEMV shapes, op by
+    op through tsd_forward_profile; prints each op's time. Small enough (~1.3 GB of weights) for
+    a full ncu capture of single launches."""
     import torch
     import __graft_entry__
     __graft_entry__.load_package()
@@ -221,8 +222,9 @@ def profile_case(wtype):
         W = synth.make_weights(hp, seed=1234, wtype="q8_0", q8_random_blocks=True)
     m = tsd.DitModel.from_weights(hp, W)
     del W
-    X = make_device_inputs(2, CFG3, 4242, "cuda:0")
-    p = m.forward_profile(2, CFG3["T"], CFG3["clip_S"], CFG3["sync_S"], CFG3["text_S"], CFG3["t5_S"],
+    SH = CFG4 if workload == "cfg4" else CFG3
+    X = make_device_inputs(2, SH, 4242, "cuda:0")
+    p = m.forward_profile(2, SH["T"], SH["clip_S"], SH["sync_S"], SH["text_S"], SH["t5_S"],
                           {k: v.data_ptr() for k, v in X.items()})
     for i, (l, ms, b) in enumerate(zip(p["labels"], p["ms"], p["bytes"])):
         print(f"{i:3d} {ms * 1000:8.1f} us {b / ms / 1e6:7.0f} GB/s  {l}")
@@ -346,7 +348,7 @@ def main():
                          "the config-3 widths (the small case the ncu captures are taken on)")
     args = ap.parse_args()
     if args.profile_case:
-        return profile_case(args.profile_case)
+        return profile_case(args.profile_case, args.workload if args.workload in ("cfg3", "cfg4") else "cfg3")
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

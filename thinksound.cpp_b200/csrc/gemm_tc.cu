@@ -607,6 +607,34 @@ __device__ __forceinline__ void finish_slice(const GemmParams & p, const CUtenso
     }
 }
 
+// 16 Q8_0 weights (one 16-byte chunk of a row) -> 16 bf16 w = bf16(q * d): each byte becomes the
+// f32 2^23 + 128 + q by a byte permute into the mantissa (after flipping its sign bit), an f32x2
+// subtract leaves q exactly, an f32x2 multiply gives q * d exactly (8 x 11 significant bits), and
+// one conversion per pair rounds to bf16: the same bits as the load-time widening.
+__device__ __forceinline__ void q8_chunk_to_bf16(const uint4 & u, float d, uint32_t (&o)[8]) {
+    const uint32_t w4[4] = {u.x ^ 0x80808080u, u.y ^ 0x80808080u, u.z ^ 0x80808080u, u.w ^ 0x80808080u};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const float f0 = __uint_as_float(__byte_perm(w4[i], 0x4B000000u, 0x7650u + 2 * h));
+            const float f1 = __uint_as_float(__byte_perm(w4[i], 0x4B000000u, 0x7650u + 2 * h + 1));
+            uint32_t r;
+            asm("{\n\t.reg .b64 a, m, s, t;\n\t"
+                "mov.b64 a, {%1, %2};\n\t"
+                "mov.b64 m, {%3, %3};\n\t"
+                "mov.b64 s, {%4, %4};\n\t"
+                "add.rn.f32x2 t, a, m;\n\t"
+                "mul.rn.f32x2 t, t, s;\n\t"
+                "{\n\t.reg .f32 lo, hi;\n\t"
+                "mov.b64 {lo, hi}, t;\n\t"
+                "cvt.rn.bf16x2.f32 %0, hi, lo;\n\t}\n\t}"
+                : "=r"(r) : "f"(f0), "f"(f1), "f"(-8388736.0f), "f"(d));
+            o[2 * i + h] = r;
+        }
+    }
+}
+
 // PAIR: the CTA-pair form (cta_group::2). A kernel holding cta_group::2 instructions must be
 // launched in clusters of an even size, so the single-CTA form is a separate instance.
 template <int EK, bool PAIR>
@@ -648,11 +676,50 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const uint32_t b_bytes = (uint32_t)(bh * 128);                   // one B atom
     const int sbytes = kpb * (kABytes + (int)b_bytes) + (p.a_q8 ? kQ8Bytes : 0);
     const int nst = p.stages;                   // ring depth, <= kMaxStages, nst * sbytes <= kStageArea
+    // Q8_0: warps 6-7 convert each stage's int8 tile; a CTA with a single tile (no epilogue to
+    // overlap with a later main loop) puts its four epilogue warps on the conversion as well
+    const bool q8_single = p.a_q8 && tile0 + tstep >= num_tiles;
+    const int q8_conv_warps = q8_single ? 6 : 2;
+    // Q8_0 conversion of every stage of this CTA's tiles by converter thread `cid` of `ncv`:
+    // 16-byte units u = row * 4 + chunk of the 128 x 64 int8 tile, each to two 16-byte chunks of
+    // the bf16 A tile in the 128-byte-swizzled layout TMA would have written (16-byte chunk j of
+    // row r at r * 128 + ((j ^ (r & 7)) << 4)); then one arrival per warp on the stage's barrier.
+    const auto convert_q8 = [&](int cid, int ncv) {
+        int s = 0;
+        uint32_t ph = 0;
+        for (int t = tile0; t < num_tiles; t += tstep) {
+            const TileCoord c = decode(p, t, nks, prank);    // kpb = 1 on this path
+            bool ok = true;
+            for (int kb = c.kb_begin; kb < c.kb_end; ++kb) {
+                if (!mbar_wait(&rfull[s], ph, s_abort, p.err, DEV_TIMEOUT_FULL)) { ok = false; break; }
+                uint8_t * sa = smem + s * sbytes;
+                const uint8_t * raw = sa + kABytes + p.BN * 128;
+                const __half * sc = reinterpret_cast<const __half *>(raw + 128 * 64);
+                for (int u = cid; u < 512; u += ncv) {
+                    const int r = u >> 2, jj = u & 3;
+                    const uint4 q = reinterpret_cast<const uint4 *>(raw + r * 64)[jj];
+                    uint32_t o[8];
+                    q8_chunk_to_bf16(q, __half2float(sc[(jj >> 1) * 128 + r]), o);
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        const int j = jj * 2 + half;
+                        *reinterpret_cast<uint4 *>(sa + r * 128 + ((j ^ (r & 7)) << 4)) =
+                            make_uint4(o[4 * half], o[4 * half + 1], o[4 * half + 2], o[4 * half + 3]);
+                    }
+                }
+                fence_proxy_async_smem();       // the MMA reads the tile through the async proxy
+                __syncwarp();
+                if ((threadIdx.x & 31) == 0) mbar_arrive(&full[s]);
+                if (++s == nst) { s = 0; ph ^= 1; }
+            }
+            if (!ok) break;
+        }
+    };
 
     if (threadIdx.x == 0) {
         // full: the producer's expect_tx (+ both converter warps' arrivals on the Q8_0 path)
         for (int s = 0; s < kMaxStages; ++s) {
-            mbar_init(&full[s], p.a_q8 ? 3 : 1); mbar_init(&empty[s], 1); mbar_init(&rfull[s], 1);
+            mbar_init(&full[s], p.a_q8 ? 1 + q8_conv_warps : 1); mbar_init(&empty[s], 1); mbar_init(&rfull[s], 1);
         }
         // acc_empty: the four epilogue warps (of both CTAs of a pair, on the leader's)
         for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], PAIR ? 8 : 4); mbar_init(&ebar[s], 1); }
@@ -822,60 +889,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             else produce(1, 1, 2);                              // weight tiles of odd K steps
         }
         // ---------------- Q8_0 converters (warps 6, 7) ----------------
-        // Each stage's int8 tile (128 rows x 64, row-major) and its scales ([2 blocks][128 rows]
-        // f16) become the bf16 A tile in the 128-byte-swizzled layout TMA would have written:
-        // 16-byte chunk j of row r at r * 128 + ((j ^ (r & 7)) << 4). w = (float)q * scale,
-        // rounded to bf16 (the load-time conversion's arithmetic). Thread t: rows t and t + 64.
-        if (p.a_q8) {
-            const int t64 = (warp - 6) * 32 + lane;
-            int s = 0;
-            uint32_t ph = 0;
-            for (int t = tile0; t < num_tiles; t += tstep) {
-                const TileCoord c = decode(p, t, nks, prank);    // kpb = 1 on this path
-                bool ok = true;
-                for (int kb = c.kb_begin; kb < c.kb_end; ++kb) {
-                    if (!mbar_wait(&rfull[s], ph, s_abort, p.err, DEV_TIMEOUT_FULL)) { ok = false; break; }
-                    uint8_t * sa = smem + s * sbytes;
-                    const uint8_t * raw = sa + kABytes + p.BN * 128;
-                    const __half * sc = reinterpret_cast<const __half *>(raw + 128 * 64);
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int r = t64 + 64 * h;
-                        const float d0 = __half2float(sc[r]), d1 = __half2float(sc[128 + r]);
-                        const uint4 * qr = reinterpret_cast<const uint4 *>(raw + r * 64);
-#pragma unroll
-                        for (int jj = 0; jj < 4; ++jj) {              // 16 int8 -> two 8-weight chunks
-                            const uint4 u = qr[jj];
-                            const float d = jj < 2 ? d0 : d1;
-                            const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
-                            uint32_t o[8];
-#pragma unroll
-                            for (int i = 0; i < 8; ++i) {
-                                const uint32_t word = w4[i >> 1];
-                                const int sh = (i & 1) * 16;
-                                const float lo = (float)(int8_t)((word >> sh) & 0xffu) * d;
-                                const float hi = (float)(int8_t)((word >> (sh + 8)) & 0xffu) * d;
-                                const __nv_bfloat162 bb = __floats2bfloat162_rn(lo, hi);
-                                o[i] = *reinterpret_cast<const uint32_t *>(&bb);
-                            }
-#pragma unroll
-                            for (int half = 0; half < 2; ++half) {
-                                const int j = jj * 2 + half;
-                                *reinterpret_cast<uint4 *>(sa + r * 128 + ((j ^ (r & 7)) << 4)) =
-                                    make_uint4(o[4 * half], o[4 * half + 1], o[4 * half + 2], o[4 * half + 3]);
-                            }
-                        }
-                    }
-                    fence_proxy_async_smem();       // the MMA reads the tile through the async proxy
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&full[s]);
-                    if (++s == nst) { s = 0; ph ^= 1; }
-                }
-                if (!ok) break;
-            }
-        }
+        if (p.a_q8) convert_q8((warp - 6) * 32 + lane, 32 * q8_conv_warps);
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
+        if (q8_single) convert_q8(64 + (warp - 2) * 32 + lane, 32 * q8_conv_warps);
         pdl_wait();
         const int q = warp & 3;                       // TMEM lane quadrant of this warp
         const int ml = q * 32 + lane;                 // TMEM lane = weight row within the tile

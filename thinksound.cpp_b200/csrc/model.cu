@@ -165,8 +165,9 @@ struct Finalizer {
     // Planar Q8_0 for the GEMM (TSD_Q8_IN_KERNEL=1) when every source is Q8_0 with one tap (the
     // reference quantises only 2-D weights; convolution weights stay F32): the weights stay resident
     // at 34 bytes per 32 and the GEMM's converter warps dequantise each tile in shared memory.
-    // Default: widen to bf16 at load (the converter warps cannot keep up with the tensor core, so
-    // the in-kernel path trades speed for 47% less weight memory; results are identical).
+    // Default: widen to bf16 at load. The in-kernel path keeps 47% less weight memory resident and
+    // gives identical results, but its conversion (two warps per stage, six in a CTA with a single
+    // tile) still costs ~1.3x the widened step at config 4.
     bool q8_gemm(std::initializer_list<const RawTensor *> ts, int taps, int K_in) {
         const char * e = getenv("TSD_Q8_IN_KERNEL");
         if (!(e && *e == '1') || taps != 1 || K_in % 64) return false;
