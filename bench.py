@@ -409,7 +409,9 @@ def main():
     g_ms, g_fl, g_by, g_n = agg(0)
     a_ms, a_fl, a_by, a_n = agg(2)
     v_ms, v_fl, v_by, v_n = agg(1)
-    tot_ms = float(prof["ms"].sum())
+    # kernel ops only (GEMM, GEMV, attention, elementwise): device copies and the graph's lane
+    # markers are not kernels, so the shares agree with an ncu launch list of the same forward
+    tot_ms = float(prof["ms"][kinds != 4].sum())
     # attention + projection path of the headline metric ("MM-DiT attn TFLOP/s"): the QKV GEMMs,
     # attention and the out-projection (linear1) GEMMs
     labels = prof["labels"]
@@ -569,6 +571,7 @@ def main():
                               "frac_of_sustained_peak": ap_fl / (ms_step * share(ap_ms) / 1000.0) / 1e12 / peak if ap_ms else None,
                               "frac_of_burst_peak": ap_fl / (ms_step * share(ap_ms) / 1000.0) / 1e12 / peak_b if ap_ms else None},
                 "other_ms": tot_ms - g_ms - a_ms - v_ms, "profiled_step_ms": tot_ms,
+                "copies_ms": float(prof["ms"][kinds == 4].sum()),
                 "step_tflops_device": fl["total"] / (ms_step / 1000.0) / 1e12,
             },
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": d2h},
