@@ -291,3 +291,44 @@ def test_many_item_batch_conditioning_gemms(small_bf16):
     fe = om.forward(items[9], mode=oracle.MODE_EXACT)
     assert oracle.rel_l2(fb[9], fo) < 5e-3
     assert oracle.rel_l2(fb[9], fe) <= 1.2 * oracle.rel_l2(fo, fe) + 1e-3
+
+
+def test_ts_server_keeps_the_dit_resident(tmp_path, small_bf16):
+    """tests/shim/ts_server_demo.cpp: the DiT part of ts-server's request path with the model
+    loaded once and reused by every request (the reference reloads it per request,
+    ts-server.cpp:74). Four requests over two input shapes: one load, and every request's
+    latent equals a fresh model's sample of the same inputs."""
+    import subprocess
+    hp, W, m, _ = small_bf16
+    path = str(tmp_path / "dit.gguf")
+    synth.write_gguf(path, hp, W)
+    libdir = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "thinksound.cpp_b200")
+    incdir = os.path.join(os.path.dirname(libdir), "include")
+    src = os.path.join(os.path.dirname(os.path.abspath(__file__)), "shim", "ts_server_demo.cpp")
+    exe = str(tmp_path / "ts_server_demo")
+    subprocess.run(["g++", "-std=c++17", "-O1", "-I", incdir, src, "-o", exe, "-L", libdir, "-ltsd_b200",
+                    f"-Wl,-rpath,{libdir}"], check=True)
+    reqs = [(20, 0.0), (20, 1.5), (40, 0.25), (20, 3.0)]
+    out = str(tmp_path / "lat.bin")
+    r = subprocess.run([exe, path, "2", out] + [f"{T}:{s}" for T, s in reqs], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    assert "loads=1" in r.stdout, r.stdout
+    print(r.stdout)
+    data = np.fromfile(out, np.float32)
+    fresh = tsd.DitModel.load(path)
+    off = 0
+    for T, seed in reqs:
+        lat = data[off:off + 64 * T].reshape(64, T)
+        off += 64 * T
+        i = np.arange
+        f32 = lambda a: np.asarray(a, np.float64).astype(np.float32)
+        cS, yS = 8 * ((T + 19) // 20), 24 * ((T + 19) // 20)
+        noise = f32(np.sin(0.37 * i(64 * T) + seed)).reshape(64, T)
+        text = f32(np.cos(0.11 * i(77 * 1024) + seed)).reshape(77, 1024)
+        t5 = f32(np.sin(0.05 * i(77 * 2048) + 1.0 + seed)).reshape(77, 2048)
+        gt = f32(np.cos(0.7 * i(1024) + seed))
+        clip = np.tile(W["empty_clip_feat"].dequant().reshape(1, 1024), (cS, 1))
+        sync = np.tile(W["empty_sync_feat"].dequant().reshape(1, 768), (yS, 1))
+        ref = fresh.sample([synth.DitInputs(noise, clip, sync, text, t5, gt, 1.0)], steps=2, cfg=5.0)[0]
+        assert oracle.rel_l2(lat, ref) < 1e-5, (T, seed)
+    fresh.close()
