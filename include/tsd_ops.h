@@ -67,10 +67,12 @@ TSD_API int tsd_op_gemm_static(const void * W, int M, int K_in, int taps, int pa
 /* The tiling tsd_op_gemm would choose for a GEMM shape given `ws_floats` / `n_counters` of
  * scratch (no launch; for tests and tuning). out[0] token tile, out[1] K splits, out[2] 1 for
  * CTA pairs, out[3] 1 if the splits reduce inside a thread-block cluster (no scratch), out[4]
- * scratch floats the plan needs (non-zero only for split-K through global memory). Needs the
- * GPU the GEMM would run on to be current (cluster occupancy is a property of the device). */
+ * scratch floats the plan needs (non-zero only for split-K through global memory), out[5] 1 if,
+ * with one tile per CTA, the split that completes a tile last gathers the other splits' partials
+ * from the scratch into its shared memory (else a reducer reads them there). Needs the GPU the
+ * GEMM would run on to be current (cluster occupancy is a property of the device). */
 TSD_API int tsd_op_gemm_plan(int M, int K_in, int taps, int nbatch, int S, int max_splits, int64_t ws_floats,
-                             int n_counters, int64_t out[5]);
+                             int n_counters, int64_t out[6]);
 
 /* The head-parallel arrival wait (tsd_hp_* in tsd.h) as an operator: one warp waits until
  * counters[r] >= *epoch * ctas for every rank r != rank of `world`, bounded by the wait limit

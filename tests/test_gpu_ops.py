@@ -147,6 +147,57 @@ def test_gemm_split_k_store_and_swiglu(mode):
     assert int(counters.abs().sum()) == 0
 
 
+@pytest.mark.parametrize("gather", [1, 0])
+@pytest.mark.parametrize("mode,gate_div", [(tsd.EPI_GATE_RESID, 1), (tsd.EPI_GATE_RESID, 0), (tsd.EPI_STORE, 1),
+                                           (tsd.EPI_SWIGLU, 1)])
+@pytest.mark.parametrize("M,K,taps,nb,S", [(512, 8192, 3, 2, 40), (1536, 4096, 3, 2, 194)])
+def test_gemm_workspace_split_k(monkeypatch, M, K, taps, nb, S, mode, gate_div, gather):
+    """Split-K through the workspace (the in-cluster reduction switched off), one tile per CTA:
+    the split that completes a tile last either gathers the other partials into its shared memory
+    and finishes the tile like an unsplit one (gather), or a reducer reads them from the
+    workspace. Both sum the partials in split order (two runs bit-identical) and leave the
+    arrival counters zero. (1536, 4096 x 3, 2 x 194) is the fused blocks' FFN down-projection.
+    gate_div 0: one gate row per batch item (the joint blocks' clip / text streams)."""
+    monkeypatch.setenv("TSD_NO_CLUSTER_SPLIT", "1")
+    if not gather:
+        monkeypatch.setenv("TSD_NO_GATHER_SPLIT", "1")
+    ws = torch.empty(8 << 20, device=DEV)
+    counters = torch.zeros(1 << 16, device=DEV, dtype=torch.int32)
+    plan = tsd.op_gemm_plan(M, K, taps, nb, S, 8, ws.numel(), counters.numel())
+    if not gather and plan["splits"] == 1:
+        pytest.skip("the model does not split this shape without the gathering reduction")
+    assert plan["splits"] > 1 and not plan["csplit"] and plan["gather"] == gather, plan
+    W = rnd(M, taps * K, scale=0.02)
+    X = rnd(nb, S, K)
+    bias = torch.randn(M, device=DEV)
+    gdiv = gate_div if gate_div else S
+    gate = torch.randn(nb * S // gdiv, M, device=DEV)
+    x0 = torch.randn(nb, S, M, device=DEV)
+    Fo = M // 2 if mode == tsd.EPI_SWIGLU else M
+    outs = []
+    for _ in range(2):
+        if mode == tsd.EPI_GATE_RESID:
+            x = x0.clone()
+            tsd.op_gemm(W, M, K, taps, taps // 2, X, nb, S, K, S * K, mode, 0, bias, None, 0, 0, resid=x, ldr=M,
+                        gate=gate, ldg=M, gate_div=gdiv, max_splits=8, ws=ws, counters=counters)
+        else:
+            x = torch.empty(nb, S, Fo, device=DEV)
+            tsd.op_gemm(W, M, K, taps, taps // 2, X, nb, S, K, S * K, mode, 0, bias if mode == tsd.EPI_STORE else None,
+                        x, 0, Fo, max_splits=8, ws=ws, counters=counters)
+        outs.append(x)
+    torch.cuda.synchronize()
+    acc = ref_gemm(W, X, taps, taps // 2)
+    if mode == tsd.EPI_GATE_RESID:
+        ref = x0 + gate.view(nb, S // gdiv, 1, M).expand(nb, S // gdiv, gdiv, M).reshape(nb, S, M) * (acc + bias)
+    elif mode == tsd.EPI_STORE:
+        ref = acc + bias
+    else:
+        ref = torch.nn.functional.silu(acc[..., 0::2]) * acc[..., 1::2]
+    assert rel(outs[0], ref) < 1e-5
+    assert torch.equal(outs[0], outs[1])
+    assert int(counters.abs().sum()) == 0
+
+
 @pytest.mark.parametrize("M,K,taps,nb,S,mode,splits", [
     (1536, 1536, 3, 2, 194, tsd.EPI_GATE_RESID, 2),  # linear1 / w2 shape class: pair tiles + cluster split-K
     (4608, 256, 1, 1, 388, tsd.EPI_STORE, 1),        # QKV-like: one pair tile per CTA pair

@@ -449,7 +449,7 @@ int tsd_op_gemm(const void * W, int M, int K_in, int taps, int pad, const void *
 }
 
 int tsd_op_gemm_plan(int M, int K_in, int taps, int nbatch, int S, int max_splits, int64_t ws_floats, int n_counters,
-                     int64_t out[5]) {
+                     int64_t out[6]) {
     if (!out) return TSD_ERR_ARG;
     int dev = 0, sms = 148;
     TSD_CUDA_TRY(cudaGetDevice(&dev));
@@ -461,6 +461,7 @@ int tsd_op_gemm_plan(int M, int K_in, int taps, int nbatch, int S, int max_split
                    ws_floats, n_counters, true))
         return TSD_ERR_ARG;
     out[0] = L.p.BN; out[1] = L.p.splits; out[2] = L.p.pair; out[3] = L.p.csplit; out[4] = gemm_ws_floats(L);
+    out[5] = L.p.gather;
     return TSD_OK;
 }
 

@@ -187,6 +187,22 @@ __device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, const vo
                  ::"r"(dst_cluster), "r"(smem_u32(src)), "r"(bytes), "r"(mbar_cluster)
                  : "memory");
 }
+// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from global memory into
+// this CTA's shared memory, completing on this CTA's mbarrier `bar` (byte count). Not a multicast.
+__device__ __forceinline__ void bulk_load_g2s(void * dst, const void * src, uint32_t bytes, uint64_t * bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"((unsigned long long)__cvta_generic_to_global(src)), "r"(bytes),
+                   "r"(smem_u32(bar))
+                 : "memory");
+}
+// Order this thread's earlier memory accesses (and what it has acquired from other threads)
+// before its later async-proxy accesses (bulk copies), in every state space.
+__device__ __forceinline__ void fence_proxy_async_all() { asm volatile("fence.proxy.async;" ::: "memory"); }
+__device__ __forceinline__ int ld_acquire_gpu(const int * a) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+    return v;
+}
 __device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
 // Arrive (release, cluster scope) on an mbarrier given by its shared::cluster address.
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {

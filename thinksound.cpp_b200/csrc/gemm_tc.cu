@@ -920,8 +920,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             e.ncols = min(p.BN, p.S - c.t0);
             e.row_base = (long long)c.b * p.S + c.t0;
             e.col = p.out_cblk ? (long long)(e.m / p.out_cblk) * p.out_cstride + e.m % p.out_cblk : e.m;
-            const bool tma = p.epi_tma && p.splits == 1;
-            const bool tma_gate = p.epi_tma && (p.splits == 1 || p.csplit);     // residual / gate maps exist
+            const bool whole = p.splits == 1 || p.gather;     // this CTA finishes whole tiles
+            const bool tma = p.epi_tma && whole;
+            const bool tma_gate = p.epi_tma && (whole || p.csplit);           // residual / gate maps exist
             const int m0 = Epi<EK>::swiglu ? c.mb * 64 : c.mb * 128;    // first output feature of the tile
             const int cb = p.out_cblk ? m0 / p.out_cblk : 0;              // its column block (output map dim 3)
             const int c0o = m0 - cb * p.out_cblk;
@@ -930,31 +931,37 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // gate + residual of the first columns are fetched while the accumulator fills
             GateCursor gcur{nullptr, 0};
             float ga[16], xa[16], gb[16], xb[16];
-            if (Epi<EK>::gate && tma_gate && gtile && threadIdx.x == 64) {
-                // the gate rows this CTA will read, into L2 while the accumulator fills (the
-                // per-token gate planes are not L2-resident)
-                int lo = 0, hi = e.ncols;
-                if (p.csplit) { lo = slice_lo(srank, p.BN, p.splits); hi = min(slice_lo(srank + 1, p.BN, p.splits), e.ncols); }
-                for (int t = lo + 32; t < hi; t += 16) tma_prefetch_l2_4d(&tmG, m0, c.t0 + t, c.b, 0);
-            }
-            if (Epi<EK>::gate && p.splits == 1) {
-                if (tma) {
-                    if (!gtile) {                                         // gate rows walked by a cursor
+            // (GATE_RESID) the gate rows this CTA will read, into L2; the first gate / residual
+            // tiles of a whole-tile epilogue in flight
+            const auto gate_prologue = [&]() {
+                if (Epi<EK>::gate && tma_gate && gtile && threadIdx.x == 64) {
+                    // (the per-token gate planes are not L2-resident)
+                    int lo = 0, hi = e.ncols;
+                    if (p.csplit) { lo = slice_lo(srank, p.BN, p.splits); hi = min(slice_lo(srank + 1, p.BN, p.splits), e.ncols); }
+                    for (int t = lo + 32; t < hi; t += 16) tma_prefetch_l2_4d(&tmG, m0, c.t0 + t, c.b, 0);
+                }
+                if (Epi<EK>::gate && whole) {
+                    if (tma) {
+                        if (!gtile) {                                         // gate rows walked by a cursor
+                            const long long grow = e.row_base / p.gate_div;
+                            gcur.g = p.gate + grow * p.ldg + e.m;
+                            gcur.gpos = (int)(e.row_base - grow * p.gate_div);
+                        }
+                        if (threadIdx.x == 64 && gtile) {
+                            for (int s2 = 0; s2 < 2 && s2 < nsteps; ++s2, ++gl)
+                                gate_issue(&tmG, ebar, ebuf, gl, m0, c.t0 + 16 * s2, c.b);
+                        }
+                    } else {
                         const long long grow = e.row_base / p.gate_div;
                         gcur.g = p.gate + grow * p.ldg + e.m;
                         gcur.gpos = (int)(e.row_base - grow * p.gate_div);
+                        gate_load16(p, e, 0, gcur, ga, xa);
                     }
-                    if (threadIdx.x == 64 && gtile) {
-                        for (int s2 = 0; s2 < 2 && s2 < nsteps; ++s2, ++gl)
-                            gate_issue(&tmG, ebar, ebuf, gl, m0, c.t0 + 16 * s2, c.b);
-                    }
-                } else {
-                    const long long grow = e.row_base / p.gate_div;
-                    gcur.g = p.gate + grow * p.ldg + e.m;
-                    gcur.gpos = (int)(e.row_base - grow * p.gate_div);
-                    gate_load16(p, e, 0, gcur, ga, xa);
                 }
-            }
+            };
+            // while the accumulator fills (a gathering split learns only afterwards whether it
+            // finishes the tile)
+            if (!p.gather) gate_prologue();
             float2 rcs[32];                                               // QKV: RoPE (cos, sin) of a chunk
             if (Epi<EK>::qkv && p.rope && c.mb * 128 < 2 * p.hidden)
                 rope_load(p, e, c, 0, (c.mb * 128 - (c.mb * 128 / p.hidden) * p.hidden + ml) & 63, rcs);
@@ -963,7 +970,73 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 break;
             tc_fence_after();
             const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + buf * 256;
-            if (p.splits == 1) {
+            if (p.gather) {
+                // Split-K through the global workspace, one tile per CTA (the operand stages are
+                // idle now). Every split but the last to complete the tile stores its partial tile
+                // and leaves; the last one (it skips its own store when the others are all in
+                // already) brings the other partials into its stages with bulk copies, adds them
+                // to its accumulator in TMEM in split order (the same sum as the reducer of the
+                // workspace path) and finishes the tile as an unsplit one.
+                int * ctr = p.counters + c.otile;
+                if (threadIdx.x == 64) *s_last = ld_acquire_gpu(ctr) == p.splits - 1 ? 2 : 0;
+                epi_bar();
+                const bool early = *s_last == 2;
+                if (!early) {
+                    float * wsp = p.ws + ((size_t)(c.otile * p.splits + c.split) * p.BN) * 128 + ml;
+                    for (int j0 = 0; j0 < p.BN; j0 += 32) {
+                        float v[32];
+                        tmem_ld32(trow + j0, v);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (j0 + j < p.BN) __stcg(wsp + (size_t)(j0 + j) * 128, v[j]);
+                    }
+                    __threadfence();
+                    epi_bar();
+                    if (threadIdx.x == 64) *s_last = atomicAdd(ctr, 1) == p.splits - 1 ? 1 : 0;
+                    epi_bar();
+                }
+                if (*s_last == 0) {            // another split finishes this tile
+                    release_acc(buf);
+                    epi_bar();                 // every thread has read s_last
+                    continue;
+                }
+                if (threadIdx.x == 64) {
+                    __threadfence();           // acquire the other splits' partial tiles ...
+                    fence_proxy_async_all();   // ... for the bulk copies
+                    *ctr = 0;                  // ready for the next launch
+                    mbar_arrive_expect_tx(&cbar[0], (uint32_t)(p.splits - 1) * (uint32_t)p.BN * 512u);
+                    for (int sp = 0, k = 0; sp < p.splits; ++sp)
+                        if (sp != c.split)
+                            bulk_load_g2s(smem + (size_t)(k++) * p.BN * 512,
+                                          p.ws + ((size_t)(c.otile * p.splits + sp) * p.BN) * 128,
+                                          (uint32_t)p.BN * 512u, &cbar[0]);
+                }
+                if (!__all_sync(0xffffffffu, mbar_wait(&cbar[0], 0, s_abort, p.err, DEV_TIMEOUT_FULL))) {
+                    release_acc(buf);
+                    break;
+                }
+                const float * parts = reinterpret_cast<const float *>(smem);   // [splits - 1][BN][128]
+                for (int j0 = 0; j0 < p.BN; j0 += 16) {
+                    float own[16], a[16];
+                    tmem_ld16(trow + j0, own);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) a[j] = 0.f;
+                    for (int sp = 0, k = 0; sp < p.splits; ++sp) {
+                        if (sp == c.split) {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) a[j] += own[j];
+                        } else {
+                            const float * src = parts + ((size_t)(k++) * p.BN + j0) * 128 + ml;
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) a[j] += src[j * 128];
+                        }
+                    }
+                    tmem_st16(trow + j0, a);
+                }
+                tmem_wait_st();
+                gate_prologue();
+            }
+            if (whole) {
                 bool failed = false;
                 if (Epi<EK>::gate && tma) {
                     // gate tiles of 16 tokens by TMA two steps ahead, residual updates by TMA
@@ -1242,6 +1315,14 @@ static bool cluster_split_enabled() {
     const char * e = getenv("TSD_NO_CLUSTER_SPLIT");
     return !(e && *e && *e != '0');
 }
+// Workspace split-K in which the split that completes a tile last gathers the other partial
+// tiles into its operand stages (one tile per CTA; the stages hold splits - 1 partials).
+// TSD_NO_GATHER_SPLIT=1 leaves the reduction to the last split's reducer reading the workspace.
+static bool gather_split_ok(int bn, int sp) {
+    const char * e = getenv("TSD_NO_GATHER_SPLIT");
+    if (e && *e && *e != '0') return false;
+    return (long long)(sp - 1) * bn * 512 <= (long long)kStageArea;
+}
 // Every feasible (BN, splits, pair), cheapest first by the model.
 static std::vector<TileChoice> tile_choices(int S, int nbatch, int mblocks, int nkb, int num_sms, int max_splits,
                                             long long ws_floats, int n_counters, bool allow_cluster, bool allow_pair,
@@ -1287,7 +1368,13 @@ static std::vector<TileChoice> tile_choices(int S, int nbatch, int mblocks, int 
                 const double t_sm = kb * std::max(t_stage / kpb, kb_bytes / 110.0);
                 const double t_l2 = (double)wave_ctas * tile_bytes / 12000.0;
                 const double epi = bn * 128.0 * 4.0 / 20.0;
-                const double reduce = sp == 1 ? 0.0 : cluster ? 2000.0 + bn * 512.0 * 2.0 / 100.0 : 40000.0;
+                // workspace split-K: the last split reduces alone (~40000 cycles), or, with one tile
+                // per CTA, gathers the partials by bulk copy (~3000 cycles + ~5 per partial column)
+                // and then runs the whole tile's epilogue, which a cluster split-K shares out among
+                // the splits (measured: the gathering form of a tiling trails its cluster form)
+                const bool gather = sp > 1 && !cluster && !pair && ctas <= num_sms && gather_split_ok(bn, sp);
+                const double reduce = sp == 1 ? 0.0 : cluster ? 2000.0 + bn * 512.0 * 2.0 / 100.0
+                                                    : gather ? 3000.0 + 5.0 * sp * bn + epi * (sp - 1) : 40000.0;
                 const double cost = (double)waves * (std::max(t_sm, t_l2) + 3000.0) + epi + reduce;
                 out.push_back({cost, bn, sp, pair});
             }
@@ -1390,6 +1477,8 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
         if (p.pair && !p.csplit) g = std::min<long long>(g, 2ll * max_active_clusters(2)) & ~1ll;   // whole pairs, co-resident
         L.grid = dim3((unsigned)g, 1, 1);
     }
+    // workspace split-K with one tile per CTA: the last split gathers the partials (gather_split_ok)
+    p.gather = p.splits > 1 && !p.csplit && !p.pair && tiles <= (long long)L.grid.x && gather_split_ok(p.BN, p.splits);
     if (q8_scales) {
         // int8 plane: 64 x 128 boxes (64-byte rows, no swizzle); scales: 128 rows x 2 blocks
         if (!make_tmap_2d(&L.tmA, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K_in, (uint64_t)M, (uint64_t)K_in, 64,

@@ -58,6 +58,8 @@ struct GemmParams {
     int csplit;        // split-K through the cluster's shared memory (one wave; cluster = the splits of a tile)
     int pair;          // CTA pairs (cta_group::2): 256 weight rows x BN tokens per pair, each CTA loading its
                        // 128 rows and half the tokens; m-blocks even, no Q8_0 A, tile walk m-block-major
+    int gather;        // split-K through the global workspace with one tile per CTA: the split that completes
+                       // a tile last gathers the other partials into its idle operand stages
     // EPI_QKV: W rows are [Q | K | V] (H each, feature = head * 64 + d); out row = item * s_item + t
     __half * q_out, * k_out, * v_out;   // [item][nh][Sj][64], this stream's tokens at s_off
     const float * qg, * kg;             // RMSNorm gains [64]

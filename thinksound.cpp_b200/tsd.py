@@ -352,10 +352,11 @@ GEMM_STATIC_WS_FLOATS, GEMM_STATIC_COUNTERS = 2097152, 8192   # include/tsd_ops.
 
 
 def op_gemm_plan(M, K_in, taps, nbatch, S, max_splits=8, ws_floats=0, n_counters=0):
-    """The tiling tsd_op_gemm chooses for a shape: dict(BN, splits, pair, csplit, ws_floats)."""
-    out = (ctypes.c_int64 * 5)()
+    """The tiling tsd_op_gemm chooses for a shape: dict(BN, splits, pair, csplit, ws_floats, gather)."""
+    out = (ctypes.c_int64 * 6)()
     check("tsd_op_gemm_plan", lib().tsd_op_gemm_plan(M, K_in, taps, nbatch, S, max_splits, ws_floats, n_counters, out))
-    return dict(BN=int(out[0]), splits=int(out[1]), pair=int(out[2]), csplit=int(out[3]), ws_floats=int(out[4]))
+    return dict(BN=int(out[0]), splits=int(out[1]), pair=int(out[2]), csplit=int(out[3]), ws_floats=int(out[4]),
+                gather=int(out[5]))
 
 
 def op_gemv(W, ggml_type, W2, M, K, x, ldx, N, bias, act, round_bf16, y, y_bf16, ldy, stream=0):
