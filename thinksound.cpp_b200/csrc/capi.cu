@@ -34,9 +34,15 @@ int make_stream(tsd_model * h) {
 
 // Reads and clears the device error word; maps it to a status.
 int check_device(Model & m, cudaStream_t st) {
-    TSD_CUDA_TRY(cudaStreamSynchronize(st));
     int e = 0;
-    TSD_CUDA_TRY(cudaMemcpy(&e, m.d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (m.h_err) {     // the error word travels with the call's last copy: one synchronisation
+        TSD_CUDA_TRY(cudaMemcpyAsync(m.h_err, m.d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+        TSD_CUDA_TRY(cudaStreamSynchronize(st));
+        e = *m.h_err;
+    } else {
+        TSD_CUDA_TRY(cudaStreamSynchronize(st));
+        TSD_CUDA_TRY(cudaMemcpy(&e, m.d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    }
     if (e) {
         fprintf(stderr, "tsd: device error word %d (a bounded wait expired)\n", e);
         cudaMemset(m.d_err, 0, sizeof(int));
@@ -62,16 +68,35 @@ struct Inputs {
     const float * latent, * t, * clip_f, * sync_f, * text_f, * t5, * gtext;
 };
 
-int stage_inputs(Model & m, Plan & p, const Inputs & in, cudaStream_t st) {
+// Copies the inputs into the plan's buffers in the order the forward consumes them (input groups
+// of runtime.h). overlap: the caller waits for the whole forward before it returns (so no later
+// call can record the group events while a graph still waits on them): the copies run on the
+// plan's copy stream after everything already queued on st, and each group records its event,
+// on which the captured graph's lanes wait. Otherwise the copies are ordered on st and the group
+// events are left as they are (completed, or never recorded: waits on them pass).
+int stage_inputs(Model & m, Plan & p, const Inputs & in, cudaStream_t st, bool overlap = false) {
     const Shape & s = p.sh;
     const size_t B = (size_t)s.B;
-    TSD_CUDA_TRY(cudaMemcpyAsync(p.lat_in, in.latent, B * m.L * s.T * 4, cudaMemcpyDefault, st));
-    TSD_CUDA_TRY(cudaMemcpyAsync(p.t_in, in.t, B * 4, cudaMemcpyDefault, st));
-    TSD_CUDA_TRY(cudaMemcpyAsync(p.clip_in, in.clip_f, B * s.clip_S * m.clip_dim * 4, cudaMemcpyDefault, st));
-    TSD_CUDA_TRY(cudaMemcpyAsync(p.sync_in, in.sync_f, B * s.sync_S * m.sync_dim * 4, cudaMemcpyDefault, st));
-    if (s.text_S) TSD_CUDA_TRY(cudaMemcpyAsync(p.text_in, in.text_f, B * s.text_S * m.text_dim * 4, cudaMemcpyDefault, st));
-    if (s.t5_S) TSD_CUDA_TRY(cudaMemcpyAsync(p.t5_in, in.t5, B * s.t5_S * m.t5_dim * 4, cudaMemcpyDefault, st));
-    TSD_CUDA_TRY(cudaMemcpyAsync(p.gtext_in, in.gtext, B * m.text_dim * 4, cudaMemcpyDefault, st));
+    overlap = overlap && st && p.copy_st;
+    cudaStream_t cs = st;
+    if (overlap) {
+        TSD_CUDA_TRY(cudaEventRecord(p.prev_done, st));
+        TSD_CUDA_TRY(cudaStreamWaitEvent(p.copy_st, p.prev_done, 0));
+        cs = p.copy_st;
+    }
+    const auto group_done = [&](int g) { return overlap ? cudaEventRecord(p.in_ev[g], cs) : cudaSuccess; };
+    TSD_CUDA_TRY(cudaMemcpyAsync(p.lat_in, in.latent, B * m.L * s.T * 4, cudaMemcpyDefault, cs));
+    TSD_CUDA_TRY(cudaMemcpyAsync(p.t_in, in.t, B * 4, cudaMemcpyDefault, cs));
+    TSD_CUDA_TRY(group_done(IN_LAT));
+    TSD_CUDA_TRY(cudaMemcpyAsync(p.sync_in, in.sync_f, B * s.sync_S * m.sync_dim * 4, cudaMemcpyDefault, cs));
+    TSD_CUDA_TRY(group_done(IN_SYNC));
+    TSD_CUDA_TRY(cudaMemcpyAsync(p.clip_in, in.clip_f, B * s.clip_S * m.clip_dim * 4, cudaMemcpyDefault, cs));
+    TSD_CUDA_TRY(group_done(IN_CLIP));
+    if (s.text_S) TSD_CUDA_TRY(cudaMemcpyAsync(p.text_in, in.text_f, B * s.text_S * m.text_dim * 4, cudaMemcpyDefault, cs));
+    if (s.t5_S) TSD_CUDA_TRY(cudaMemcpyAsync(p.t5_in, in.t5, B * s.t5_S * m.t5_dim * 4, cudaMemcpyDefault, cs));
+    TSD_CUDA_TRY(group_done(IN_TEXT));
+    TSD_CUDA_TRY(cudaMemcpyAsync(p.gtext_in, in.gtext, B * m.text_dim * 4, cudaMemcpyDefault, cs));
+    TSD_CUDA_TRY(group_done(IN_GTEXT));
     return TSD_OK;
 }
 
@@ -229,7 +254,8 @@ int tsd_forward_batched(tsd_model * h, int B, const float * latent, int64_t T, c
     Plan * p = nullptr;
     int rc = get_plan(m, Shape{B, (int)T, (int)clip_S, (int)sync_S, (int)text_S, (int)t5_S}, &p);
     if (rc) return rc;
-    rc = stage_inputs(m, *p, Inputs{latent, t, clip_f, sync_f, text_f, t5, global_text}, h->stream);
+    // this call returns only after the forward (check_device): the copies may overlap it
+    rc = stage_inputs(m, *p, Inputs{latent, t, clip_f, sync_f, text_f, t5, global_text}, h->stream, !dbg);
     if (rc) return rc;
     rc = plan_run(m, *p, h->stream, dbg, ud);
     if (rc) return rc;

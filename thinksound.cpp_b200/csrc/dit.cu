@@ -21,6 +21,10 @@ Plan::~Plan() {
     for (cudaStream_t q : side)
         if (q) cudaStreamDestroy(q);
     for (cudaEvent_t e : events) cudaEventDestroy(e);
+    if (copy_st) cudaStreamDestroy(copy_st);
+    for (cudaEvent_t e : in_ev)
+        if (e) cudaEventDestroy(e);
+    if (prev_done) cudaEventDestroy(prev_done);
     for (void * p : allocs) cudaFree(p);
 }
 
@@ -106,6 +110,17 @@ struct Builder {
         o.kind = OP_COPY;
         o.launches = 0;
         o.label = sync == 1 ? "fork" : "join";
+        P.ops.push_back(std::move(o));
+    }
+    // This lane's next ops read input group `g` (graph replay: wait for its copy to land).
+    void wait_input(int g) {
+        Op o;
+        o.sync = 3;
+        o.input = g;
+        o.kind = OP_COPY;
+        o.launches = 0;
+        o.lane = lane;
+        o.label = "wait input";
         P.ops.push_back(std::move(o));
     }
     void copy(void * dst, const void * src, size_t bytes) {
@@ -416,6 +431,7 @@ struct Builder {
         mark(1);
         // ---- audio_input_proj (mmdit.cpp:150-155) ----
         tag = "pre.audio";
+        wait_input(IN_LAT);
         op([=](cudaStream_t st) { return latent_to_tokens(lat_in, B, L, T, lat_tok, st); });
         gemm(m.ap0, lat_tok, B, T, L, (long long)T * L, EPI_STORE, ACT_SILU, a1, 1, H);
         gemm(m.ap13, a1, B, T, H, (long long)T * H, EPI_SWIGLU, ACT_NONE, hbuf, 1, F, nullptr, 0, nullptr, 0, 1, 1);
@@ -431,6 +447,7 @@ struct Builder {
         // ---- clip (mmdit.cpp:164-167) ----
         tag = "pre.clip";
         lane = 1;
+        wait_input(IN_CLIP);
         inv = true;
         op([=](cudaStream_t st) { return cast_f32_bf16(clip_in, (long long)B * cS * clip_dim, clip_tok, st); });
         gemm(m.cp0, clip_tok, B, cS, m.clip_dim, (long long)cS * m.clip_dim, EPI_STORE, ACT_SILU, a1_l[1], 1, H);
@@ -442,6 +459,7 @@ struct Builder {
         lane = 0;
         // ---- sync (mmdit.cpp:168-177) ----
         tag = "pre.sync";
+        wait_input(IN_SYNC);
         inv = true;
         op([=](cudaStream_t st) { return sync_prep(sync_in, B, yS, sync_dim, sync_pe, sync_tok, st); });
         gemm(m.sp0, sync_tok, B, yS, m.sync_dim, (long long)yS * m.sync_dim, EPI_STORE, ACT_SILU, a1, 1, H);
@@ -451,6 +469,7 @@ struct Builder {
         // ---- text (mmdit.cpp:178-183) ----
         tag = "pre.text";
         lane = 2;
+        wait_input(IN_TEXT);
         inv = true;
         op([=](cudaStream_t st) {
             return text_prep(text_in, text_S, text_dim, t5_in, t5_S, t5_dim, B, text_tok, st);
@@ -465,6 +484,7 @@ struct Builder {
         mark(2);
         // ---- conditioning vectors (mmdit.cpp:184-200) ----
         tag = "pre.cond";
+        wait_input(IN_GTEXT);
         inv = true;
         gemv(m.tcp, P.gtext_in, m.text_dim, B, ACT_NONE, text_fc, H);
         snap("text_fc", text_fc, (long long)B * H);
@@ -649,12 +669,28 @@ int plan_build(Model & m, const Shape & sh, std::unique_ptr<Plan> & out) {
     Builder b{m, *p};
     b.build();
     if (b.rc) return b.rc;
+    // overlapped input staging: the copy stream and the per-group events exist before the first
+    // capture, so every captured graph holds the waits on them
+    TSD_CUDA_TRY(cudaStreamCreateWithFlags(&p->copy_st, cudaStreamNonBlocking));
+    for (cudaEvent_t & e : p->in_ev) TSD_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    TSD_CUDA_TRY(cudaEventCreateWithFlags(&p->prev_done, cudaEventDisableTiming));
     out = std::move(p);
     return TSD_OK;
 }
 
+// Op-by-op execution on one stream: the inputs of every group have landed first.
+static cudaError_t wait_all_inputs(Plan & p, cudaStream_t st) {
+    for (cudaEvent_t e : p.in_ev)
+        if (e) {
+            const cudaError_t r = cudaStreamWaitEvent(st, e, 0);
+            if (r != cudaSuccess) return r;
+        }
+    return cudaSuccess;
+}
+
 int plan_profile(Model & m, Plan & p, cudaStream_t st, std::vector<float> & ms) {
     (void)m;
+    TSD_CUDA_TRY(wait_all_inputs(p, st));
     std::vector<cudaEvent_t> ev(p.ops.size() + 1);
     for (auto & e : ev) TSD_CUDA_TRY(cudaEventCreate(&e));
     int rc = TSD_OK;
@@ -678,6 +714,7 @@ int plan_profile(Model & m, Plan & p, cudaStream_t st, std::vector<float> & ms) 
 int plan_run(Model & m, Plan & p, cudaStream_t st, tsd_dbg_fn dbg, void * ud, bool reuse_cond, tsd_inject_fn inject) {
     (void)m;
     if (dbg || inject) {
+        TSD_CUDA_TRY(wait_all_inputs(p, st));
         std::vector<float> h;
         for (const Op & o : p.ops) {
             if (o.fn) TSD_CUDA_TRY(o.fn(st));
@@ -707,6 +744,7 @@ int plan_run(Model & m, Plan & p, cudaStream_t st, tsd_dbg_fn dbg, void * ud, bo
         TSD_CUDA_TRY(cudaStreamIsCapturing(st, &cs));
         const bool can_capture = (st != nullptr) && cs == cudaStreamCaptureStatusNone;
         if (!can_capture) {
+            TSD_CUDA_TRY(wait_all_inputs(p, st));
             for (const Op & o : p.ops)
                 if (o.fn && !(reuse_cond && o.invariant)) TSD_CUDA_TRY(o.fn(st));
             return TSD_OK;
@@ -736,6 +774,10 @@ int plan_run(Model & m, Plan & p, cudaStream_t st, tsd_dbg_fn dbg, void * ud, bo
                     if (e == cudaSuccess) e = cudaStreamWaitEvent(st, p.events[ev + l], 0);
                 }
                 ev += kSideLanes;
+            } else if (o.sync == 3) {     // input group: an external wait on its copy event
+                if (p.in_ev[o.input])
+                    e = cudaStreamWaitEvent(o.lane == 0 ? st : p.side[o.lane - 1], p.in_ev[o.input],
+                                            cudaEventWaitExternal);
             } else if (!(reuse_cond && o.invariant)) {
                 e = o.fn(o.lane == 0 ? st : p.side[o.lane - 1]);
             }

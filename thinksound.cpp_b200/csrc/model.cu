@@ -98,6 +98,7 @@ Model::~Model() {
     for (auto & kv : raw)
         if (kv.second.d) cudaFree(kv.second.d);
     for (void * p : allocs) cudaFree(p);
+    if (h_err) cudaFreeHost(h_err);
 }
 
 void * Model::dalloc(size_t bytes) {
@@ -495,6 +496,7 @@ int model_finalize(Model & m) {
     m.d_err = reinterpret_cast<int *>(m.dalloc(256));
     if (!m.d_err) return TSD_ERR_CUDA;
     TSD_CUDA_TRY(cudaMemset(m.d_err, 0, 256));
+    if (!m.h_err) TSD_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void **>(&m.h_err), sizeof(int), cudaHostAllocDefault));
     m.finalized = true;
     return TSD_OK;
 }

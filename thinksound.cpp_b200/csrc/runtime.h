@@ -96,6 +96,7 @@ struct Model {
     std::vector<std::array<StreamW, 3>> joint;
     std::vector<StreamW> fused;
     int * d_err = nullptr;
+    int * h_err = nullptr;     // pinned host copy of *d_err, read after each synchronous call
     std::unique_ptr<Plan> plan;
     HeadParallel hpar;
 
@@ -131,15 +132,21 @@ struct Op {
     double flops = 0, bytes = 0;   // algorithmic work of the op
     // Graph replay only: the op's lane (0 = the caller's stream, 1..kSideLanes = side streams).
     // Marker ops (fn empty): sync 1 = fork (side lanes wait for lane 0), 2 = join (lane 0 waits
-    // for the side lanes). Op-by-op execution runs everything in order on one stream.
+    // for the side lanes), 3 = this lane waits for input group `input` (Plan::in_ev) to land.
+    // Op-by-op execution runs everything in order on one stream.
     int lane = 0;
     int sync = 0;
+    int input = 0;
     // Conditioning-only: the op reads only the staged clip / sync / text / global inputs (or
     // other conditioning-only ops' outputs) and writes buffers nothing else writes, so a replay
     // with unchanged conditioning inputs may skip it (the sampler's steps after the first).
     bool invariant = false;
 };
 constexpr int kSideLanes = 2;
+// Input groups of a forward, in the order the plan's first ops consume them: each has its own
+// copy-completion event, so that a graph replay starts each input chain as soon as its inputs
+// have landed instead of after all of them.
+enum InputGroup : int { IN_LAT = 0, IN_SYNC = 1, IN_CLIP = 2, IN_TEXT = 3, IN_GTEXT = 4, kInputGroups = 5 };
 
 struct Shape {
     int B, T, clip_S, sync_S, text_S, t5_S;
@@ -163,6 +170,12 @@ struct Plan {
     cudaStream_t graph_stream[2] = {};
     cudaStream_t side[kSideLanes] = {};        // side lanes of the captured graph
     std::vector<cudaEvent_t> events;           // fork / join events (capture only)
+    // Overlapped input staging (stage_inputs with a host-synchronised caller): the copies run on
+    // copy_st, each group recording in_ev[group]; the captured graph's lanes wait on those events
+    // (external event waits), so the first kernels start under the later groups' copies.
+    cudaStream_t copy_st = nullptr;
+    cudaEvent_t in_ev[kInputGroups] = {};
+    cudaEvent_t prev_done = nullptr;           // the caller's stream before the copies
     ~Plan();
 };
 
