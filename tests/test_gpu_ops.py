@@ -147,6 +147,50 @@ def test_gemm_split_k_store_and_swiglu(mode):
     assert int(counters.abs().sum()) == 0
 
 
+@pytest.mark.parametrize("mode,gate_div", [(tsd.EPI_STORE, 1), (tsd.EPI_SWIGLU, 1), (tsd.EPI_GATE_RESID, 1),
+                                           (tsd.EPI_GATE_RESID, 0)])
+@pytest.mark.parametrize("S,nb,taps", [(72, 2, 3), (72, 5, 3), (40, 7, 7), (100, 3, 1)])
+def test_gemm_multi_item_tiles(monkeypatch, S, nb, taps, mode, gate_div):
+    """Several short batch items side by side in one token tile (each weight tile read once for all
+    of them; the clip stream's 72-token items): the same sums in the same K order as one item per
+    tile, so bit-identical to it (no split-K on either side), and within 1e-5 of the f32
+    reference. nb = 5 / 7 leave the last tile of items partly empty."""
+    M, K = 512, 512
+    W = rnd(M, taps * K, scale=0.03)
+    X = rnd(nb, S, K)
+    bias = torch.randn(M, device=DEV)
+    gdiv = gate_div if gate_div else S
+    gate = torch.randn(nb * S // gdiv, M, device=DEV)
+    x0 = torch.randn(nb, S, M, device=DEV)
+    Fo = M // 2 if mode == tsd.EPI_SWIGLU else M
+    out = {}
+    for form in ("multi", "single"):
+        monkeypatch.delenv("TSD_FORCE_MULTI_ITEM", raising=False)
+        monkeypatch.delenv("TSD_NO_MULTI_ITEM", raising=False)
+        monkeypatch.setenv("TSD_FORCE_MULTI_ITEM" if form == "multi" else "TSD_NO_MULTI_ITEM", "1")
+        plan = tsd.op_gemm_plan(M, K, taps, nb, S, 1)
+        assert (plan["BN"] > (S + 15) // 16 * 16) == (form == "multi"), (form, plan)
+        if mode == tsd.EPI_GATE_RESID:
+            x = x0.clone()
+            tsd.op_gemm(W, M, K, taps, taps // 2, X, nb, S, K, S * K, mode, 0, bias, None, 0, 0, resid=x, ldr=M,
+                        gate=gate, ldg=M, gate_div=gdiv, max_splits=1)
+        else:
+            x = torch.empty(nb, S, Fo, device=DEV)
+            tsd.op_gemm(W, M, K, taps, taps // 2, X, nb, S, K, S * K, mode, 0, bias if mode == tsd.EPI_STORE else None,
+                        x, 0, Fo, max_splits=1)
+        out[form] = x
+    torch.cuda.synchronize()
+    acc = ref_gemm(W, X, taps, taps // 2)
+    if mode == tsd.EPI_GATE_RESID:
+        ref = x0 + gate.view(nb, S // gdiv, 1, M).expand(nb, S // gdiv, gdiv, M).reshape(nb, S, M) * (acc + bias)
+    elif mode == tsd.EPI_STORE:
+        ref = acc + bias
+    else:
+        ref = torch.nn.functional.silu(acc[..., 0::2]) * acc[..., 1::2]
+    assert rel(out["multi"], ref) < 1e-5
+    assert torch.equal(out["multi"], out["single"])
+
+
 @pytest.mark.parametrize("gather", [1, 0])
 @pytest.mark.parametrize("mode,gate_div", [(tsd.EPI_GATE_RESID, 1), (tsd.EPI_GATE_RESID, 0), (tsd.EPI_STORE, 1),
                                            (tsd.EPI_SWIGLU, 1)])

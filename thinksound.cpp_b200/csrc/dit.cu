@@ -194,10 +194,12 @@ struct Builder {
                 const GemmParams & q = L.p;   // same epilogue, new tiling
                 GemmParams & cp = C.p;
                 const int BN = cp.BN, nt = cp.n_tiles, sp = cp.splits, cs = cp.csplit, order = cp.order, st = cp.stages;
-                const int aq8 = cp.a_q8, pr = cp.pair, kpb = cp.kpb;
+                const int aq8 = cp.a_q8, pr = cp.pair, kpb = cp.kpb, ga = cp.gather, ipt = cp.ipt, bni = cp.bni;
+                const int groups = cp.groups;
                 cp = q;
                 cp.BN = BN; cp.n_tiles = nt; cp.splits = sp; cp.csplit = cs; cp.order = order; cp.stages = st;
                 cp.a_q8 = aq8; cp.pair = pr; cp.kpb = kpb;   // the tiling fields that go with C's tensor maps
+                cp.gather = ga; cp.ipt = ipt; cp.bni = bni; cp.groups = groups;
                 gemm_finalize(C);
                 const float t = time_gemm(C);
                 if (tune_log) fprintf(stderr, " | BN=%d sp=%d pair=%d %.1f us", BN, sp, pr, t * 1000.f);

@@ -121,7 +121,7 @@ extern "C" int tsd_op_gemm_static(const void * W, int M, int K_in, int taps, int
                    kStaticWsFloats, kStaticCounters, /*allow_cluster=*/true))
         return TSD_ERR_ARG;
     const long long need_ws = gemm_ws_floats(L);
-    const long long need_cnt = need_ws ? (long long)L.p.mblocks * L.p.nbatch * L.p.n_tiles : 0;
+    const long long need_cnt = need_ws ? (long long)L.p.mblocks * L.p.groups * L.p.n_tiles : 0;
     if (need_ws > kStaticWsFloats || need_cnt > kStaticCounters) {   // the planner keeps plans within the limits
         fprintf(stderr,
                 "tsd_op_gemm_static: the plan needs %lld partial floats and %lld counters, beyond the static scratch "

@@ -40,6 +40,8 @@ constexpr int kEBufBytes = 16384;          // epilogue staging buffer (x2): 32 t
 constexpr int kSmemBytes = kStageArea + 2 * kEBufBytes + 1024 /*align*/ + 256 /*barriers*/;
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Token columns the epilogue finishes at a time: the tile, or one item of a multi-item tile.
+__device__ __forceinline__ int epi_bn(const GemmParams & p) { return p.ipt > 1 ? p.bni : p.BN; }
 
 struct TileCoord { int mb, b, t0, kb_begin, kb_end, split, otile; };
 
@@ -50,7 +52,7 @@ __device__ __forceinline__ TileCoord decode(const GemmParams & p, int t, int nkb
     TileCoord c;
     int nt;
     if (p.order == 0) {           // m-block-major: consecutive tiles share the weight tile
-        const int per_mb = p.nbatch * p.n_tiles * p.splits;
+        const int per_mb = p.groups * p.n_tiles * p.splits;
         c.mb = t / per_mb;
         const int rem = t - c.mb * per_mb;
         if (p.pair) c.mb = 2 * c.mb + prank;
@@ -59,13 +61,14 @@ __device__ __forceinline__ TileCoord decode(const GemmParams & p, int t, int nkb
     } else {                      // token-tile-major: consecutive tiles share the activation tile
         c.mb = t % p.mblocks;
         const int r = t / p.mblocks;
-        const int ntt = p.nbatch * p.n_tiles;
+        const int ntt = p.groups * p.n_tiles;
         nt = r % ntt;
         c.split = r / ntt;
     }
-    c.b = nt / p.n_tiles;
-    c.t0 = (nt - c.b * p.n_tiles) * p.BN;
-    c.otile = c.mb * (p.nbatch * p.n_tiles) + nt;     // output tile (all K splits of it)
+    const int g = nt / p.n_tiles;                     // batch group (one item unless ipt > 1)
+    c.b = g * p.ipt;                                  // first item of the tile
+    c.t0 = (nt - g * p.n_tiles) * p.BN;               // (0 in a multi-item tile: n_tiles = 1)
+    c.otile = c.mb * (p.groups * p.n_tiles) + nt;     // output tile (all K splits of it)
     c.kb_begin = (int)((long long)nkb * c.split / p.splits);
     c.kb_end = (int)((long long)nkb * (c.split + 1) / p.splits);
     return c;
@@ -184,7 +187,7 @@ __device__ __forceinline__ void tma_chunk(const GemmParams & p, const CUtensorMa
     if (threadIdx.x == 64) {
         constexpr int rowb = (Epi<EK>::swiglu ? 64 : 128) * (Epi<EK>::bf16 ? 2 : 4);
         tma_store_4d(tmO, sbuf, c0o, t0 + j0, b, cb);
-        if (j0 + 16 < p.BN) tma_store_4d(tmO, sbuf + 16 * rowb, c0o, t0 + j0 + 16, b, cb);
+        if (j0 + 16 < epi_bn(p)) tma_store_4d(tmO, sbuf + 16 * rowb, c0o, t0 + j0 + 16, b, cb);
         bulk_commit();
     }
     ++gc;
@@ -297,7 +300,7 @@ __device__ __forceinline__ void emit_qkv(const GemmParams & p, const EpiCtx & e,
                 const float o = __shfl_xor_sync(0xffffffffu, v[j], 1);
                 v[j] = (d & 1) ? o * cs[j].y + v[j] * cs[j].x : v[j] * cs[j].x - o * cs[j].y;
             }
-            if (j0 + 32 < p.BN) rope_load(p, e, c, j0 + 32, d, cs);
+            if (j0 + 32 < epi_bn(p)) rope_load(p, e, c, j0 + 32, d, cs);
         }
     }
     if (p.epi_tma) {
@@ -318,7 +321,7 @@ __device__ __forceinline__ void emit_qkv(const GemmParams & p, const EpiCtx & e,
             const CUtensorMap * tm = which == 0 ? tmQ : which == 1 ? tmK : tmV;
             const int h0 = (f0 - which * p.hidden) >> 6;
             const int hh = q >> 1, half = q & 1;       // this warp's box: head hh, tokens half * 16 ..
-            if (half == 0 || j0 + 16 < p.BN)
+            if (half == 0 || j0 + 16 < epi_bn(p))
                 tma_store_4d(tm, sbuf + hh * 4096 + half * 2048, 0, c.t0 + j0 + half * 16, h0 + hh, c.b);
             bulk_commit();
         }
@@ -669,7 +672,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int srank = PAIR ? (int)(crank >> 1) : (int)crank;   // cluster split-K: this CTA's split
     const int tile0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
     const int tstep = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
-    const int num_tiles = (PAIR ? p.mblocks >> 1 : p.mblocks) * p.nbatch * p.n_tiles * p.splits;
+    const int num_tiles = (PAIR ? p.mblocks >> 1 : p.mblocks) * p.groups * p.n_tiles * p.splits;
     const int bh = PAIR ? p.BN >> 1 : p.BN;                   // token rows of B this CTA loads
     // one stage: kpb A atoms (bf16 128 x 64, SW128) | kpb B atoms (bh x 64) | Q8_0 path (kpb = 1):
     // int8 tile + scales; a multiple of 1024 bytes, so every stage's SW128 atoms stay aligned
@@ -785,10 +788,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const auto issue_b = [&](int st, int kc, int yb, int b) {
             uint8_t * sb = smem + st * sbytes + kpb * kABytes;
             if (p.a_q8) mbar_arrive_expect_tx(&full[st], b_bytes);
-            if constexpr (PAIR)
+            if constexpr (PAIR) {
                 tma_load_4d_pair(sb, &tmB, mapa_shared(smem_u32(&full[st]), lead), 0, yb, kc, b);
-            else
-                tma_load_4d(sb, &tmB, &full[st], 0, yb, kc, b);
+            } else {
+                // multi-item tile: one box of bni rows x kpb atoms per item, item after item (an item
+                // past the batch reads the fill value zero)
+                for (int i = 0; i < p.ipt; ++i)
+                    tma_load_4d(sb + (size_t)i * kpb * p.bni * 128, &tmB, &full[st], 0, yb, kc, b + i);
+            }
         };
         const int amask = a_parts - 1;                       // a_parts is 1 or 2
         int pre = 0;
@@ -844,6 +851,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (lane == 0 && prank == 0) {
             // ---------------- MMA issuer (a pair's leader issues for both CTAs) ----------------
             const uint32_t idesc = make_idesc_f16(PAIR ? 256 : 128, p.BN, true);
+            const uint32_t idesc_item = make_idesc_f16(128, p.ipt > 1 ? p.bni : p.BN, true);
             const uint16_t pmask = (uint16_t)(3u << lead);
             int it = 0, lt = 0;
             int s = 0;                 // ring slot of `it` and the parity of its fill
@@ -870,6 +878,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         const uint64_t adesc = make_sdesc_sw128(sa + j * kABytes);
                         const uint64_t bdesc = make_sdesc_sw128(sa + kpb * kABytes + j * b_bytes);
                         const uint32_t acc0 = (kb > c.kb_begin || j > 0) ? 1u : 0u;
+                        if constexpr (!PAIR) {   // (no single-CTA MMA in the pair instance)
+                            if (p.ipt > 1) {
+                                // multi-item tile: item i's bni token rows (its own atoms, item-major in
+                                // the stage) into accumulator columns i * bni ..
+                                for (int i = 0; i < p.ipt; ++i) {
+                                    const uint64_t bd = make_sdesc_sw128(sa + kpb * kABytes + (i * kpb + j) * p.bni * 128);
+#pragma unroll
+                                    for (int kk = 0; kk < 4; ++kk)
+                                        umma_f16_ss(dacc + i * p.bni, adesc + 2 * kk, bd + 2 * kk, idesc_item,
+                                                    (acc0 | kk) ? 1u : 0u);
+                                }
+                                continue;
+                            }
+                        }
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk) {
                             if constexpr (PAIR) umma_f16_ss_pair(dacc, adesc + 2 * kk, bdesc + 2 * kk, idesc, (acc0 | kk) ? 1u : 0u);
@@ -909,15 +931,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 else mbar_arrive(&acc_empty[buf]);
             }
         };
+        const int ebn = epi_bn(p);                    // token columns finished at a time
         for (int t = tile0; t < num_tiles; t += tstep, ++lt) {
-            const TileCoord c = decode(p, t, nks, prank);
+            TileCoord c = decode(p, t, nks, prank);      // (a multi-item tile advances c.b per item)
             const int buf = lt & 1;
             EpiCtx e;
             // output feature of this thread (SwiGLU: rows 2i / 2i + 1 are w1 / w3 of feature i)
             e.m = Epi<EK>::swiglu ? c.mb * 64 + (ml >> 1) : c.mb * 128 + ml;
             e.m_ok = e.m < p.m_valid;
             e.bias = (p.bias && e.m_ok && !Epi<EK>::swiglu) ? p.bias[e.m] : 0.f;
-            e.ncols = min(p.BN, p.S - c.t0);
+            e.ncols = min(ebn, p.S - c.t0);
             e.row_base = (long long)c.b * p.S + c.t0;
             e.col = p.out_cblk ? (long long)(e.m / p.out_cblk) * p.out_cstride + e.m % p.out_cblk : e.m;
             const bool whole = p.splits == 1 || p.gather;     // this CTA finishes whole tiles
@@ -926,7 +949,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const int m0 = Epi<EK>::swiglu ? c.mb * 64 : c.mb * 128;    // first output feature of the tile
             const int cb = p.out_cblk ? m0 / p.out_cblk : 0;              // its column block (output map dim 3)
             const int c0o = m0 - cb * p.out_cblk;
-            const int nsteps = p.BN >> 4;                                 // GATE_RESID: 16-token steps
+            const int nsteps = ebn >> 4;                                  // GATE_RESID: 16-token steps
             const bool gtile = p.gate_div == 1;                           // per-token gate (else one per item)
             // gate + residual of the first columns are fetched while the accumulator fills
             GateCursor gcur{nullptr, 0};
@@ -1038,6 +1061,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             }
             if (whole) {
                 bool failed = false;
+                // one pass per item of a multi-item tile (item it in accumulator columns it * bni ..)
+                for (int it = 0; it < p.ipt && !failed; ++it) {
+                if (it > 0) {
+                    if (++c.b >= p.nbatch) break;
+                    e.row_base = (long long)c.b * p.S + c.t0;
+                    gate_prologue();
+                    if (Epi<EK>::qkv && p.rope && c.mb * 128 < 2 * p.hidden)
+                        rope_load(p, e, c, 0, (c.mb * 128 - (c.mb * 128 / p.hidden) * p.hidden + ml) & 63, rcs);
+                }
+                const uint32_t trow_i = trow + (uint32_t)(it * p.bni);
                 if (Epi<EK>::gate && tma) {
                     // gate tiles of 16 tokens by TMA two steps ahead, residual updates by TMA
                     // reduce-add (gate_step)
@@ -1051,7 +1084,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                 if (++gcur.gpos == p.gate_div) { gcur.gpos = 0; gcur.g += p.ldg; }
                             }
                         }
-                        tmem_ld16(trow + 16 * s2, v);
+                        tmem_ld16(trow_i + 16 * s2, v);
                         if (!gate_step(p, e, &tmO, &tmG, gtile, ebar, ebuf, gs, gl, v, gv, ml, m0, c.t0 + 16 * s2,
                                        s2 + 2 < nsteps ? c.t0 + 16 * (s2 + 2) : -1, c.b)) {
                             failed = true;
@@ -1062,16 +1095,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     // The next chunk's TMEM load and its gate / residual loads are in flight
                     // while this chunk's results are stored.
                     uint32_t va[16], vb[16];
-                    tmem_ld16_async(trow, va);
+                    tmem_ld16_async(trow_i, va);
                     tmem_wait_ld(va);
-                    for (int c0 = 0; c0 < p.BN; c0 += 32) {
-                        const bool nb = c0 + 16 < p.BN;
-                        if (nb) { gate_load16(p, e, c0 + 16, gcur, gb, xb); tmem_ld16_async(trow + c0 + 16, vb); }
+                    for (int c0 = 0; c0 < ebn; c0 += 32) {
+                        const bool nb = c0 + 16 < ebn;
+                        if (nb) { gate_load16(p, e, c0 + 16, gcur, gb, xb); tmem_ld16_async(trow_i + c0 + 16, vb); }
                         gate_store16(p, e, c0, va, ga, xa);
                         if (!nb) break;
                         tmem_wait_ld(vb);
-                        const bool na = c0 + 32 < p.BN;
-                        if (na) { gate_load16(p, e, c0 + 32, gcur, ga, xa); tmem_ld16_async(trow + c0 + 32, va); }
+                        const bool na = c0 + 32 < ebn;
+                        if (na) { gate_load16(p, e, c0 + 32, gcur, ga, xa); tmem_ld16_async(trow_i + c0 + 32, va); }
                         gate_store16(p, e, c0 + 16, vb, gb, xb);
                         if (!na) break;
                         tmem_wait_ld(va);
@@ -1079,15 +1112,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 } else {
                     // One call site per epilogue body keeps the instruction footprint small (a
                     // TMEM load is ~50 cycles; prefetching it would double the inlined code).
-                    for (int j0 = 0; j0 < p.BN; j0 += 32) {
+                    for (int j0 = 0; j0 < ebn; j0 += 32) {
                         uint32_t v[32];
-                        tmem_ld32_async(trow + j0, v);
+                        tmem_ld32_async(trow_i + j0, v);
                         tmem_wait_ld(v);
                         if (Epi<EK>::qkv) emit_qkv(p, e, c, j0, v, ml, lane, q, ebuf, nqk, gs, &tmO, &tmG, &tmV, rcs);
                         else if (tma) tma_chunk<EK>(p, &tmO, e, j0, v, ml, lane, ebuf, gs, c0o, cb, c.b, c.t0);
                         else if (Epi<EK>::swiglu) emit_swiglu<EK>(p, e, j0, v, lane);
                         else emit_store<EK>(p, e, j0, v);
                     }
+                }
                 }
                 release_acc(buf);
                 if (failed) break;
@@ -1301,6 +1335,7 @@ static int max_active_clusters(int cs) {
 struct TileChoice {
     double cost;
     int BN, splits, pair;
+    int ipt = 1;       // batch items per token tile (BN = ipt x the item's rows when > 1)
 };
 // CTA pairs (cta_group::2) halve the token bytes each SM draws: a pair computes 256 weight
 // rows x BN tokens, each CTA loading its 128 weight rows and BN / 2 tokens. They need an even
@@ -1323,7 +1358,25 @@ static bool gather_split_ok(int bn, int sp) {
     if (e && *e && *e != '0') return false;
     return (long long)(sp - 1) * bn * 512 <= (long long)kStageArea;
 }
-// Every feasible (BN, splits, pair), cheapest first by the model.
+// Several short batch items in one token tile (TSD_NO_MULTI_ITEM=1: one item per tile).
+static bool multi_item_enabled() {
+    const char * e = getenv("TSD_NO_MULTI_ITEM");
+    return !(e && *e && *e != '0');
+}
+// Rows per item of a multi-item tile for items of S tokens, and whether `ipt` of them fit: the
+// epilogue reads the accumulator of an item in 32-column chunks, so the last item's chunks must
+// stay inside the tile's 256 TMEM columns.
+static int item_rows(int S) { return (S + 15) / 16 * 16; }
+// K blocks per stage of a multi-item tile: two (one box of two atoms per item) while two stages
+// fit, else one.
+static int multi_item_kpb(bool k128, int bn, int nkb) {
+    return (k128 && kStageArea / (2 * (kABytes + 128 * bn)) >= 2 && nkb % 2 == 0 && nkb / 2 >= 2) ? 2 : 1;
+}
+static bool multi_item_fits(int S, int ipt) {
+    const int bni = item_rows(S);
+    return ipt >= 2 && S <= 128 && (ipt - 1) * bni + (bni + 31) / 32 * 32 <= 256;
+}
+// Every feasible (BN, splits, pair, items per tile), cheapest first by the model.
 static std::vector<TileChoice> tile_choices(int S, int nbatch, int mblocks, int nkb, int num_sms, int max_splits,
                                             long long ws_floats, int n_counters, bool allow_cluster, bool allow_pair,
                                             bool k128, bool q8) {
@@ -1380,6 +1433,30 @@ static std::vector<TileChoice> tile_choices(int S, int nbatch, int mblocks, int 
             }
         }
     }
+    // Multi-item tiles (short conv streams: items of <= 128 tokens): ipt items side by side, each
+    // in bni rows, so every weight tile is read once for all of them instead of once per item.
+    // Single CTAs, no split. Per K=16 step one MMA per item (N = bni); the token-tile issuer
+    // sends one box per item (~500 cycles each).
+    if (nbatch >= 2 && multi_item_enabled())
+        for (int ipt = 2; ipt <= nbatch && multi_item_fits(S, ipt); ++ipt) {
+            const int bni = item_rows(S), bn = ipt * bni;
+            const long long otiles = (long long)mblocks * ((nbatch + ipt - 1) / ipt);
+            const long long waves = (otiles + num_sms - 1) / num_sms;
+            const double kb = nkb;
+            const double kb_bytes = 16384.0 + 128.0 * bn;
+            const int kpb = multi_item_kpb(k128 && !q8, bn, nkb);
+            const int nst = std::min(kMaxStages, kStageArea / (kpb * (kABytes + 128 * bn) + (q8 ? kQ8Bytes : 0)));
+            const double ex = 4.0 * kpb * ipt * std::max(65.0, bni / 2.0);
+            // one token box per item and stage; a stage comes back after the load latency (~2550
+            // cycles under load) plus the MMAs that hold it, nst stages in flight
+            const double t_stage = std::max(std::max(std::max(ex, 500.0 * ipt), (2550.0 + ex) / nst), q8 ? 600.0 : 300.0);
+            const double t_sm = kb * std::max(t_stage / kpb, kb_bytes / 110.0);
+            const double t_l2 = (double)std::min<long long>(otiles, num_sms) * kb * kb_bytes / 12000.0;
+            const double epi = bn * 128.0 * 4.0 / 20.0;
+            TileChoice t{(double)waves * (std::max(t_sm, t_l2) + 3000.0) + epi, bn, 1, 0};
+            t.ipt = ipt;
+            out.push_back(t);
+        }
     std::stable_sort(out.begin(), out.end(), [](const TileChoice & a, const TileChoice & b) { return a.cost < b.cost; });
     return out;
 }
@@ -1402,7 +1479,7 @@ int gemm_candidates(int M, int K_in, int taps, int nbatch, int S, int num_sms, i
 
 long long gemm_ws_floats(const GemmLaunch & L) {
     const GemmParams & p = L.p;
-    return p.splits > 1 && !p.csplit ? (long long)p.mblocks * p.nbatch * p.n_tiles * p.splits * p.BN * 128 : 0;
+    return p.splits > 1 && !p.csplit ? (long long)p.mblocks * p.groups * p.n_tiles * p.splits * p.BN * 128 : 0;
 }
 
 static bool make_tmap_4d(CUtensorMap * m, const void * ptr, CUtensorMapDataType dt, int esize, const uint64_t (&d)[4],
@@ -1432,13 +1509,19 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
         if (force_pair == 1)          // the model's best pair choice
             for (const TileChoice & x : c)
                 if (x.pair) { t = x; break; }
+        if (force_bn <= 0 && getenv("TSD_FORCE_MULTI_ITEM"))   // tests: the best multi-item choice, if any
+            for (const TileChoice & x : c)
+                if (x.ipt > 1) { t = x; break; }
         for (const TileChoice & x : c)
             if (force_bn > 0 && x.BN == force_bn && x.splits == force_splits && (force_pair < 0 || x.pair == force_pair)) {
                 t = x;
                 break;
             }
         p.BN = t.BN;
-        p.n_tiles = (S + t.BN - 1) / t.BN;
+        p.ipt = t.ipt;
+        p.bni = t.ipt > 1 ? item_rows(S) : t.BN;
+        p.n_tiles = t.ipt > 1 ? 1 : (S + t.BN - 1) / t.BN;
+        p.groups = (nbatch + t.ipt - 1) / t.ipt;
         p.splits = t.splits;
         p.pair = t.pair;
         p.a_q8 = q8_scales != nullptr;
@@ -1447,11 +1530,12 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
         const int b_atom = (p.pair ? p.BN / 2 : p.BN) * 128;
         const int st2 = kStageArea / (2 * (kABytes + b_atom));
         p.kpb = (!p.a_q8 && K_in % 128 == 0 && st2 >= 3 && nkb % (2 * p.splits) == 0 && nkb / (2 * p.splits) >= 2) ? 2 : 1;
+        if (p.ipt > 1) p.kpb = multi_item_kpb(!p.a_q8 && K_in % 128 == 0, p.BN, nkb);
         p.stages = std::min(kMaxStages, kStageArea / (p.kpb * (kABytes + b_atom) + (p.a_q8 ? kQ8Bytes : 0)));
     }
     if (getenv("TSD_DEBUG_PLAN")) {
-        fprintf(stderr, "tsd plan: M=%d K=%d taps=%d nbatch=%d S=%d -> BN=%d tiles/item=%d splits=%d pair=%d kpb=%d stages=%d | max active clusters",
-                M, K_in, taps, nbatch, S, p.BN, p.n_tiles, p.splits, p.pair, p.kpb, p.stages);
+        fprintf(stderr, "tsd plan: M=%d K=%d taps=%d nbatch=%d S=%d -> BN=%d tiles/item=%d items/tile=%d splits=%d pair=%d kpb=%d stages=%d | max active clusters",
+                M, K_in, taps, nbatch, S, p.BN, p.n_tiles, p.ipt, p.splits, p.pair, p.kpb, p.stages);
         for (int k = 2; k <= 8; ++k) fprintf(stderr, " %d:%d", k, max_active_clusters(k));
         fprintf(stderr, "\n");
     }
@@ -1460,7 +1544,7 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
         const char * o = getenv("TSD_TILE_ORDER");
         p.order = (o && *o == '1') ? 1 : 0;
     }
-    const long long tiles = (long long)p.mblocks * nbatch * p.n_tiles * p.splits;   // CTA tiles
+    const long long tiles = (long long)p.mblocks * p.groups * p.n_tiles * p.splits;   // CTA tiles
     const int cpt = p.pair ? 2 : 1;
     // one wave of split tiles: the splits of an output tile run as one cluster (rank = split,
     // which m-block-major order makes consecutive; pairs: rank = 2 * split + half)
@@ -1468,7 +1552,7 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
         const int rows_max = 16 * (((p.BN >> 4) + p.splits - 1) / p.splits);
         const int mac = p.splits > 1 && cpt * p.splits <= 8 ? max_active_clusters(cpt * p.splits) : 0;
         p.csplit = allow_cluster && cluster_split_enabled() && p.splits > 1 && tiles <= num_sms && mac > 0 &&
-                   (long long)(p.mblocks / cpt) * nbatch * p.n_tiles <= mac &&
+                   (long long)(p.mblocks / cpt) * p.groups * p.n_tiles <= mac &&
                    (long long)p.BN * 512 + (long long)(p.splits - 1) * rows_max * 512 <= (long long)kStageArea;
     }
     if (p.csplit || p.pair) p.order = 0;
@@ -1493,7 +1577,7 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
         // activations as [item][K atom][token][64]: one box = kpb atoms of the B tile's tokens
         const uint64_t d[4] = {64, (uint64_t)S, (uint64_t)(K_in / 64), (uint64_t)nbatch};
         const uint64_t st[3] = {(uint64_t)x_row_stride * 2, 128, (uint64_t)x_batch_stride * 2};
-        const uint32_t box[4] = {64, (uint32_t)(p.pair ? p.BN / 2 : p.BN), (uint32_t)p.kpb, 1};
+        const uint32_t box[4] = {64, (uint32_t)(p.pair ? p.BN / 2 : p.ipt > 1 ? p.bni : p.BN), (uint32_t)p.kpb, 1};
         if (!make_tmap_4d(&L.tmB, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d, st, box, true)) return false;
     }
     return true;

@@ -60,6 +60,10 @@ struct GemmParams {
                        // 128 rows and half the tokens; m-blocks even, no Q8_0 A, tile walk m-block-major
     int gather;        // split-K through the global workspace with one tile per CTA: the split that completes
                        // a tile last gathers the other partials into its idle operand stages
+    int ipt;           // batch items per token tile: > 1 puts several short items side by side in one tile
+                       // (single CTAs, no split), each in `bni` rows, so a weight tile is read once for all
+    int bni;           // token rows per item of a multi-item tile (a multiple of 16, >= S)
+    int groups;        // token tiles along the batch: nbatch, or ceil(nbatch / ipt)
     // EPI_QKV: W rows are [Q | K | V] (H each, feature = head * 64 + d); out row = item * s_item + t
     __half * q_out, * k_out, * v_out;   // [item][nh][Sj][64], this stream's tokens at s_off
     const float * qg, * kg;             // RMSNorm gains [64]
