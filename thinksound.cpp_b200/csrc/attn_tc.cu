@@ -177,10 +177,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 tmem_wait_ld(w);
                 if (valid >= 64) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(u[i]));
-                        m4[(i + 2) & 3] = fmaxf(m4[(i + 2) & 3], __uint_as_float(w[i]));
-                    }
+                    for (int i = 0; i < 32; ++i)
+                        m4[i & 3] = max3(m4[i & 3], __uint_as_float(u[i]), __uint_as_float(w[i]));
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
@@ -217,8 +215,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             }
             // pass 2: P = 2^(s * scale - m), fp16 pairs (key 2c in the low half) into the P columns;
             // one exponential in four on the FMA pipes (exp2_poly), the rest on the SFU
-            float r4[4] = {0.f, 0.f, 0.f, 0.f};
+            float2 r01 = make_float2(0.f, 0.f), r23 = make_float2(0.f, 0.f);   // partial row sums
             const float nm = -m_new;
+            const float2 sc2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(nm, nm);
             {
                 // columns 0-31 are read again (the last read of S_j: S_{j+1} may then overwrite it,
                 // and runs while the exponentials below are computed); columns 32-63 are in w
@@ -235,16 +234,16 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 #pragma unroll
                         for (int c = 0; c < 8; ++c) {
                             const int i0 = c1 + 2 * c;
-                            float x0 = fmaf(__uint_as_float(v[i0]), a.scale_log2, nm);
-                            float x1 = fmaf(__uint_as_float(v[i0 + 1]), a.scale_log2, nm);
+                            // s * scale - m for the column pair (one packed FMA)
+                            float2 x = fma2(make_float2(__uint_as_float(v[i0]), __uint_as_float(v[i0 + 1])), sc2, nm2);
                             if (vlim < 32) {           // only in the ragged last chunk
-                                if (i0 >= vlim) x0 = -INFINITY;
-                                if (i0 + 1 >= vlim) x1 = -INFINITY;
+                                if (i0 >= vlim) x.x = -INFINITY;
+                                if (i0 + 1 >= vlim) x.y = -INFINITY;
                             }
-                            const float p0 = ex2_approx(x0);
-                            const float p1 = (i0 & 2) ? exp2_poly(x1) : ex2_approx(x1);
-                            r4[(2 * c) & 3] += p0;
-                            r4[(2 * c + 1) & 3] += p1;
+                            const float p0 = ex2_approx(x.x);
+                            const float p1 = (i0 & 2) ? exp2_poly(x.y) : ex2_approx(x.y);
+                            if (c & 1) r23 = add2(r23, make_float2(p0, p1));
+                            else r01 = add2(r01, make_float2(p0, p1));
                             const __half2 h2 = __floats2half2_rn(p0, p1);
                             pk[c] = *reinterpret_cast<const uint32_t *>(&h2);
                         }
@@ -254,7 +253,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 piece(u, 0);
                 piece(w, 32);
             }
-            l_run = l_run * alpha + ((r4[0] + r4[1]) + (r4[2] + r4[3]));
+            l_run = l_run * alpha + ((r01.x + r01.y) + (r23.x + r23.y));
             m_run = m_new;
             tmem_wait_st();
             tc_fence_before();

@@ -472,6 +472,30 @@ __device__ __forceinline__ float exp2_poly(float x) {
     return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 // 2^x on the SFU (ex2.approx); used for the softmax exponent.
+// Packed pairs of f32 (sm_100 f32x2 instructions): each lane is the scalar operation with the
+// same rounding (fma.rn / add.rn), one instruction for both.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+    float2 r;
+    asm("{\n\t.reg .b64 pa, pb, pc, pd;\n\t"
+        "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\tmov.b64 pc, {%6, %7};\n\t"
+        "fma.rn.f32x2 pd, pa, pb, pc;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return r;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+    float2 r;
+    asm("{\n\t.reg .b64 pa, pb, pd;\n\t"
+        "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+        "add.rn.f32x2 pd, pa, pb;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return r;
+}
+// max(a, b, c) in one instruction (three-input max of sm_100); exact, like two fmaxf.
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
