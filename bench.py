@@ -206,10 +206,11 @@ def run_reference(args, rank, world):
 
 # ----------------------------------------------------------------------------------- ours
 def profile_case(wtype, workload="cfg3"):
-    """One forward (B=2, config-3 token counts, or config 4's with workload "cfg4") of a depth-3
-    model (2 joint + 1 fused blocks) with the full model's GEMM / attention / GEMV shapes, op by
-    op through tsd_forward_profile; prints each op's time. Small enough (~1.3 GB of weights) for
-    a full ncu capture of single launches."""
+    """One forward (B=2, config-3 token counts, or config 4's with workload "cfg4", or a batch of
+    32 sequences with config-3 token counts, a quarter of config 5's, with workload "cfg5") of a
+    depth-3 model (2 joint + 1 fused blocks) with the full model's GEMM / attention / GEMV shapes,
+    op by op through tsd_forward_profile; prints each op's time. Small enough (~1.3 GB of weights,
+    a few GB of activations) for a full ncu capture of single launches."""
     import torch
     import __graft_entry__
     __graft_entry__.load_package()
@@ -223,8 +224,9 @@ def profile_case(wtype, workload="cfg3"):
     m = tsd.DitModel.from_weights(hp, W)
     del W
     SH = CFG4 if workload == "cfg4" else CFG3
-    X = make_device_inputs(2, SH, 4242, "cuda:0")
-    p = m.forward_profile(2, SH["T"], SH["clip_S"], SH["sync_S"], SH["text_S"], SH["t5_S"],
+    B = 32 if workload == "cfg5" else 2
+    X = make_device_inputs(B, SH, 4242, "cuda:0")
+    p = m.forward_profile(B, SH["T"], SH["clip_S"], SH["sync_S"], SH["text_S"], SH["t5_S"],
                           {k: v.data_ptr() for k, v in X.items()})
     for i, (l, ms, b) in enumerate(zip(p["labels"], p["ms"], p["bytes"])):
         print(f"{i:3d} {ms * 1000:8.1f} us {b / ms / 1e6:7.0f} GB/s  {l}")
@@ -348,7 +350,7 @@ def main():
                          "the config-3 widths (the small case the ncu captures are taken on)")
     args = ap.parse_args()
     if args.profile_case:
-        return profile_case(args.profile_case, args.workload if args.workload in ("cfg3", "cfg4") else "cfg3")
+        return profile_case(args.profile_case, args.workload)
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
