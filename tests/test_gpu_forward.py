@@ -293,14 +293,18 @@ def test_many_item_batch_conditioning_gemms(small_bf16):
     assert oracle.rel_l2(fb[9], fe) <= 1.2 * oracle.rel_l2(fo, fe) + 1e-3
 
 
-def test_multi_item_tiles_in_the_forward(monkeypatch, small_bf16):
+@pytest.mark.parametrize("pair", [0, 1])
+def test_multi_item_tiles_in_the_forward(monkeypatch, small_bf16, pair):
     """Every GEMM over short items (here the 20-token latent and 8-token clip streams) forced onto
-    tiles that hold several batch items: a 5-item batch, whose last tile is partly empty, matches
-    the oracle item by item and the same model's default tiling."""
+    tiles that hold several batch items (pair = 1: on CTA pairs where the tiling allows): a
+    5-item batch, whose last tile is partly empty, matches the oracle item by item and the same
+    model's default tiling."""
     hp, W, m, om = small_bf16
     items = synth.make_inputs(hp, seed=77, batch=5, **SHAPE)
     ref = m.forward(items)
     monkeypatch.setenv("TSD_FORCE_MULTI_ITEM", "1")
+    if pair:
+        monkeypatch.setenv("TSD_FORCE_PAIR", "1")
     mf = tsd.DitModel.from_weights(hp, W)
     try:
         fm = mf.forward(items)

@@ -150,11 +150,13 @@ def test_gemm_split_k_store_and_swiglu(mode):
 @pytest.mark.parametrize("mode,gate_div", [(tsd.EPI_STORE, 1), (tsd.EPI_SWIGLU, 1), (tsd.EPI_GATE_RESID, 1),
                                            (tsd.EPI_GATE_RESID, 0)])
 @pytest.mark.parametrize("S,nb,taps", [(72, 2, 3), (72, 5, 3), (40, 7, 7), (100, 3, 1)])
-def test_gemm_multi_item_tiles(monkeypatch, S, nb, taps, mode, gate_div):
+@pytest.mark.parametrize("pair", [0, 1])
+def test_gemm_multi_item_tiles(monkeypatch, S, nb, taps, mode, gate_div, pair):
     """Several short batch items side by side in one token tile (each weight tile read once for all
-    of them; the clip stream's 72-token items): the same sums in the same K order as one item per
-    tile, so bit-identical to it (no split-K on either side), and within 1e-5 of the f32
-    reference. nb = 5 / 7 leave the last tile of items partly empty."""
+    of them; the clip stream's 72-token items), on single CTAs or CTA pairs (each CTA of a pair
+    loading whole items): the same sums in the same K order as one item per tile on single CTAs,
+    so bit-identical to it (no split-K on either side), and within 1e-5 of the f32 reference.
+    nb = 5 / 7 / 3 leave the last tile of items partly empty."""
     M, K = 512, 512
     W = rnd(M, taps * K, scale=0.03)
     X = rnd(nb, S, K)
@@ -165,11 +167,13 @@ def test_gemm_multi_item_tiles(monkeypatch, S, nb, taps, mode, gate_div):
     Fo = M // 2 if mode == tsd.EPI_SWIGLU else M
     out = {}
     for form in ("multi", "single"):
-        monkeypatch.delenv("TSD_FORCE_MULTI_ITEM", raising=False)
-        monkeypatch.delenv("TSD_NO_MULTI_ITEM", raising=False)
+        for v in ("TSD_FORCE_MULTI_ITEM", "TSD_NO_MULTI_ITEM", "TSD_FORCE_PAIR", "TSD_NO_PAIR"):
+            monkeypatch.delenv(v, raising=False)
         monkeypatch.setenv("TSD_FORCE_MULTI_ITEM" if form == "multi" else "TSD_NO_MULTI_ITEM", "1")
+        monkeypatch.setenv("TSD_FORCE_PAIR" if form == "multi" and pair else "TSD_NO_PAIR", "1")
         plan = tsd.op_gemm_plan(M, K, taps, nb, S, 1)
         assert (plan["BN"] > (S + 15) // 16 * 16) == (form == "multi"), (form, plan)
+        assert plan["pair"] == (pair if form == "multi" else 0), (form, plan)
         if mode == tsd.EPI_GATE_RESID:
             x = x0.clone()
             tsd.op_gemm(W, M, K, taps, taps // 2, X, nb, S, K, S * K, mode, 0, bias, None, 0, 0, resid=x, ldr=M,

@@ -789,7 +789,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             uint8_t * sb = smem + st * sbytes + kpb * kABytes;
             if (p.a_q8) mbar_arrive_expect_tx(&full[st], b_bytes);
             if constexpr (PAIR) {
-                tma_load_4d_pair(sb, &tmB, mapa_shared(smem_u32(&full[st]), lead), 0, yb, kc, b);
+                if (p.ipt > 1) {
+                    // multi-item pair tile: this CTA's items b + 2i + prank, one box each
+                    for (int i = 0; 2 * i < p.ipt; ++i)
+                        tma_load_4d_pair(sb + (size_t)i * kpb * p.bni * 128, &tmB,
+                                         mapa_shared(smem_u32(&full[st]), lead), 0, yb, kc, b + 2 * i + prank);
+                } else {
+                    tma_load_4d_pair(sb, &tmB, mapa_shared(smem_u32(&full[st]), lead), 0, yb, kc, b);
+                }
             } else {
                 // multi-item tile: one box of bni rows x kpb atoms per item, item after item (an item
                 // past the batch reads the fill value zero)
@@ -815,7 +822,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const int kb0 = c.kb_begin * kpb;
             const int tap = kb0 / kpt;                       // conv tap and K block within it
             int kc = kb0 - tap * kpt;
-            int yb = c.t0 + prank * bh + tap - p.pad;        // first token row of the B tile
+            // first token row of the B tile (a multi-item pair tile: whole items on each CTA)
+            int yb = c.t0 + (p.ipt > 1 ? 0 : prank * bh) + tap - p.pad;
             const int ya = c.mb * 128;
             bool ok = true;
             for (int ks = c.kb_begin; ks < c.kb_end; ++ks, ++it) {
@@ -851,7 +859,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (lane == 0 && prank == 0) {
             // ---------------- MMA issuer (a pair's leader issues for both CTAs) ----------------
             const uint32_t idesc = make_idesc_f16(PAIR ? 256 : 128, p.BN, true);
-            const uint32_t idesc_item = make_idesc_f16(128, p.ipt > 1 ? p.bni : p.BN, true);
+            // multi-item tiles: one MMA per item (single CTA, N = bni) or per item pair (N = 2 bni)
+            const uint32_t idesc_item = make_idesc_f16(PAIR ? 256 : 128, p.ipt > 1 ? (PAIR ? 2 : 1) * p.bni : p.BN, true);
             const uint16_t pmask = (uint16_t)(3u << lead);
             int it = 0, lt = 0;
             int s = 0;                 // ring slot of `it` and the parity of its fill
@@ -878,6 +887,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         const uint64_t adesc = make_sdesc_sw128(sa + j * kABytes);
                         const uint64_t bdesc = make_sdesc_sw128(sa + kpb * kABytes + j * b_bytes);
                         const uint32_t acc0 = (kb > c.kb_begin || j > 0) ? 1u : 0u;
+                        if constexpr (PAIR) {
+                            if (p.ipt > 1) {
+                                // multi-item pair tile: per item pair i, N = 2 bni (the leader's item, then
+                                // the peer's) into accumulator columns 2 i bni ..
+                                for (int i = 0; 2 * i < p.ipt; ++i) {
+                                    const uint64_t bd = make_sdesc_sw128(sa + kpb * kABytes + (i * kpb + j) * p.bni * 128);
+#pragma unroll
+                                    for (int kk = 0; kk < 4; ++kk)
+                                        umma_f16_ss_pair(dacc + 2 * i * p.bni, adesc + 2 * kk, bd + 2 * kk, idesc_item,
+                                                         (acc0 | kk) ? 1u : 0u);
+                                }
+                                continue;
+                            }
+                        }
                         if constexpr (!PAIR) {   // (no single-CTA MMA in the pair instance)
                             if (p.ipt > 1) {
                                 // multi-item tile: item i's bni token rows (its own atoms, item-major in
@@ -1437,26 +1460,36 @@ static std::vector<TileChoice> tile_choices(int S, int nbatch, int mblocks, int 
     // in bni rows, so every weight tile is read once for all of them instead of once per item.
     // Single CTAs, no split. Per K=16 step one MMA per item (N = bni); the token-tile issuer
     // sends one box per item (~500 cycles each).
+    // A CTA pair takes an even number of items: each CTA loads whole items (b + 2i + its rank),
+    // one pair MMA per item pair (N = 2 bni).
+    const bool pairs_ok = allow_pair && allow_cluster && mblocks % 2 == 0 && pairs_enabled() && max_active_clusters(2) >= 1;
     if (nbatch >= 2 && multi_item_enabled())
-        for (int ipt = 2; ipt <= nbatch && multi_item_fits(S, ipt); ++ipt) {
-            const int bni = item_rows(S), bn = ipt * bni;
-            const long long otiles = (long long)mblocks * ((nbatch + ipt - 1) / ipt);
-            const long long waves = (otiles + num_sms - 1) / num_sms;
-            const double kb = nkb;
-            const double kb_bytes = 16384.0 + 128.0 * bn;
-            const int kpb = multi_item_kpb(k128 && !q8, bn, nkb);
-            const int nst = std::min(kMaxStages, kStageArea / (kpb * (kABytes + 128 * bn) + (q8 ? kQ8Bytes : 0)));
-            const double ex = 4.0 * kpb * ipt * std::max(65.0, bni / 2.0);
-            // one token box per item and stage; a stage comes back after the load latency (~2550
-            // cycles under load) plus the MMAs that hold it, nst stages in flight
-            const double t_stage = std::max(std::max(std::max(ex, 500.0 * ipt), (2550.0 + ex) / nst), q8 ? 600.0 : 300.0);
-            const double t_sm = kb * std::max(t_stage / kpb, kb_bytes / 110.0);
-            const double t_l2 = (double)std::min<long long>(otiles, num_sms) * kb * kb_bytes / 12000.0;
-            const double epi = bn * 128.0 * 4.0 / 20.0;
-            TileChoice t{(double)waves * (std::max(t_sm, t_l2) + 3000.0) + epi, bn, 1, 0};
-            t.ipt = ipt;
-            out.push_back(t);
-        }
+        for (int pair = 0; pair <= (pairs_ok ? 1 : 0); ++pair)
+            for (int ipt = 2; ipt <= nbatch && multi_item_fits(S, ipt); ++ipt) {
+                if (pair && ipt % 2) continue;
+                const int cpt = pair ? 2 : 1;
+                const int bni = item_rows(S), bn = ipt * bni;
+                const long long otiles = (long long)(mblocks / cpt) * ((nbatch + ipt - 1) / ipt);   // (pair tiles)
+                const long long slots = pair ? std::min<long long>(num_sms & ~1, 2ll * max_active_clusters(2)) : num_sms;
+                const long long waves = (otiles * cpt + slots - 1) / slots;
+                const double kb = nkb;
+                const int b_atom = 128 * bn / cpt;
+                const double kb_bytes = 16384.0 + b_atom;
+                const int kpb = pair ? ((k128 && !q8 && kStageArea / (2 * (kABytes + b_atom)) >= 3 && nkb % 2 == 0 && nkb / 2 >= 2) ? 2 : 1)
+                                     : multi_item_kpb(k128 && !q8, bn, nkb);
+                const int nst = std::min(kMaxStages, kStageArea / (kpb * (kABytes + b_atom) + (q8 ? kQ8Bytes : 0)));
+                const double ex = 4.0 * kpb * (ipt / cpt) * std::max(65.0, cpt * bni / 2.0);
+                // one token box per item and stage; a stage comes back after the load latency
+                // (~2550 cycles under load) plus the MMAs that hold it, nst stages in flight
+                const double t_stage = std::max(std::max(std::max(ex, 500.0 * ipt / cpt), (2550.0 + ex) / nst),
+                                                q8 ? 600.0 : 300.0);
+                const double t_sm = kb * std::max(t_stage / kpb, kb_bytes / 110.0);
+                const double t_l2 = (double)std::min<long long>(otiles * cpt, slots) * kb * kb_bytes / 12000.0;
+                const double epi = bn * 128.0 * 4.0 / 20.0;
+                TileChoice t{(double)waves * (std::max(t_sm, t_l2) + 3000.0) + epi, bn, 1, pair};
+                t.ipt = ipt;
+                out.push_back(t);
+            }
     std::stable_sort(out.begin(), out.end(), [](const TileChoice & a, const TileChoice & b) { return a.cost < b.cost; });
     return out;
 }
@@ -1509,9 +1542,9 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
         if (force_pair == 1)          // the model's best pair choice
             for (const TileChoice & x : c)
                 if (x.pair) { t = x; break; }
-        if (force_bn <= 0 && getenv("TSD_FORCE_MULTI_ITEM"))   // tests: the best multi-item choice, if any
-            for (const TileChoice & x : c)
-                if (x.ipt > 1) { t = x; break; }
+        if (force_bn <= 0 && getenv("TSD_FORCE_MULTI_ITEM"))   // tests: the best multi-item choice (a pair
+            for (const TileChoice & x : c)                    // one with TSD_FORCE_PAIR), if any
+                if (x.ipt > 1 && (force_pair != 1 || x.pair)) { t = x; break; }
         for (const TileChoice & x : c)
             if (force_bn > 0 && x.BN == force_bn && x.splits == force_splits && (force_pair < 0 || x.pair == force_pair)) {
                 t = x;
@@ -1530,7 +1563,7 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
         const int b_atom = (p.pair ? p.BN / 2 : p.BN) * 128;
         const int st2 = kStageArea / (2 * (kABytes + b_atom));
         p.kpb = (!p.a_q8 && K_in % 128 == 0 && st2 >= 3 && nkb % (2 * p.splits) == 0 && nkb / (2 * p.splits) >= 2) ? 2 : 1;
-        if (p.ipt > 1) p.kpb = multi_item_kpb(!p.a_q8 && K_in % 128 == 0, p.BN, nkb);
+        if (p.ipt > 1 && !p.pair) p.kpb = multi_item_kpb(!p.a_q8 && K_in % 128 == 0, p.BN, nkb);
         p.stages = std::min(kMaxStages, kStageArea / (p.kpb * (kABytes + b_atom) + (p.a_q8 ? kQ8Bytes : 0)));
     }
     if (getenv("TSD_DEBUG_PLAN")) {
@@ -1577,7 +1610,7 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
         // activations as [item][K atom][token][64]: one box = kpb atoms of the B tile's tokens
         const uint64_t d[4] = {64, (uint64_t)S, (uint64_t)(K_in / 64), (uint64_t)nbatch};
         const uint64_t st[3] = {(uint64_t)x_row_stride * 2, 128, (uint64_t)x_batch_stride * 2};
-        const uint32_t box[4] = {64, (uint32_t)(p.pair ? p.BN / 2 : p.ipt > 1 ? p.bni : p.BN), (uint32_t)p.kpb, 1};
+        const uint32_t box[4] = {64, (uint32_t)(p.ipt > 1 ? p.bni : p.pair ? p.BN / 2 : p.BN), (uint32_t)p.kpb, 1};
         if (!make_tmap_4d(&L.tmB, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d, st, box, true)) return false;
     }
     return true;
