@@ -640,7 +640,9 @@ __device__ __forceinline__ void q8_chunk_to_bf16(const uint4 & u, float d, uint3
 
 // PAIR: the CTA-pair form (cta_group::2). A kernel holding cta_group::2 instructions must be
 // launched in clusters of an even size, so the single-CTA form is a separate instance.
-template <int EK, bool PAIR>
+// MI: the multi-item form (several batch items per token tile, p.ipt > 1); a separate instance so
+// that one-item tiles run the straight-line code (the extra loops cost the others ~2%, measured).
+template <int EK, bool PAIR, bool MI>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmG,
@@ -789,7 +791,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             uint8_t * sb = smem + st * sbytes + kpb * kABytes;
             if (p.a_q8) mbar_arrive_expect_tx(&full[st], b_bytes);
             if constexpr (PAIR) {
-                if (p.ipt > 1) {
+                if (MI) {
                     // multi-item pair tile: this CTA's items b + 2i + prank, one box each
                     for (int i = 0; 2 * i < p.ipt; ++i)
                         tma_load_4d_pair(sb + (size_t)i * kpb * p.bni * 128, &tmB,
@@ -800,8 +802,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             } else {
                 // multi-item tile: one box of bni rows x kpb atoms per item, item after item (an item
                 // past the batch reads the fill value zero)
-                for (int i = 0; i < p.ipt; ++i)
-                    tma_load_4d(sb + (size_t)i * kpb * p.bni * 128, &tmB, &full[st], 0, yb, kc, b + i);
+                if (MI) {
+                    for (int i = 0; i < p.ipt; ++i)
+                        tma_load_4d(sb + (size_t)i * kpb * p.bni * 128, &tmB, &full[st], 0, yb, kc, b + i);
+                } else {
+                    tma_load_4d(sb, &tmB, &full[st], 0, yb, kc, b);
+                }
             }
         };
         const int amask = a_parts - 1;                       // a_parts is 1 or 2
@@ -823,7 +829,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const int tap = kb0 / kpt;                       // conv tap and K block within it
             int kc = kb0 - tap * kpt;
             // first token row of the B tile (a multi-item pair tile: whole items on each CTA)
-            int yb = c.t0 + (p.ipt > 1 ? 0 : prank * bh) + tap - p.pad;
+            int yb = c.t0 + (MI ? 0 : prank * bh) + tap - p.pad;
             const int ya = c.mb * 128;
             bool ok = true;
             for (int ks = c.kb_begin; ks < c.kb_end; ++ks, ++it) {
@@ -860,7 +866,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // ---------------- MMA issuer (a pair's leader issues for both CTAs) ----------------
             const uint32_t idesc = make_idesc_f16(PAIR ? 256 : 128, p.BN, true);
             // multi-item tiles: one MMA per item (single CTA, N = bni) or per item pair (N = 2 bni)
-            const uint32_t idesc_item = make_idesc_f16(PAIR ? 256 : 128, p.ipt > 1 ? (PAIR ? 2 : 1) * p.bni : p.BN, true);
+            const uint32_t idesc_item = make_idesc_f16(PAIR ? 256 : 128, MI ? (PAIR ? 2 : 1) * p.bni : p.BN, true);
             const uint16_t pmask = (uint16_t)(3u << lead);
             int it = 0, lt = 0;
             int s = 0;                 // ring slot of `it` and the parity of its fill
@@ -887,8 +893,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         const uint64_t adesc = make_sdesc_sw128(sa + j * kABytes);
                         const uint64_t bdesc = make_sdesc_sw128(sa + kpb * kABytes + j * b_bytes);
                         const uint32_t acc0 = (kb > c.kb_begin || j > 0) ? 1u : 0u;
-                        if constexpr (PAIR) {
-                            if (p.ipt > 1) {
+                        if constexpr (PAIR && MI) {
+                            {
                                 // multi-item pair tile: per item pair i, N = 2 bni (the leader's item, then
                                 // the peer's) into accumulator columns 2 i bni ..
                                 for (int i = 0; 2 * i < p.ipt; ++i) {
@@ -901,8 +907,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                 continue;
                             }
                         }
-                        if constexpr (!PAIR) {   // (no single-CTA MMA in the pair instance)
-                            if (p.ipt > 1) {
+                        if constexpr (!PAIR && MI) {   // (no single-CTA MMA in the pair instance)
+                            {
                                 // multi-item tile: item i's bni token rows (its own atoms, item-major in
                                 // the stage) into accumulator columns i * bni ..
                                 for (int i = 0; i < p.ipt; ++i) {
@@ -954,7 +960,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 else mbar_arrive(&acc_empty[buf]);
             }
         };
-        const int ebn = epi_bn(p);                    // token columns finished at a time
+        const int ebn = MI ? p.bni : p.BN;            // token columns finished at a time
         for (int t = tile0; t < num_tiles; t += tstep, ++lt) {
             TileCoord c = decode(p, t, nks, prank);      // (a multi-item tile advances c.b per item)
             const int buf = lt & 1;
@@ -1085,15 +1091,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             if (whole) {
                 bool failed = false;
                 // one pass per item of a multi-item tile (item it in accumulator columns it * bni ..)
-                for (int it = 0; it < p.ipt && !failed; ++it) {
-                if (it > 0) {
+                for (int it = 0; it < (MI ? p.ipt : 1) && !failed; ++it) {
+                if (MI && it > 0) {
                     if (++c.b >= p.nbatch) break;
                     e.row_base = (long long)c.b * p.S + c.t0;
                     gate_prologue();
                     if (Epi<EK>::qkv && p.rope && c.mb * 128 < 2 * p.hidden)
                         rope_load(p, e, c, 0, (c.mb * 128 - (c.mb * 128 / p.hidden) * p.hidden + ml) & 63, rcs);
                 }
-                const uint32_t trow_i = trow + (uint32_t)(it * p.bni);
+                const uint32_t trow_i = MI ? trow + (uint32_t)(it * p.bni) : trow;
                 if (Epi<EK>::gate && tma) {
                     // gate tiles of 16 tokens by TMA two steps ahead, residual updates by TMA
                     // reduce-add (gate_step)
@@ -1322,7 +1328,7 @@ static int max_active_clusters(int cs) {
     if (dev < 0 || dev >= 64 || cs < 1 || cs > 8) return 0;
     if (!done[dev]) {
         done[dev] = true;
-        cudaFuncSetAttribute(gemm_tc_kernel<EK_F32, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        cudaFuncSetAttribute(gemm_tc_kernel<EK_F32, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
         int sms = 148;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         for (int k = 1; k <= 8; ++k) {
@@ -1336,7 +1342,7 @@ static int max_active_clusters(int cs) {
             cfg.attrs = at;
             cfg.numAttrs = 1;
             int n = 0;
-            if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<EK_F32, false>, &cfg) != cudaSuccess) {
+            if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<EK_F32, false, false>, &cfg) != cudaSuccess) {
                 cudaGetLastError();
                 n = 0;
             }
@@ -1685,18 +1691,20 @@ void gemm_finalize(GemmLaunch & L) {
 }
 
 namespace {
-template <int EK, bool PAIR> cudaError_t launch_form(cudaLaunchConfig_t & cfg, const GemmLaunch & L, const GemmParams & p) {
+template <int EK, bool PAIR, bool MI>
+cudaError_t launch_form(cudaLaunchConfig_t & cfg, const GemmLaunch & L, const GemmParams & p) {
     static bool attr = false;   // per instance
     if (!attr) {
         cudaError_t e =
-            cudaFuncSetAttribute(gemm_tc_kernel<EK, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+            cudaFuncSetAttribute(gemm_tc_kernel<EK, PAIR, MI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<EK, PAIR>, L.tmA, L.tmB, L.tmO, L.tmG, L.tmV, L.tmS, p);
+    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<EK, PAIR, MI>, L.tmA, L.tmB, L.tmO, L.tmG, L.tmV, L.tmS, p);
 }
 template <int EK> cudaError_t launch_kind(cudaLaunchConfig_t & cfg, const GemmLaunch & L, const GemmParams & p) {
-    return p.pair ? launch_form<EK, true>(cfg, L, p) : launch_form<EK, false>(cfg, L, p);
+    if (p.ipt > 1) return p.pair ? launch_form<EK, true, true>(cfg, L, p) : launch_form<EK, false, true>(cfg, L, p);
+    return p.pair ? launch_form<EK, true, false>(cfg, L, p) : launch_form<EK, false, false>(cfg, L, p);
 }
 }  // namespace
 
