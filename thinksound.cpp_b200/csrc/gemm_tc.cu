@@ -640,13 +640,16 @@ __device__ __forceinline__ void q8_chunk_to_bf16(const uint4 & u, float d, uint3
 
 // PAIR: the CTA-pair form (cta_group::2). A kernel holding cta_group::2 instructions must be
 // launched in clusters of an even size, so the single-CTA form is a separate instance.
-// MI: the multi-item form (several batch items per token tile, p.ipt > 1); a separate instance so
-// that one-item tiles run the straight-line code (the extra loops cost the others ~2%, measured).
-template <int EK, bool PAIR, bool MI>
+// FORM: 0 one item per token tile, no gathering split; 1 the multi-item form (several batch items
+// per token tile, p.ipt > 1); 2 a workspace split-K whose last split gathers the partials
+// (p.gather). Separate instances, so that the common form runs straight-line code: compiled into
+// one kernel, the other forms' loops and branches cost every GEMM 1-2% (measured).
+template <int EK, bool PAIR, int FORM>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmG,
                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmS, const GemmParams p) {
+    constexpr bool MI = FORM == 1, GATHER = FORM == 2;
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t * ebuf = smem + kStageArea;                       // epilogue staging [2][kEBufBytes]
@@ -972,7 +975,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             e.ncols = min(ebn, p.S - c.t0);
             e.row_base = (long long)c.b * p.S + c.t0;
             e.col = p.out_cblk ? (long long)(e.m / p.out_cblk) * p.out_cstride + e.m % p.out_cblk : e.m;
-            const bool whole = p.splits == 1 || p.gather;     // this CTA finishes whole tiles
+            const bool whole = p.splits == 1 || GATHER;       // this CTA finishes whole tiles
             const bool tma = p.epi_tma && whole;
             const bool tma_gate = p.epi_tma && (whole || p.csplit);           // residual / gate maps exist
             const int m0 = Epi<EK>::swiglu ? c.mb * 64 : c.mb * 128;    // first output feature of the tile
@@ -1013,7 +1016,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             };
             // while the accumulator fills (a gathering split learns only afterwards whether it
             // finishes the tile)
-            if (!p.gather) gate_prologue();
+            if constexpr (!GATHER) gate_prologue();
             float2 rcs[32];                                               // QKV: RoPE (cos, sin) of a chunk
             if (Epi<EK>::qkv && p.rope && c.mb * 128 < 2 * p.hidden)
                 rope_load(p, e, c, 0, (c.mb * 128 - (c.mb * 128 / p.hidden) * p.hidden + ml) & 63, rcs);
@@ -1022,7 +1025,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 break;
             tc_fence_after();
             const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + buf * 256;
-            if (p.gather) {
+            if constexpr (GATHER) {
                 // Split-K through the global workspace, one tile per CTA (the operand stages are
                 // idle now). Every split but the last to complete the tile stores its partial tile
                 // and leaves; the last one (it skips its own store when the others are all in
@@ -1328,7 +1331,7 @@ static int max_active_clusters(int cs) {
     if (dev < 0 || dev >= 64 || cs < 1 || cs > 8) return 0;
     if (!done[dev]) {
         done[dev] = true;
-        cudaFuncSetAttribute(gemm_tc_kernel<EK_F32, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        cudaFuncSetAttribute(gemm_tc_kernel<EK_F32, false, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
         int sms = 148;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         for (int k = 1; k <= 8; ++k) {
@@ -1342,7 +1345,7 @@ static int max_active_clusters(int cs) {
             cfg.attrs = at;
             cfg.numAttrs = 1;
             int n = 0;
-            if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<EK_F32, false, false>, &cfg) != cudaSuccess) {
+            if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<EK_F32, false, 0>, &cfg) != cudaSuccess) {
                 cudaGetLastError();
                 n = 0;
             }
@@ -1691,20 +1694,21 @@ void gemm_finalize(GemmLaunch & L) {
 }
 
 namespace {
-template <int EK, bool PAIR, bool MI>
+template <int EK, bool PAIR, int FORM>
 cudaError_t launch_form(cudaLaunchConfig_t & cfg, const GemmLaunch & L, const GemmParams & p) {
     static bool attr = false;   // per instance
     if (!attr) {
         cudaError_t e =
-            cudaFuncSetAttribute(gemm_tc_kernel<EK, PAIR, MI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+            cudaFuncSetAttribute(gemm_tc_kernel<EK, PAIR, FORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<EK, PAIR, MI>, L.tmA, L.tmB, L.tmO, L.tmG, L.tmV, L.tmS, p);
+    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<EK, PAIR, FORM>, L.tmA, L.tmB, L.tmO, L.tmG, L.tmV, L.tmS, p);
 }
 template <int EK> cudaError_t launch_kind(cudaLaunchConfig_t & cfg, const GemmLaunch & L, const GemmParams & p) {
-    if (p.ipt > 1) return p.pair ? launch_form<EK, true, true>(cfg, L, p) : launch_form<EK, false, true>(cfg, L, p);
-    return p.pair ? launch_form<EK, true, false>(cfg, L, p) : launch_form<EK, false, false>(cfg, L, p);
+    if (p.ipt > 1) return p.pair ? launch_form<EK, true, 1>(cfg, L, p) : launch_form<EK, false, 1>(cfg, L, p);
+    if (p.gather) return launch_form<EK, false, 2>(cfg, L, p);     // (a gathering split never pairs)
+    return p.pair ? launch_form<EK, true, 0>(cfg, L, p) : launch_form<EK, false, 0>(cfg, L, p);
 }
 }  // namespace
 
