@@ -640,16 +640,17 @@ __device__ __forceinline__ void q8_chunk_to_bf16(const uint4 & u, float d, uint3
 
 // PAIR: the CTA-pair form (cta_group::2). A kernel holding cta_group::2 instructions must be
 // launched in clusters of an even size, so the single-CTA form is a separate instance.
-// FORM: 0 one item per token tile, no gathering split; 1 the multi-item form (several batch items
-// per token tile, p.ipt > 1); 2 a workspace split-K whose last split gathers the partials
-// (p.gather). Separate instances, so that the common form runs straight-line code: compiled into
-// one kernel, the other forms' loops and branches cost every GEMM 1-2% (measured).
+// FORM bits: 1 the multi-item form (several batch items per token tile, p.ipt > 1); 2 a workspace
+// split-K whose last split gathers the partials (p.gather); 4 planar Q8_0 weights converted in
+// shared memory (p.a_q8). Separate instances, so that the common form (0) runs straight-line
+// code: compiled into one kernel, the other forms' loops and branches cost every GEMM 1-2%
+// (measured).
 template <int EK, bool PAIR, int FORM>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmG,
                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmS, const GemmParams p) {
-    constexpr bool MI = FORM == 1, GATHER = FORM == 2;
+    constexpr bool MI = (FORM & 1) != 0, GATHER = (FORM & 2) != 0, Q8 = (FORM & 4) != 0;
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t * ebuf = smem + kStageArea;                       // epilogue staging [2][kEBufBytes]
@@ -682,11 +683,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     // one stage: kpb A atoms (bf16 128 x 64, SW128) | kpb B atoms (bh x 64) | Q8_0 path (kpb = 1):
     // int8 tile + scales; a multiple of 1024 bytes, so every stage's SW128 atoms stay aligned
     const uint32_t b_bytes = (uint32_t)(bh * 128);                   // one B atom
-    const int sbytes = kpb * (kABytes + (int)b_bytes) + (p.a_q8 ? kQ8Bytes : 0);
+    const int sbytes = kpb * (kABytes + (int)b_bytes) + (Q8 ? kQ8Bytes : 0);
     const int nst = p.stages;                   // ring depth, <= kMaxStages, nst * sbytes <= kStageArea
     // Q8_0: warps 6-7 convert each stage's int8 tile; a CTA with a single tile (no epilogue to
     // overlap with a later main loop) puts its four epilogue warps on the conversion as well
-    const bool q8_single = p.a_q8 && tile0 + tstep >= num_tiles;
+    const bool q8_single = Q8 && tile0 + tstep >= num_tiles;
     const int q8_conv_warps = q8_single ? 6 : 2;
     // Q8_0 conversion of every stage of this CTA's tiles by converter thread `cid` of `ncv`:
     // 16-byte units u = row * 4 + chunk of the 128 x 64 int8 tile, each to two 16-byte chunks of
@@ -727,7 +728,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (threadIdx.x == 0) {
         // full: the producer's expect_tx (+ both converter warps' arrivals on the Q8_0 path)
         for (int s = 0; s < kMaxStages; ++s) {
-            mbar_init(&full[s], p.a_q8 ? 1 + q8_conv_warps : 1); mbar_init(&empty[s], 1); mbar_init(&rfull[s], 1);
+            mbar_init(&full[s], Q8 ? 1 + q8_conv_warps : 1); mbar_init(&empty[s], 1); mbar_init(&rfull[s], 1);
         }
         // acc_empty: the four epilogue warps (of both CTAs of a pair, on the leader's)
         for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], PAIR ? 8 : 4); mbar_init(&ebar[s], 1); }
@@ -776,7 +777,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const uint32_t stage_tx = (uint32_t)kpb * (kABytes + b_bytes) * (PAIR ? 2u : 1u);
         const auto issue_a = [&](int st, int kb, int ya) {
             uint8_t * sa = smem + st * sbytes;
-            if (p.a_q8) {
+            if (Q8) {
                 uint8_t * raw = sa + kABytes + p.BN * 128;
                 mbar_arrive_expect_tx(&rfull[st], 128 * 64 + 2 * 128 * 2);
                 tma_load_2d(raw, &tmA, &rfull[st], kb * 64, ya);
@@ -792,7 +793,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         };
         const auto issue_b = [&](int st, int kc, int yb, int b) {
             uint8_t * sb = smem + st * sbytes + kpb * kABytes;
-            if (p.a_q8) mbar_arrive_expect_tx(&full[st], b_bytes);
+            if (Q8) mbar_arrive_expect_tx(&full[st], b_bytes);
             if constexpr (PAIR) {
                 if (MI) {
                     // multi-item pair tile: this CTA's items b + 2i + prank, one box each
@@ -856,14 +857,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const int issued = it > pre ? it : pre;
             const unsigned long long t_start = globaltimer();
             for (int i = (issued > nst ? issued - nst : 0); i < issued; ++i) {
-                uint64_t * bar = (p.a_q8 && do_a) ? &rfull[i % nst] : &full[i % nst];
+                uint64_t * bar = (Q8 && do_a) ? &rfull[i % nst] : &full[i % nst];
                 while (!mbar_try_wait(bar, (i / nst) & 1) && globaltimer() - t_start < wait_ns()) {}
             }
         }
     };
 
     if (warp == 0) {
-        if (lane == 0) produce(p.a_q8 ? 3 : 1, 0, p.a_q8 ? 1 : 2);
+        if (lane == 0) produce(Q8 ? 3 : 1, 0, Q8 ? 1 : 2);
     } else if (warp == 1) {
         if (lane == 0 && prank == 0) {
             // ---------------- MMA issuer (a pair's leader issues for both CTAs) ----------------
@@ -938,12 +939,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             }
         }
     } else if (warp >= 6) {
-        if (!p.a_q8 && lane == 0) {
+        if (!Q8 && lane == 0) {
             if (warp == 6) produce(2, 0, 1);                    // activation tiles
             else produce(1, 1, 2);                              // weight tiles of odd K steps
         }
         // ---------------- Q8_0 converters (warps 6, 7) ----------------
-        if (p.a_q8) convert_q8((warp - 6) * 32 + lane, 32 * q8_conv_warps);
+        if (Q8) convert_q8((warp - 6) * 32 + lane, 32 * q8_conv_warps);
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
         if (q8_single) convert_q8(64 + (warp - 2) * 32 + lane, 32 * q8_conv_warps);
@@ -1706,6 +1707,11 @@ cudaError_t launch_form(cudaLaunchConfig_t & cfg, const GemmLaunch & L, const Ge
     return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<EK, PAIR, FORM>, L.tmA, L.tmB, L.tmO, L.tmG, L.tmV, L.tmS, p);
 }
 template <int EK> cudaError_t launch_kind(cudaLaunchConfig_t & cfg, const GemmLaunch & L, const GemmParams & p) {
+    if (p.a_q8) {   // (Q8_0 weights never pair)
+        if (p.ipt > 1) return launch_form<EK, false, 5>(cfg, L, p);
+        if (p.gather) return launch_form<EK, false, 6>(cfg, L, p);
+        return launch_form<EK, false, 4>(cfg, L, p);
+    }
     if (p.ipt > 1) return p.pair ? launch_form<EK, true, 1>(cfg, L, p) : launch_form<EK, false, 1>(cfg, L, p);
     if (p.gather) return launch_form<EK, false, 2>(cfg, L, p);     // (a gathering split never pairs)
     return p.pair ? launch_form<EK, true, 0>(cfg, L, p) : launch_form<EK, false, 0>(cfg, L, p);
