@@ -642,15 +642,17 @@ __device__ __forceinline__ void q8_chunk_to_bf16(const uint4 & u, float d, uint3
 // launched in clusters of an even size, so the single-CTA form is a separate instance.
 // FORM bits: 1 the multi-item form (several batch items per token tile, p.ipt > 1); 2 a workspace
 // split-K whose last split gathers the partials (p.gather); 4 planar Q8_0 weights converted in
-// shared memory (p.a_q8). Separate instances, so that the common form (0) runs straight-line
-// code: compiled into one kernel, the other forms' loops and branches cost every GEMM 1-2%
-// (measured).
+// shared memory (p.a_q8); 8 split-K inside a cluster (p.csplit); 16 a workspace split-K reduced
+// by the last split's reducer. Separate instances, so that the common form (0, no split) runs
+// straight-line code: compiled into one kernel, the other forms' loops and branches cost every
+// GEMM 1-2% (measured).
 template <int EK, bool PAIR, int FORM>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmG,
                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmS, const GemmParams p) {
     constexpr bool MI = (FORM & 1) != 0, GATHER = (FORM & 2) != 0, Q8 = (FORM & 4) != 0;
+    constexpr bool CSPLIT = (FORM & 8) != 0, WSRED = (FORM & 16) != 0;
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t * ebuf = smem + kStageArea;                       // epilogue staging [2][kEBufBytes]
@@ -672,7 +674,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int kpb = p.kpb;                       // K blocks per stage (a K step); kpt % kpb == 0
     const int nks = nkb / kpb;                   // K steps; tile K ranges are in K steps
     // CTA pairs: consecutive cluster ranks 2j (leader) and 2j + 1 share pair tiles
-    const uint32_t crank = (PAIR || p.csplit) ? cluster_ctarank() : 0u;
+    const uint32_t crank = (PAIR || CSPLIT) ? cluster_ctarank() : 0u;
     const int prank = PAIR ? (int)(crank & 1u) : 0;           // this CTA's half of the pair tile
     const uint32_t lead = crank & ~1u;                           // cluster rank of the pair leader
     const int srank = PAIR ? (int)(crank >> 1) : (int)crank;   // cluster split-K: this CTA's split
@@ -733,7 +735,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         // acc_empty: the four epilogue warps (of both CTAs of a pair, on the leader's)
         for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], PAIR ? 8 : 4); mbar_init(&ebar[s], 1); }
         mbar_init(&cbar[0], 1);
-        for (int s = 1; s < 3; ++s) mbar_init(&cbar[s], p.csplit ? p.splits - 1 : 1);
+        for (int s = 1; s < 3; ++s) mbar_init(&cbar[s], CSPLIT ? p.splits - 1 : 1);
         *s_abort = 0;
         fence_mbar_init();
     }
@@ -753,8 +755,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     // pairs / cluster split-K: every CTA's barriers are initialised before any other CTA of the
     // cluster signals them; cbar[0] then expects the bytes of this split's slice from each of
     // the other splits
-    if (p.csplit || PAIR) cluster_sync_all();
-    if (p.csplit && threadIdx.x == 64) {
+    if (CSPLIT || PAIR) cluster_sync_all();
+    if (CSPLIT && threadIdx.x == 64) {
         const int rows = slice_lo(srank + 1, p.BN, p.splits) - slice_lo(srank, p.BN, p.splits);
         mbar_arrive_expect_tx(&cbar[0], (uint32_t)((p.splits - 1) * rows * 512));
     }
@@ -976,9 +978,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             e.ncols = min(ebn, p.S - c.t0);
             e.row_base = (long long)c.b * p.S + c.t0;
             e.col = p.out_cblk ? (long long)(e.m / p.out_cblk) * p.out_cstride + e.m % p.out_cblk : e.m;
-            const bool whole = p.splits == 1 || GATHER;       // this CTA finishes whole tiles
+            constexpr bool whole = !CSPLIT && !WSRED;         // this CTA finishes whole tiles
             const bool tma = p.epi_tma && whole;
-            const bool tma_gate = p.epi_tma && (whole || p.csplit);           // residual / gate maps exist
+            const bool tma_gate = p.epi_tma && (whole || CSPLIT);             // residual / gate maps exist
             const int m0 = Epi<EK>::swiglu ? c.mb * 64 : c.mb * 128;    // first output feature of the tile
             const int cb = p.out_cblk ? m0 / p.out_cblk : 0;              // its column block (output map dim 3)
             const int c0o = m0 - cb * p.out_cblk;
@@ -993,7 +995,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 if (Epi<EK>::gate && tma_gate && gtile && threadIdx.x == 64) {
                     // (the per-token gate planes are not L2-resident)
                     int lo = 0, hi = e.ncols;
-                    if (p.csplit) { lo = slice_lo(srank, p.BN, p.splits); hi = min(slice_lo(srank + 1, p.BN, p.splits), e.ncols); }
+                    if (CSPLIT) { lo = slice_lo(srank, p.BN, p.splits); hi = min(slice_lo(srank + 1, p.BN, p.splits), e.ncols); }
                     for (int t = lo + 32; t < hi; t += 16) tma_prefetch_l2_4d(&tmG, m0, c.t0 + t, c.b, 0);
                 }
                 if (Epi<EK>::gate && whole) {
@@ -1092,7 +1094,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 tmem_wait_st();
                 gate_prologue();
             }
-            if (whole) {
+            if constexpr (whole) {
                 bool failed = false;
                 // one pass per item of a multi-item tile (item it in accumulator columns it * bni ..)
                 for (int it = 0; it < (MI ? p.ipt : 1) && !failed; ++it) {
@@ -1158,7 +1160,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 }
                 release_acc(buf);
                 if (failed) break;
-            } else if (p.csplit) {
+            } else if constexpr (CSPLIT) {
                 // Split-K inside the cluster (one tile per CTA; the operand stages are idle now):
                 // partial tile -> own shared memory; the row slices the other ranks finish are
                 // pushed into their receive slots by bulk copies that complete on their barrier;
@@ -1707,13 +1709,19 @@ cudaError_t launch_form(cudaLaunchConfig_t & cfg, const GemmLaunch & L, const Ge
     return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<EK, PAIR, FORM>, L.tmA, L.tmB, L.tmO, L.tmG, L.tmV, L.tmS, p);
 }
 template <int EK> cudaError_t launch_kind(cudaLaunchConfig_t & cfg, const GemmLaunch & L, const GemmParams & p) {
-    if (p.a_q8) {   // (Q8_0 weights never pair)
+    // (Q8_0 weights never pair; pairs split K only inside a cluster; multi-item tiles never split)
+    if (p.a_q8) {
         if (p.ipt > 1) return launch_form<EK, false, 5>(cfg, L, p);
-        if (p.gather) return launch_form<EK, false, 6>(cfg, L, p);
+        if (p.splits > 1)
+            return p.csplit ? launch_form<EK, false, 12>(cfg, L, p)
+                            : p.gather ? launch_form<EK, false, 6>(cfg, L, p) : launch_form<EK, false, 20>(cfg, L, p);
         return launch_form<EK, false, 4>(cfg, L, p);
     }
     if (p.ipt > 1) return p.pair ? launch_form<EK, true, 1>(cfg, L, p) : launch_form<EK, false, 1>(cfg, L, p);
-    if (p.gather) return launch_form<EK, false, 2>(cfg, L, p);     // (a gathering split never pairs)
+    if (p.splits > 1) {
+        if (p.csplit) return p.pair ? launch_form<EK, true, 8>(cfg, L, p) : launch_form<EK, false, 8>(cfg, L, p);
+        return p.gather ? launch_form<EK, false, 2>(cfg, L, p) : launch_form<EK, false, 16>(cfg, L, p);
+    }
     return p.pair ? launch_form<EK, true, 0>(cfg, L, p) : launch_form<EK, false, 0>(cfg, L, p);
 }
 }  // namespace
