@@ -254,6 +254,8 @@ __device__ __forceinline__ void rope_load(const GemmParams & p, const EpiCtx & e
     }
 }
 
+// TMA_ONLY: the caller's kernel form always has the TMA epilogue maps (p.epi_tma).
+template <bool TMA_ONLY>
 __device__ __forceinline__ void emit_qkv(const GemmParams & p, const EpiCtx & e, const TileCoord & c, int j0,
                                          const uint32_t (&w)[32], int ml, int lane, int q, uint8_t * ebuf, int & nqk,
                                          int & gs, const CUtensorMap * tmQ, const CUtensorMap * tmK,
@@ -303,7 +305,7 @@ __device__ __forceinline__ void emit_qkv(const GemmParams & p, const EpiCtx & e,
             if (j0 + 32 < epi_bn(p)) rope_load(p, e, c, j0 + 32, d, cs);
         }
     }
-    if (p.epi_tma) {
+    if (TMA_ONLY || p.epi_tma) {
         // this warp pair's head: [32 tokens][64] fp16 in the staging buffer, then two 16-token
         // TMA boxes per head (the second only inside the tile); tokens past the stream's length
         // are clipped. The four boxes are issued by lane 0 of the four epilogue warps (a TMA
@@ -643,7 +645,8 @@ __device__ __forceinline__ void q8_chunk_to_bf16(const uint4 & u, float d, uint3
 // FORM bits: 1 the multi-item form (several batch items per token tile, p.ipt > 1); 2 a workspace
 // split-K whose last split gathers the partials (p.gather); 4 planar Q8_0 weights converted in
 // shared memory (p.a_q8); 8 split-K inside a cluster (p.csplit); 16 a workspace split-K reduced
-// by the last split's reducer. Separate instances, so that the common form (0, no split) runs
+// by the last split's reducer; 32 an epilogue without TMA maps (p.epi_tma false: plain stores),
+// which the other forms leave out. Separate instances, so that the common form (0, no split) runs
 // straight-line code: compiled into one kernel, the other forms' loops and branches cost every
 // GEMM 1-2% (measured).
 template <int EK, bool PAIR, int FORM>
@@ -652,7 +655,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmG,
                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmS, const GemmParams p) {
     constexpr bool MI = (FORM & 1) != 0, GATHER = (FORM & 2) != 0, Q8 = (FORM & 4) != 0;
-    constexpr bool CSPLIT = (FORM & 8) != 0, WSRED = (FORM & 16) != 0;
+    constexpr bool CSPLIT = (FORM & 8) != 0, WSRED = (FORM & 16) != 0, PLAIN = (FORM & 32) != 0;
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t * ebuf = smem + kStageArea;                       // epilogue staging [2][kEBufBytes]
@@ -979,7 +982,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             e.row_base = (long long)c.b * p.S + c.t0;
             e.col = p.out_cblk ? (long long)(e.m / p.out_cblk) * p.out_cstride + e.m % p.out_cblk : e.m;
             constexpr bool whole = !CSPLIT && !WSRED;         // this CTA finishes whole tiles
-            const bool tma = p.epi_tma && whole;
+            const bool tma = whole && !PLAIN;                 // (forms without PLAIN: p.epi_tma)
             const bool tma_gate = p.epi_tma && (whole || CSPLIT);             // residual / gate maps exist
             const int m0 = Epi<EK>::swiglu ? c.mb * 64 : c.mb * 128;    // first output feature of the tile
             const int cb = p.out_cblk ? m0 / p.out_cblk : 0;              // its column block (output map dim 3)
@@ -1151,7 +1154,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         uint32_t v[32];
                         tmem_ld32_async(trow_i + j0, v);
                         tmem_wait_ld(v);
-                        if (Epi<EK>::qkv) emit_qkv(p, e, c, j0, v, ml, lane, q, ebuf, nqk, gs, &tmO, &tmG, &tmV, rcs);
+                        if (Epi<EK>::qkv) emit_qkv<!PLAIN>(p, e, c, j0, v, ml, lane, q, ebuf, nqk, gs, &tmO, &tmG, &tmV, rcs);
                         else if (tma) tma_chunk<EK>(p, &tmO, e, j0, v, ml, lane, ebuf, gs, c0o, cb, c.b, c.t0);
                         else if (Epi<EK>::swiglu) emit_swiglu<EK>(p, e, j0, v, lane);
                         else emit_store<EK>(p, e, j0, v);
@@ -1710,6 +1713,17 @@ cudaError_t launch_form(cudaLaunchConfig_t & cfg, const GemmLaunch & L, const Ge
 }
 template <int EK> cudaError_t launch_kind(cudaLaunchConfig_t & cfg, const GemmLaunch & L, const GemmParams & p) {
     // (Q8_0 weights never pair; pairs split K only inside a cluster; multi-item tiles never split)
+    if (!p.epi_tma && (p.splits == 1 || p.gather)) {   // whole tiles through plain stores
+        const int f = 32 | (p.ipt > 1 ? 1 : 0) | (p.gather ? 2 : 0) | (p.a_q8 ? 4 : 0);
+        switch (f) {
+            case 32: return p.pair ? launch_form<EK, true, 32>(cfg, L, p) : launch_form<EK, false, 32>(cfg, L, p);
+            case 33: return p.pair ? launch_form<EK, true, 33>(cfg, L, p) : launch_form<EK, false, 33>(cfg, L, p);
+            case 34: return launch_form<EK, false, 34>(cfg, L, p);
+            case 36: return launch_form<EK, false, 36>(cfg, L, p);
+            case 37: return launch_form<EK, false, 37>(cfg, L, p);
+            default: return launch_form<EK, false, 38>(cfg, L, p);
+        }
+    }
     if (p.a_q8) {
         if (p.ipt > 1) return launch_form<EK, false, 5>(cfg, L, p);
         if (p.splits > 1)
