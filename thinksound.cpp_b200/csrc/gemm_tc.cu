@@ -868,8 +868,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
     };
 
-    if (warp == 0) {
-        if (lane == 0) produce(Q8 ? 3 : 1, 0, Q8 ? 1 : 2);
+    if (warp == 0 || (!Q8 && warp >= 6)) {
+        // one call site for every producer thread (one inlined copy of the loop): warp 0 weight
+        // tiles of even K steps (Q8_0: every tile of both operands), warp 6 the activation
+        // tiles, warp 7 the weight tiles of odd K steps
+        if (lane == 0) produce(Q8 ? 3 : warp == 6 ? 2 : 1, warp == 7 ? 1 : 0, Q8 ? 1 : 2);
     } else if (warp == 1) {
         if (lane == 0 && prank == 0) {
             // ---------------- MMA issuer (a pair's leader issues for both CTAs) ----------------
@@ -944,12 +947,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             }
         }
     } else if (warp >= 6) {
-        if (!Q8 && lane == 0) {
-            if (warp == 6) produce(2, 0, 1);                    // activation tiles
-            else produce(1, 1, 2);                              // weight tiles of odd K steps
-        }
         // ---------------- Q8_0 converters (warps 6, 7) ----------------
-        if (Q8) convert_q8((warp - 6) * 32 + lane, 32 * q8_conv_warps);
+        if constexpr (Q8) convert_q8((warp - 6) * 32 + lane, 32 * q8_conv_warps);
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
         if (q8_single) convert_q8(64 + (warp - 2) * 32 + lane, 32 * q8_conv_warps);
