@@ -799,21 +799,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const auto issue_b = [&](int st, int kc, int yb, int b) {
             uint8_t * sb = smem + st * sbytes + kpb * kABytes;
             if (Q8) mbar_arrive_expect_tx(&full[st], b_bytes);
+            // multi-item tile: one box per K atom holding bni token rows of each of this CTA's items,
+            // item after item (a pair: the leader the first ipt / 2 items, the peer the rest), so
+            // the items' rows form one operand of ipt * bni rows for a single MMA; rows past an
+            // item's end and items past the batch read the fill value zero
             if constexpr (PAIR) {
                 if (MI) {
-                    // multi-item pair tile: this CTA's items b + 2i + prank, one box each
-                    for (int i = 0; 2 * i < p.ipt; ++i)
-                        tma_load_4d_pair(sb + (size_t)i * kpb * p.bni * 128, &tmB,
-                                         mapa_shared(smem_u32(&full[st]), lead), 0, yb, kc, b + 2 * i + prank);
+                    for (int j = 0; j < kpb; ++j)
+                        tma_load_4d_pair(sb + (size_t)j * b_bytes, &tmB, mapa_shared(smem_u32(&full[st]), lead), 0,
+                                         yb, kc + j, b + prank * (p.ipt >> 1));
                 } else {
                     tma_load_4d_pair(sb, &tmB, mapa_shared(smem_u32(&full[st]), lead), 0, yb, kc, b);
                 }
             } else {
-                // multi-item tile: one box of bni rows x kpb atoms per item, item after item (an item
-                // past the batch reads the fill value zero)
                 if (MI) {
-                    for (int i = 0; i < p.ipt; ++i)
-                        tma_load_4d(sb + (size_t)i * kpb * p.bni * 128, &tmB, &full[st], 0, yb, kc, b + i);
+                    for (int j = 0; j < kpb; ++j) tma_load_4d(sb + (size_t)j * b_bytes, &tmB, &full[st], 0, yb, kc + j, b);
                 } else {
                     tma_load_4d(sb, &tmB, &full[st], 0, yb, kc, b);
                 }
@@ -876,9 +876,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     } else if (warp == 1) {
         if (lane == 0 && prank == 0) {
             // ---------------- MMA issuer (a pair's leader issues for both CTAs) ----------------
+            // (a multi-item tile: N = ipt * bni, every item's rows in one MMA)
             const uint32_t idesc = make_idesc_f16(PAIR ? 256 : 128, p.BN, true);
-            // multi-item tiles: one MMA per item (single CTA, N = bni) or per item pair (N = 2 bni)
-            const uint32_t idesc_item = make_idesc_f16(PAIR ? 256 : 128, MI ? (PAIR ? 2 : 1) * p.bni : p.BN, true);
             const uint16_t pmask = (uint16_t)(3u << lead);
             int it = 0, lt = 0;
             int s = 0;                 // ring slot of `it` and the parity of its fill
@@ -905,34 +904,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         const uint64_t adesc = make_sdesc_sw128(sa + j * kABytes);
                         const uint64_t bdesc = make_sdesc_sw128(sa + kpb * kABytes + j * b_bytes);
                         const uint32_t acc0 = (kb > c.kb_begin || j > 0) ? 1u : 0u;
-                        if constexpr (PAIR && MI) {
-                            {
-                                // multi-item pair tile: per item pair i, N = 2 bni (the leader's item, then
-                                // the peer's) into accumulator columns 2 i bni ..
-                                for (int i = 0; 2 * i < p.ipt; ++i) {
-                                    const uint64_t bd = make_sdesc_sw128(sa + kpb * kABytes + (i * kpb + j) * p.bni * 128);
-#pragma unroll
-                                    for (int kk = 0; kk < 4; ++kk)
-                                        umma_f16_ss_pair(dacc + 2 * i * p.bni, adesc + 2 * kk, bd + 2 * kk, idesc_item,
-                                                         (acc0 | kk) ? 1u : 0u);
-                                }
-                                continue;
-                            }
-                        }
-                        if constexpr (!PAIR && MI) {   // (no single-CTA MMA in the pair instance)
-                            {
-                                // multi-item tile: item i's bni token rows (its own atoms, item-major in
-                                // the stage) into accumulator columns i * bni ..
-                                for (int i = 0; i < p.ipt; ++i) {
-                                    const uint64_t bd = make_sdesc_sw128(sa + kpb * kABytes + (i * kpb + j) * p.bni * 128);
-#pragma unroll
-                                    for (int kk = 0; kk < 4; ++kk)
-                                        umma_f16_ss(dacc + i * p.bni, adesc + 2 * kk, bd + 2 * kk, idesc_item,
-                                                    (acc0 | kk) ? 1u : 0u);
-                                }
-                                continue;
-                            }
-                        }
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk) {
                             if constexpr (PAIR) umma_f16_ss_pair(dacc, adesc + 2 * kk, bdesc + 2 * kk, idesc, (acc0 | kk) ? 1u : 0u);
@@ -1404,11 +1375,6 @@ static bool multi_item_enabled() {
 // epilogue reads the accumulator of an item in 32-column chunks, so the last item's chunks must
 // stay inside the tile's 256 TMEM columns.
 static int item_rows(int S) { return (S + 15) / 16 * 16; }
-// K blocks per stage of a multi-item tile: two (one box of two atoms per item) while two stages
-// fit, else one.
-static int multi_item_kpb(bool k128, int bn, int nkb) {
-    return (k128 && kStageArea / (2 * (kABytes + 128 * bn)) >= 2 && nkb % 2 == 0 && nkb / 2 >= 2) ? 2 : 1;
-}
 static bool multi_item_fits(int S, int ipt) {
     const int bni = item_rows(S);
     return ipt >= 2 && S <= 128 && (ipt - 1) * bni + (bni + 31) / 32 * 32 <= 256;
@@ -1472,10 +1438,9 @@ static std::vector<TileChoice> tile_choices(int S, int nbatch, int mblocks, int 
     }
     // Multi-item tiles (short conv streams: items of <= 128 tokens): ipt items side by side, each
     // in bni rows, so every weight tile is read once for all of them instead of once per item.
-    // Single CTAs, no split. Per K=16 step one MMA per item (N = bni); the token-tile issuer
-    // sends one box per item (~500 cycles each).
-    // A CTA pair takes an even number of items: each CTA loads whole items (b + 2i + its rank),
-    // one pair MMA per item pair (N = 2 bni).
+    // No split. The token-tile issuer sends one box per K atom holding all of the CTA's items
+    // (~500 cycles each), and per K=16 step one MMA covers every item (N = ipt bni). A CTA pair
+    // takes an even number of items: each CTA loads half of them.
     const bool pairs_ok = allow_pair && allow_cluster && mblocks % 2 == 0 && pairs_enabled() && max_active_clusters(2) >= 1;
     if (nbatch >= 2 && multi_item_enabled())
         for (int pair = 0; pair <= (pairs_ok ? 1 : 0); ++pair)
@@ -1489,13 +1454,12 @@ static std::vector<TileChoice> tile_choices(int S, int nbatch, int mblocks, int 
                 const double kb = nkb;
                 const int b_atom = 128 * bn / cpt;
                 const double kb_bytes = 16384.0 + b_atom;
-                const int kpb = pair ? ((k128 && !q8 && kStageArea / (2 * (kABytes + b_atom)) >= 3 && nkb % 2 == 0 && nkb / 2 >= 2) ? 2 : 1)
-                                     : multi_item_kpb(k128 && !q8, bn, nkb);
+                const int kpb = (k128 && !q8 && kStageArea / (2 * (kABytes + b_atom)) >= 3 && nkb % 2 == 0 && nkb / 2 >= 2) ? 2 : 1;
                 const int nst = std::min(kMaxStages, kStageArea / (kpb * (kABytes + b_atom) + (q8 ? kQ8Bytes : 0)));
-                const double ex = 4.0 * kpb * (ipt / cpt) * std::max(65.0, cpt * bni / 2.0);
-                // one token box per item and stage; a stage comes back after the load latency
-                // (~2550 cycles under load) plus the MMAs that hold it, nst stages in flight
-                const double t_stage = std::max(std::max(std::max(ex, 500.0 * ipt / cpt), (2550.0 + ex) / nst),
+                const double ex = 4.0 * kpb * std::max(65.0, bn / 2.0);
+                // one token box per K atom; a stage comes back after the load latency (~2550
+                // cycles under load) plus the MMAs that hold it, nst stages in flight
+                const double t_stage = std::max(std::max(std::max(ex, 500.0 * kpb), (2550.0 + ex) / nst),
                                                 q8 ? 600.0 : 300.0);
                 const double t_sm = kb * std::max(t_stage / kpb, kb_bytes / 110.0);
                 const double t_l2 = (double)std::min<long long>(otiles * cpt, slots) * kb * kb_bytes / 12000.0;
@@ -1577,7 +1541,6 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
         const int b_atom = (p.pair ? p.BN / 2 : p.BN) * 128;
         const int st2 = kStageArea / (2 * (kABytes + b_atom));
         p.kpb = (!p.a_q8 && K_in % 128 == 0 && st2 >= 3 && nkb % (2 * p.splits) == 0 && nkb / (2 * p.splits) >= 2) ? 2 : 1;
-        if (p.ipt > 1 && !p.pair) p.kpb = multi_item_kpb(!p.a_q8 && K_in % 128 == 0, p.BN, nkb);
         p.stages = std::min(kMaxStages, kStageArea / (p.kpb * (kABytes + b_atom) + (p.a_q8 ? kQ8Bytes : 0)));
     }
     if (getenv("TSD_DEBUG_PLAN")) {
@@ -1624,7 +1587,10 @@ bool gemm_plan(GemmLaunch & L, const void * W, int M, int K_in, int taps, int pa
         // activations as [item][K atom][token][64]: one box = kpb atoms of the B tile's tokens
         const uint64_t d[4] = {64, (uint64_t)S, (uint64_t)(K_in / 64), (uint64_t)nbatch};
         const uint64_t st[3] = {(uint64_t)x_row_stride * 2, 128, (uint64_t)x_batch_stride * 2};
-        const uint32_t box[4] = {64, (uint32_t)(p.ipt > 1 ? p.bni : p.pair ? p.BN / 2 : p.BN), (uint32_t)p.kpb, 1};
+        // (a multi-item tile: one K atom of bni rows of each of this CTA's items per box)
+        const int mi_items = p.ipt > 1 ? (p.pair ? p.ipt / 2 : p.ipt) : 1;
+        const uint32_t box[4] = {64, (uint32_t)(p.ipt > 1 ? p.bni : p.pair ? p.BN / 2 : p.BN),
+                                 (uint32_t)(p.ipt > 1 ? 1 : p.kpb), (uint32_t)mi_items};
         if (!make_tmap_4d(&L.tmB, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d, st, box, true)) return false;
     }
     return true;
