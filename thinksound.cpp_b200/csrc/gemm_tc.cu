@@ -1373,7 +1373,7 @@ static bool multi_item_enabled() {
 }
 // Rows per item of a multi-item tile for items of S tokens, and whether `ipt` of them fit: the
 // epilogue reads the accumulator of an item in 32-column chunks, so the last item's chunks must
-// stay inside the tile's 256 TMEM columns.
+// stay inside the tile's 256 TMEM columns (which also keeps the one MMA's N = ipt * bni <= 256).
 static int item_rows(int S) { return (S + 15) / 16 * 16; }
 static bool multi_item_fits(int S, int ipt) {
     const int bni = item_rows(S);
